@@ -1,0 +1,185 @@
+/*
+ * vfr_retrieval.h -- C ABI of libvfr_retrieval.so, the B200 (sm_100a)
+ * feature-retrieval library.
+ *
+ * The hot path is the per-frame k=8 squared-L2 nearest-neighbour search of
+ * HuBERT/ContentVec features against a FAISS Flat / IVF-Flat retrieval index,
+ * followed by the inverse-square-distance weighted gather-blend at index_rate.
+ *
+ * Conventions, mirrored from the reference bridge
+ * (crates/vocal-tensorrt/native/bridge.h:21-32):
+ *   - every fallible call returns 0 on success, 1 on a failure whose message
+ *     is stored in *error (if error != NULL), 2 on an unknown failure;
+ *   - *error is allocated with malloc and released with vfr_free_error (plain
+ *     free() compatible, like vocal_trt_free_error, bridge.h:23);
+ *   - device pointers are plain CUDA device addresses on the index's device;
+ *     calls are asynchronous and ordered on the given stream; the blend and
+ *     search entry points perform no allocation, host synchronisation or
+ *     host<->device copy once the index's workspace covers the frame count
+ *     (see vfr_retrieval_reserve).
+ *
+ * Results are those of the reference's CPU retrieval
+ * (crates/vocal-cpu/src/retrieval.rs:27-83): exact fp32 squared distances in
+ * its AVX2 summation order, top-8 with scan-order tie-breaking, f64 weights
+ * 1/max(d,1e-12)^2, f32 blend q*(1-r) + retrieved*r.  Where the reference CPU
+ * and CUDA paths differ, this library follows the CUDA path: a frame whose
+ * probed lists are all empty keeps its query (the CPU path returns an error),
+ * and index_rate is clamped to [0,1] with r <= 0 leaving features untouched.
+ */
+#ifndef VFR_RETRIEVAL_H
+#define VFR_RETRIEVAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VFR_API __attribute__((visibility("default")))
+#else
+#define VFR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque device-resident index (role of vocal::RetrievalGpuIndex,
+ * crates/vocal-tensorrt/native/bridge.h:64-67). */
+typedef struct VfrIndex VfrIndex;
+
+/* Parsed host-side index: the normalised arrays of the reference's
+ * RetrievalIndex (crates/vocal-model/src/retrieval.rs:6-14). */
+typedef struct VfrHostIndex VfrHostIndex;
+
+/* Stream handle with the layout of vocal::Stream
+ * (crates/vocal-tensorrt/native/bridge.h:54): one cudaStream_t. */
+typedef struct VfrStream {
+    void *stream;
+} VfrStream;
+
+/* ------------------------------------------------------------------------ */
+/* Drop-in entry points: same names, argument meaning and error behaviour as */
+/* crates/vocal-tensorrt/native/bridge.h:241-251 (Rust externs at           */
+/* crates/vocal-tensorrt/src/ffi.rs:174-199).                               */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces vocal_faiss_gpu_create (crates/vocal-tensorrt/native/retrieval.cu:34-90).
+ * Validates the normalised arrays (d in 1..4096, 0 < nprobe <= min(nlist, 32),
+ * 0 < n <= INT32_MAX, payload sizes, monotone offsets covering n), copies them
+ * to the current CUDA device and builds the derived device layout (bf16
+ * shadow, row norms, tensor-map descriptors). */
+VFR_API int vocal_faiss_gpu_create(int32_t dimensions, int32_t nlist, int32_t nprobe, size_t vector_count,
+                           const float *centroids, size_t centroid_count, const int32_t *offsets,
+                           size_t offset_count, const float *vectors, size_t vector_value_count,
+                           const int32_t *ids, size_t id_count, VfrIndex **out, char **error);
+
+/* Replaces vocal_faiss_gpu_destroy (crates/vocal-tensorrt/native/retrieval.cu:92-94). */
+VFR_API void vocal_faiss_gpu_destroy(VfrIndex *index);
+
+/* Replaces vocal_faiss_gpu_blend (crates/vocal-tensorrt/native/retrieval.cu:96-128).
+ * features: device f32 [frames][width], blended in place.  index_rate: device
+ * f32 scalar, read by the kernels (a captured CUDA graph sees updates). */
+VFR_API int vocal_faiss_gpu_blend(VfrIndex *index, float *features, size_t frames, int32_t width,
+                          const float *index_rate, VfrStream *stream, char **error);
+
+/* Frees an error string (bridge.h:23, vocal_trt_free_error). */
+VFR_API void vfr_free_error(char *message);
+
+/* ------------------------------------------------------------------------ */
+/* Index loading (restates crates/vocal-model/src/retrieval.rs:45-268)      */
+/* ------------------------------------------------------------------------ */
+
+/* RetrievalIndex::from_faiss (retrieval.rs:62-193): bounded reader of
+ * little-endian FAISS IxF2 / IwFl (L2, Flat quantizer, ArrayInvertedLists). */
+VFR_API int vfr_index_parse_faiss(const uint8_t *bytes, size_t length, VfrHostIndex **out, char **error);
+
+/* RetrievalIndex::from_package (retrieval.rs:45-57): finds the U8 tensor
+ * aux.retrieval.faiss in a VFRM v1 image (crates/vocal-model/src/inspection.rs:
+ * 70-178) and parses it.  *out is NULL (return 0) when the tensor is absent.
+ * feature_dims > 0 additionally requires d == feature_dims (768 v2, 256 v1). */
+VFR_API int vfr_index_from_vfrm(const uint8_t *image, size_t length, int32_t feature_dims, VfrHostIndex **out,
+                        char **error);
+
+VFR_API void vfr_index_free(VfrHostIndex *index);
+
+/* Accessors (retrieval.rs:16-43).  Array pointers stay valid until free. */
+VFR_API void vfr_index_info(const VfrHostIndex *index, int32_t *dimensions, int32_t *nlist, int32_t *nprobe,
+                    int64_t *vector_count);
+VFR_API const float *vfr_index_centroids(const VfrHostIndex *index);
+VFR_API const int32_t *vfr_index_offsets(const VfrHostIndex *index);
+VFR_API const float *vfr_index_vectors(const VfrHostIndex *index);
+VFR_API const int32_t *vfr_index_ids(const VfrHostIndex *index);
+
+/* GpuRetrievalIndex::new (crates/vocal-tensorrt/src/retrieval.rs:30-87):
+ * uploads a parsed index (same checks as vocal_faiss_gpu_create). */
+VFR_API int vfr_index_upload(const VfrHostIndex *index, VfrIndex **out, char **error);
+
+/* ------------------------------------------------------------------------ */
+/* Extended entry points                                                    */
+/* ------------------------------------------------------------------------ */
+
+/* Search engine selection. */
+enum {
+    VFR_ENGINE_AUTO = 0,   /* tensor-core candidates + exact re-rank, exact fallback */
+    VFR_ENGINE_EXACT = 1,  /* SIMT exact scan only (no tensor cores) */
+    VFR_ENGINE_TENSOR = 2  /* tensor-core candidates + exact re-rank */
+};
+
+typedef struct VfrOptions {
+    int32_t struct_size;   /* sizeof(VfrOptions) */
+    int32_t engine;        /* VFR_ENGINE_* */
+    int32_t candidates;    /* re-rank width per frame (16..128, multiple of 16); 0 = 64 */
+    int32_t reserved0;
+    int64_t label_base;    /* added to every returned label (row-sharded shards) */
+    int64_t max_frames;    /* workspace pre-size; 0 = grow on demand (outside capture) */
+} VfrOptions;
+
+/* vocal_faiss_gpu_create with options (NULL = defaults). */
+VFR_API int vfr_retrieval_create(int32_t dimensions, int32_t nlist, int32_t nprobe, size_t vector_count,
+                         const float *centroids, size_t centroid_count, const int32_t *offsets,
+                         size_t offset_count, const float *vectors, size_t vector_value_count,
+                         const int32_t *ids, size_t id_count, const VfrOptions *options, VfrIndex **out,
+                         char **error);
+
+/* Sizes the per-index workspace for up to max_frames frames per call, so that
+ * later calls allocate nothing (required before CUDA graph capture). */
+VFR_API int vfr_retrieval_reserve(VfrIndex *index, size_t max_frames, char **error);
+
+/* Search without blend: per frame the k (1..8) nearest rows as exact squared
+ * distances (ascending, ties in scan order) and FAISS labels (ids[] +
+ * label_base).  Missing results: +inf / -1.  All pointers are device memory. */
+VFR_API int vfr_retrieval_search(VfrIndex *index, const float *queries, size_t frames, int32_t width, int32_t k,
+                         float *distances, int64_t *labels, VfrStream *stream, char **error);
+
+/* Out-of-place blend: reads queries, writes out (may alias queries). */
+VFR_API int vfr_retrieval_blend_from(VfrIndex *index, const float *queries, float *out, size_t frames, int32_t width,
+                             const float *index_rate, VfrStream *stream, char **error);
+
+/* JSON diagnostics (engine, candidate width, empty-frame count, fallback
+ * count, layout).  Returns the length needed (excluding NUL); writes at most
+ * length bytes including NUL.  Synchronises the index's device. */
+VFR_API size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t length);
+
+/* Row-sharded multi-GPU building blocks (one process per GPU; the exchange is
+ * a collective of the caller's choice, NCCL all-gather in the Python host).
+ *
+ * vfr_merge_topk: k-way merge of `shards` per-shard top-8 lists
+ *   dist/labels [shards][frames][8] -> out [frames][8], ordered by
+ *   (distance, label); flat shards carry global row ids as labels, so this is
+ *   the single-index scan order.
+ * vfr_gather_owned: for every (frame, slot) label in [label_base,
+ *   label_base + n) of this shard write its fp32 vector to out[frame][slot][:],
+ *   else -0.0 (so a sum over shards reproduces each vector bit-exactly).
+ * vfr_blend_gathered: the reference weights + blend from per-frame distances
+ *   [frames][8] and gathered neighbour vectors [frames][8][width]. */
+VFR_API int vfr_merge_topk(const float *dist, const int64_t *labels, int32_t shards, size_t frames, float *out_dist,
+                   int64_t *out_labels, VfrStream *stream, char **error);
+VFR_API int vfr_gather_owned(VfrIndex *index, const int64_t *labels, size_t frames, float *out, VfrStream *stream,
+                     char **error);
+VFR_API int vfr_blend_gathered(const float *queries, float *out, const float *dist, const float *neighbours,
+                       size_t frames, int32_t width, const float *index_rate, VfrStream *stream, char **error);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VFR_RETRIEVAL_H */

@@ -1,0 +1,188 @@
+"""ctypes loader for the CPU oracle (oracle/vfr_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU legs of bench.py, never by the product package.  The C code restates
+crates/vocal-model/src/retrieval.rs:62-268 (FAISS reader) and
+crates/vocal-cpu/src/retrieval.rs:5-83 (search + blend) of the reference.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+OK, ERR_CONFIG, ERR_NO_CANDIDATE = 0, 1, 2
+
+
+class _Index(ctypes.Structure):
+    _fields_ = [
+        ("d", ctypes.c_int64),
+        ("nprobe", ctypes.c_int64),
+        ("nlist", ctypes.c_int64),
+        ("n", ctypes.c_int64),
+        ("centroids", ctypes.POINTER(ctypes.c_float)),
+        ("offsets", ctypes.POINTER(ctypes.c_int32)),
+        ("vectors", ctypes.POINTER(ctypes.c_float)),
+        ("ids", ctypes.POINTER(ctypes.c_int32)),
+    ]
+
+
+def build() -> str:
+    """Compiles liboracle.so with the committed Makefile (gcc only)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        P = ctypes.POINTER
+        L.orc_parse_faiss.argtypes = [ctypes.c_char_p, ctypes.c_size_t, P(_Index), ctypes.c_char_p, ctypes.c_size_t]
+        L.orc_parse_faiss.restype = ctypes.c_int
+        L.orc_free.argtypes = [P(_Index)]
+        L.orc_vfrm_find_faiss.argtypes = [ctypes.c_char_p, ctypes.c_size_t, P(ctypes.c_uint64), P(ctypes.c_uint64)]
+        L.orc_vfrm_find_faiss.restype = ctypes.c_int
+        for name in ("orc_l2_scalar", "orc_l2_avx2", "orc_l2_lanes"):
+            fn = getattr(L, name)
+            fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+            fn.restype = ctypes.c_float
+        L.orc_blend_row.argtypes = [P(_Index), ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_int]
+        L.orc_blend_row.restype = ctypes.c_int
+        L.orc_blend_batch.argtypes = [P(_Index), ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        L.orc_blend_batch.restype = ctypes.c_int
+        L.orc_search_batch.argtypes = [P(_Index), ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int64,
+                                       ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_void_p]
+        L.orc_search_batch.restype = ctypes.c_int
+        L.orc_view.argtypes = [P(_Index), ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                               ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class OracleIndex:
+    """Normalised RetrievalIndex arrays as the reference parser produces them.
+
+    Either parsed from FAISS bytes (`from_faiss`) or wrapped from arrays
+    (`from_arrays`, no copy beyond contiguity).
+    """
+
+    def __init__(self):
+        self._c = _Index()
+        self._owned = False
+        self._keep = ()
+
+    @classmethod
+    def from_faiss(cls, data: bytes) -> "OracleIndex":
+        L = lib()
+        self = cls()
+        err = ctypes.create_string_buffer(256)
+        rc = L.orc_parse_faiss(data, len(data), ctypes.byref(self._c), err, 256)
+        if rc != 0:
+            raise ValueError(err.value.decode())
+        self._owned = True
+        return self
+
+    @classmethod
+    def from_arrays(cls, centroids, offsets, vectors, ids, nprobe: int) -> "OracleIndex":
+        self = cls()
+        c = np.ascontiguousarray(centroids, np.float32)
+        o = np.ascontiguousarray(offsets, np.int32)
+        v = np.ascontiguousarray(vectors, np.float32)
+        i = np.ascontiguousarray(ids, np.int32)
+        d = c.shape[1]
+        lib().orc_view(ctypes.byref(self._c), d, c.shape[0], int(nprobe), v.shape[0], _ptr(c), _ptr(o), _ptr(v),
+                       _ptr(i))
+        self._keep = (c, o, v, i)
+        return self
+
+    def __del__(self):
+        if self._owned and _lib is not None:
+            _lib.orc_free(ctypes.byref(self._c))
+            self._owned = False
+
+    # accessors mirroring RetrievalIndex (crates/vocal-model/src/retrieval.rs:16-43)
+    @property
+    def d(self) -> int:
+        return int(self._c.d)
+
+    @property
+    def nlist(self) -> int:
+        return int(self._c.nlist)
+
+    @property
+    def nprobe(self) -> int:
+        return int(self._c.nprobe)
+
+    def __len__(self) -> int:
+        return int(self._c.n)
+
+    def centroids(self) -> np.ndarray:
+        return np.ctypeslib.as_array(self._c.centroids, (self.nlist * self.d,)).reshape(self.nlist, self.d).copy()
+
+    def offsets(self) -> np.ndarray:
+        return np.ctypeslib.as_array(self._c.offsets, (self.nlist + 1,)).copy()
+
+    def vectors(self) -> np.ndarray:
+        n = len(self)
+        return np.ctypeslib.as_array(self._c.vectors, (n * self.d,)).reshape(n, self.d).copy()
+
+    def ids(self) -> np.ndarray:
+        return np.ctypeslib.as_array(self._c.ids, (len(self),)).copy()
+
+    # the path itself
+    def blend(self, feats: np.ndarray, ratio: float, simd: bool = True, threads: int = 1):
+        """Reference call site semantics: in place on a copy; returns
+        (blended, per-frame status) where status 2 means the reference
+        returned `IVF search selected no candidate` for that frame (its row is
+        left untouched)."""
+        out = np.ascontiguousarray(feats, np.float32).copy()
+        frames = out.shape[0]
+        status = np.zeros(frames, np.int32)
+        lib().orc_blend_batch(ctypes.byref(self._c), _ptr(out), frames, out.shape[1], ctypes.c_float(ratio),
+                              int(simd), int(threads), _ptr(status))
+        return out, status
+
+    def search(self, queries: np.ndarray, simd: bool = True, nprobe: int = 0, threads: int = 1):
+        """Top-8 (squared distance, storage row, FAISS label, count)."""
+        q = np.ascontiguousarray(queries, np.float32)
+        frames = q.shape[0]
+        dist = np.empty((frames, 8), np.float32)
+        rows = np.empty((frames, 8), np.int64)
+        labels = np.empty((frames, 8), np.int64)
+        count = np.empty(frames, np.int32)
+        lib().orc_search_batch(ctypes.byref(self._c), _ptr(q), frames, int(simd), int(nprobe), int(threads),
+                               _ptr(dist), _ptr(rows), _ptr(labels), _ptr(count))
+        return dist, rows, labels, count
+
+
+def l2(a: np.ndarray, b: np.ndarray, kind: str = "avx2") -> float:
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    fn = {"avx2": lib().orc_l2_avx2, "scalar": lib().orc_l2_scalar, "lanes": lib().orc_l2_lanes}[kind]
+    return float(fn(_ptr(a), _ptr(b), a.shape[0]))
+
+
+def vfrm_find_faiss(image: bytes):
+    """(offset, length) of aux.retrieval.faiss, None when absent; raises on a
+    malformed container."""
+    off = ctypes.c_uint64()
+    n = ctypes.c_uint64()
+    rc = lib().orc_vfrm_find_faiss(image, len(image), ctypes.byref(off), ctypes.byref(n))
+    if rc < 0:
+        raise ValueError("malformed VFRM container")
+    return (off.value, n.value) if rc == 1 else None

@@ -1,0 +1,381 @@
+// C ABI of libvfr_retrieval.so (declared in include/vfr_retrieval.h).
+//
+// Index ownership, validation and dispatch.  The validation and the drop-in
+// entry points follow crates/vocal-tensorrt/native/retrieval.cu:34-128 (same
+// limits and messages); the error convention follows
+// crates/vocal-tensorrt/native/bridge.h:24-32.
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "kernels.h"
+#include "tc_path.h"
+#include "vfr_common.h"
+
+namespace vfr {
+
+char *make_error(const char *message) noexcept {
+    if (!message) message = "native retrieval error";
+    size_t bytes = std::strlen(message) + 1;
+    auto *result = static_cast<char *>(std::malloc(bytes));
+    if (result) std::memcpy(result, message, bytes);
+    return result;
+}
+
+namespace {
+
+// Makes the index's device current for the duration of a call.
+class DeviceGuard {
+public:
+    explicit DeviceGuard(int device) {
+        cuda_check(cudaGetDevice(&previous_));
+        if (previous_ != device) cuda_check(cudaSetDevice(device));
+        device_ = device;
+    }
+    ~DeviceGuard() {
+        if (previous_ != device_) cudaSetDevice(previous_);
+    }
+
+private:
+    int previous_ = 0;
+    int device_ = 0;
+};
+
+void free_index(VfrIndex *ix) noexcept {
+    if (!ix) return;
+    int previous = 0;
+    cudaGetDevice(&previous);
+    cudaSetDevice(ix->device);
+    release_tc(ix);
+    for (void *p : {static_cast<void *>(ix->centroids), static_cast<void *>(ix->offsets),
+                    static_cast<void *>(ix->vectors), static_cast<void *>(ix->ids),
+                    static_cast<void *>(ix->row_of_id), static_cast<void *>(ix->counters)})
+        if (p) cudaFree(p);
+    cudaSetDevice(previous);
+    delete ix;
+}
+
+template <class T>
+void alloc_copy(T **dst, const T *src, size_t count) {
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(dst), std::max<size_t>(count, 1) * sizeof(T)), "cudaMalloc");
+    if (count) cuda_check(cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice), "cudaMemcpy");
+}
+
+// retrieval.cu:42-59 checks, with the same messages.
+void validate_arrays(int32_t d, int32_t nlist, int32_t nprobe, size_t n, const float *centroids,
+                     size_t centroid_count, const int32_t *offsets, size_t offset_count, const float *vectors,
+                     size_t vector_value_count, const int32_t *ids, size_t id_count) {
+    require(d > 0 && d <= 4096, "invalid FAISS GPU index dimension");
+    require(nlist > 0 && nprobe > 0 && nprobe <= nlist && nprobe <= kMaxProbe, "invalid FAISS GPU IVF configuration");
+    require(n > 0 && n <= static_cast<size_t>(INT32_MAX), "invalid FAISS GPU vector count");
+    require(centroids && centroid_count == static_cast<size_t>(nlist) * d, "invalid FAISS centroid payload");
+    require(offsets && offset_count == static_cast<size_t>(nlist) + 1, "invalid FAISS list offsets");
+    require(vectors && vector_value_count == n * static_cast<size_t>(d), "invalid FAISS vector payload");
+    require(ids && id_count == n, "invalid FAISS id payload");
+    require(offsets[0] == 0 && offsets[nlist] == static_cast<int32_t>(n), "FAISS list offsets do not cover vectors");
+    for (int32_t i = 0; i < nlist; ++i) require(offsets[i] <= offsets[i + 1], "FAISS list offsets are not monotonic");
+}
+
+VfrIndex *create_index(int32_t d, int32_t nlist, int32_t nprobe, size_t n, const float *centroids,
+                       size_t centroid_count, const int32_t *offsets, size_t offset_count, const float *vectors,
+                       size_t vector_value_count, const int32_t *ids, size_t id_count, const VfrOptions *opt) {
+    validate_arrays(d, nlist, nprobe, n, centroids, centroid_count, offsets, offset_count, vectors,
+                    vector_value_count, ids, id_count);
+    VfrOptions o{};
+    o.struct_size = sizeof(VfrOptions);
+    if (opt) {
+        require(opt->struct_size >= static_cast<int32_t>(offsetof(VfrOptions, max_frames) + sizeof(int64_t)),
+                "VfrOptions.struct_size too small");
+        o = *opt;
+    }
+    require(o.engine >= VFR_ENGINE_AUTO && o.engine <= VFR_ENGINE_TENSOR, "invalid retrieval engine");
+    if (o.candidates == 0) o.candidates = 64;
+    require(o.candidates >= 16 && o.candidates <= 128 && o.candidates % 16 == 0,
+            "candidate width must be a multiple of 16 in 16..128");
+    require(o.label_base >= 0 && o.max_frames >= 0, "invalid label base or frame reservation");
+    // The reference parser guarantees ids form a permutation of 0..n; the raw
+    // ABI (like retrieval.cu) accepts any ids, so the inverse map used by
+    // vfr_gather_owned is only built when they do.
+    std::vector<int32_t> inverse(n, -1);
+    bool permutation = true;
+    for (size_t r = 0; r < n && permutation; ++r) {
+        if (ids[r] < 0 || static_cast<size_t>(ids[r]) >= n || inverse[ids[r]] >= 0) permutation = false;
+        else inverse[ids[r]] = static_cast<int32_t>(r);
+    }
+    auto *ix = new VfrIndex{};
+    try {
+        cuda_check(cudaGetDevice(&ix->device));
+        ix->d = d;
+        ix->nlist = nlist;
+        ix->nprobe = nprobe;
+        ix->n = static_cast<int64_t>(n);
+        ix->label_base = o.label_base;
+        ix->engine = o.engine;
+        ix->candidates = o.candidates;
+        ix->host_offsets.assign(offsets, offsets + nlist + 1);
+        alloc_copy(&ix->centroids, centroids, centroid_count);
+        alloc_copy(&ix->offsets, offsets, offset_count);
+        alloc_copy(&ix->vectors, vectors, vector_value_count);
+        alloc_copy(&ix->ids, ids, id_count);
+        if (permutation) alloc_copy(&ix->row_of_id, inverse.data(), n);
+        cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->counters), sizeof(DeviceCounters)));
+        cuda_check(cudaMemset(ix->counters, 0, sizeof(DeviceCounters)));
+        if (ix->engine != VFR_ENGINE_EXACT) build_tc(ix);
+        if (o.max_frames > 0) reserve_tc(ix, static_cast<size_t>(o.max_frames));
+        cuda_check(cudaDeviceSynchronize());
+    } catch (...) {
+        free_index(ix);
+        throw;
+    }
+    return ix;
+}
+
+cudaStream_t stream_of(VfrStream *stream) {
+    require(stream && stream->stream, "invalid FAISS CUDA stream");
+    return static_cast<cudaStream_t>(stream->stream);
+}
+
+ExactArgs exact_args(VfrIndex *ix, const float *queries, float *out, const float *rate, int mode) {
+    ExactArgs a{};
+    a.d = ix->d;
+    a.nlist = ix->nlist;
+    a.nprobe = ix->nprobe;
+    a.centroids = ix->centroids;
+    a.offsets = ix->offsets;
+    a.vectors = ix->vectors;
+    a.ids = ix->ids;
+    a.queries = queries;
+    a.out = out;
+    a.index_rate = rate;
+    a.mode = mode;
+    a.label_base = ix->label_base;
+    a.counters = ix->counters;
+    return a;
+}
+
+void blend_impl(VfrIndex *ix, const float *queries, float *out, size_t frames, int32_t width, const float *rate,
+                VfrStream *stream) {
+    require(ix && queries && out && frames > 0 && rate, "invalid FAISS GPU blend arguments");
+    require(frames <= static_cast<size_t>(INT32_MAX), "FAISS frame count exceeds CUDA grid limit");
+    require(width == ix->d, "FAISS feature width mismatch");
+    cudaStream_t s = stream_of(stream);
+    DeviceGuard guard(ix->device);
+    if (ix->have_tc && use_tc(ix, frames)) {
+        run_tc(ix, queries, out, rate, kModeBlend, 8, nullptr, nullptr, frames, s);
+    } else {
+        launch_exact(exact_args(ix, queries, out, rate, kModeBlend), static_cast<long long>(frames), s);
+    }
+    cuda_check(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace vfr
+
+using vfr::guarded;
+using vfr::require;
+
+extern "C" int vocal_faiss_gpu_create(int32_t dimensions, int32_t nlist, int32_t nprobe, size_t vector_count,
+                                      const float *centroids, size_t centroid_count, const int32_t *offsets,
+                                      size_t offset_count, const float *vectors, size_t vector_value_count,
+                                      const int32_t *ids, size_t id_count, VfrIndex **out, char **error) {
+    return guarded(error, [&] {
+        require(out, "null FAISS GPU index output");
+        *out = nullptr;
+        *out = vfr::create_index(dimensions, nlist, nprobe, vector_count, centroids, centroid_count, offsets,
+                                 offset_count, vectors, vector_value_count, ids, id_count, nullptr);
+    });
+}
+
+extern "C" int vfr_retrieval_create(int32_t dimensions, int32_t nlist, int32_t nprobe, size_t vector_count,
+                                    const float *centroids, size_t centroid_count, const int32_t *offsets,
+                                    size_t offset_count, const float *vectors, size_t vector_value_count,
+                                    const int32_t *ids, size_t id_count, const VfrOptions *options,
+                                    VfrIndex **out, char **error) {
+    return guarded(error, [&] {
+        require(out, "null FAISS GPU index output");
+        *out = nullptr;
+        *out = vfr::create_index(dimensions, nlist, nprobe, vector_count, centroids, centroid_count, offsets,
+                                 offset_count, vectors, vector_value_count, ids, id_count, options);
+    });
+}
+
+extern "C" void vocal_faiss_gpu_destroy(VfrIndex *index) { vfr::free_index(index); }
+
+extern "C" int vocal_faiss_gpu_blend(VfrIndex *index, float *features, size_t frames, int32_t width,
+                                     const float *index_rate, VfrStream *stream, char **error) {
+    return guarded(error, [&] { vfr::blend_impl(index, features, features, frames, width, index_rate, stream); });
+}
+
+extern "C" int vfr_retrieval_blend_from(VfrIndex *index, const float *queries, float *out, size_t frames,
+                                        int32_t width, const float *index_rate, VfrStream *stream, char **error) {
+    return guarded(error, [&] { vfr::blend_impl(index, queries, out, frames, width, index_rate, stream); });
+}
+
+extern "C" int vfr_retrieval_search(VfrIndex *index, const float *queries, size_t frames, int32_t width, int32_t k,
+                                    float *distances, int64_t *labels, VfrStream *stream, char **error) {
+    return guarded(error, [&] {
+        require(index && queries && distances && labels && frames > 0, "invalid FAISS GPU search arguments");
+        require(frames <= static_cast<size_t>(INT32_MAX), "FAISS frame count exceeds CUDA grid limit");
+        require(width == index->d, "FAISS feature width mismatch");
+        require(k >= 1 && k <= vfr::kTopK, "search k must be in 1..8");
+        cudaStream_t s = vfr::stream_of(stream);
+        vfr::DeviceGuard guard(index->device);
+        if (index->have_tc && vfr::use_tc(index, frames)) {
+            vfr::run_tc(index, queries, nullptr, nullptr, vfr::kModeSearch, k, distances, labels, frames, s);
+        } else {
+            vfr::ExactArgs a = vfr::exact_args(index, queries, nullptr, nullptr, vfr::kModeSearch);
+            a.k = k;
+            a.dist_out = distances;
+            a.label_out = labels;
+            vfr::launch_exact(a, static_cast<long long>(frames), s);
+        }
+        vfr::cuda_check(cudaGetLastError());
+    });
+}
+
+extern "C" int vfr_retrieval_reserve(VfrIndex *index, size_t max_frames, char **error) {
+    return guarded(error, [&] {
+        require(index, "null index");
+        require(max_frames <= static_cast<size_t>(INT32_MAX), "FAISS frame count exceeds CUDA grid limit");
+        vfr::DeviceGuard guard(index->device);
+        if (index->have_tc) vfr::reserve_tc(index, max_frames);
+    });
+}
+
+extern "C" size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t length) {
+    if (!index) return 0;
+    vfr::DeviceCounters c{};
+    int previous = 0;
+    cudaGetDevice(&previous);
+    cudaSetDevice(index->device);
+    cudaDeviceSynchronize();
+    cudaMemcpy(&c, index->counters, sizeof(c), cudaMemcpyDeviceToHost);
+    cudaSetDevice(previous);
+    const char *engine = index->engine == VFR_ENGINE_EXACT ? "exact" : index->engine == VFR_ENGINE_TENSOR ? "tensor"
+                                                                                                          : "auto";
+    char buf[1024];
+    int m = std::snprintf(buf, sizeof(buf),
+                          "{\"engine\":\"%s\",\"tensor_cores\":%s,\"candidates\":%d,\"dimensions\":%d,\"nlist\":%d,"
+                          "\"nprobe\":%d,\"vectors\":%lld,\"label_base\":%lld,\"device\":%d,\"workspace_frames\":%zu,"
+                          "\"workspace_bytes\":%zu,\"empty_frames\":%llu,\"fallback_frames\":%llu,"
+                          "\"candidate_frames\":%llu,\"timeouts\":%llu,\"max_row_norm\":%.9g,"
+                          "\"max_row_residual\":%.9g}",
+                          engine, index->have_tc ? "true" : "false", index->candidates, index->d, index->nlist,
+                          index->nprobe, static_cast<long long>(index->n), static_cast<long long>(index->label_base),
+                          index->device, index->ws.frames, index->ws.bytes, c.empty_frames, c.fallback_frames,
+                          c.candidate_frames, c.timeouts, index->max_row_norm, index->max_row_residual);
+    size_t need = m > 0 ? static_cast<size_t>(m) : 0;
+    if (json && length) {
+        size_t w = std::min(need, length - 1);
+        std::memcpy(json, buf, w);
+        json[w] = 0;
+    }
+    return need;
+}
+
+extern "C" void vfr_free_error(char *message) { std::free(message); }
+
+// ---- host index (parse / VFRM / upload) -----------------------------------
+
+extern "C" int vfr_index_parse_faiss(const uint8_t *bytes, size_t length, VfrHostIndex **out, char **error) {
+    return guarded(error, [&] {
+        require(out, "null index output");
+        *out = nullptr;
+        auto *h = new VfrHostIndex{};
+        try {
+            h->h = vfr::parse_faiss(bytes, length);
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+}
+
+extern "C" int vfr_index_from_vfrm(const uint8_t *image, size_t length, int32_t feature_dims, VfrHostIndex **out,
+                                   char **error) {
+    return guarded(error, [&] {
+        require(out && image, "null VFRM input or output");
+        *out = nullptr;
+        size_t off = 0, size = 0;
+        if (!vfr::find_vfrm_faiss(image, length, &off, &size)) return;
+        auto *h = new VfrHostIndex{};
+        try {
+            h->h = vfr::parse_faiss(image + off, size);
+            if (feature_dims > 0 && h->h.d != feature_dims)
+                throw std::runtime_error("RVC retrieval index: index feature width does not match the voice model");
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+}
+
+extern "C" void vfr_index_free(VfrHostIndex *index) { delete index; }
+
+extern "C" void vfr_index_info(const VfrHostIndex *index, int32_t *dimensions, int32_t *nlist, int32_t *nprobe,
+                               int64_t *vector_count) {
+    if (!index) return;
+    if (dimensions) *dimensions = index->h.d;
+    if (nlist) *nlist = index->h.nlist;
+    if (nprobe) *nprobe = index->h.nprobe;
+    if (vector_count) *vector_count = index->h.n;
+}
+extern "C" const float *vfr_index_centroids(const VfrHostIndex *index) { return index ? index->h.centroids.data() : nullptr; }
+extern "C" const int32_t *vfr_index_offsets(const VfrHostIndex *index) { return index ? index->h.offsets.data() : nullptr; }
+extern "C" const float *vfr_index_vectors(const VfrHostIndex *index) { return index ? index->h.vectors.data() : nullptr; }
+extern "C" const int32_t *vfr_index_ids(const VfrHostIndex *index) { return index ? index->h.ids.data() : nullptr; }
+
+extern "C" int vfr_index_upload(const VfrHostIndex *index, VfrIndex **out, char **error) {
+    return guarded(error, [&] {
+        require(index && out, "null index or output");
+        require(index->h.n > 0, "retrieval index has no vectors");
+        const auto &h = index->h;
+        *out = nullptr;
+        *out = vfr::create_index(h.d, h.nlist, h.nprobe, static_cast<size_t>(h.n), h.centroids.data(),
+                                 h.centroids.size(), h.offsets.data(), h.offsets.size(), h.vectors.data(),
+                                 h.vectors.size(), h.ids.data(), h.ids.size(), nullptr);
+    });
+}
+
+// ---- sharded building blocks ----------------------------------------------
+
+extern "C" int vfr_merge_topk(const float *dist, const int64_t *labels, int32_t shards, size_t frames,
+                              float *out_dist, int64_t *out_labels, VfrStream *stream, char **error) {
+    return guarded(error, [&] {
+        require(dist && labels && out_dist && out_labels, "invalid merge arguments");
+        require(shards >= 1 && shards <= 64, "shard count must be in 1..64");
+        require(frames <= static_cast<size_t>(INT32_MAX), "frame count exceeds CUDA grid limit");
+        vfr::launch_merge_topk(dist, labels, shards, static_cast<long long>(frames), out_dist, out_labels,
+                               vfr::stream_of(stream));
+        vfr::cuda_check(cudaGetLastError());
+    });
+}
+
+extern "C" int vfr_gather_owned(VfrIndex *index, const int64_t *labels, size_t frames, float *out, VfrStream *stream,
+                                char **error) {
+    return guarded(error, [&] {
+        require(index && labels && out, "invalid gather arguments");
+        require(index->row_of_id, "index ids are not a permutation of 0..n");
+        require(frames <= static_cast<size_t>(INT32_MAX) / 8, "frame count exceeds CUDA grid limit");
+        vfr::DeviceGuard guard(index->device);
+        vfr::launch_gather_owned(index->vectors, index->row_of_id, index->n, index->label_base, index->d, labels,
+                                 static_cast<long long>(frames), out, vfr::stream_of(stream));
+        vfr::cuda_check(cudaGetLastError());
+    });
+}
+
+extern "C" int vfr_blend_gathered(const float *queries, float *out, const float *dist, const float *neighbours,
+                                  size_t frames, int32_t width, const float *index_rate, VfrStream *stream,
+                                  char **error) {
+    return guarded(error, [&] {
+        require(queries && out && dist && neighbours && index_rate, "invalid blend arguments");
+        require(width > 0 && width <= 4096, "invalid feature width");
+        require(frames <= static_cast<size_t>(INT32_MAX), "frame count exceeds CUDA grid limit");
+        vfr::launch_blend_gathered(queries, out, dist, neighbours, static_cast<long long>(frames), width, index_rate,
+                                   vfr::stream_of(stream));
+        vfr::cuda_check(cudaGetLastError());
+    });
+}

@@ -1,0 +1,123 @@
+// Device primitives shared by the exact (SIMT) and tensor-core paths.
+//
+// Exactness contract: distances, neighbour order and blended features equal
+// the reference CPU retrieval (crates/vocal-cpu/src/retrieval.rs:5-83)
+// bit-for-bit.  Every floating-point operation below therefore uses an
+// explicit round-to-nearest intrinsic so nvcc cannot contract mul+add into
+// FMA, and every reduction follows the reference's order:
+//   * avx2_l2 (retrieval.rs:10-26): eight lane accumulators, lane j summing
+//     (a_i - b_i)^2 for i = j (mod 8), i < 8*floor(d/8), in increasing i,
+//     starting at +0.0; the lanes folded 0..7 starting at -0.0 (Rust's float
+//     Sum); plus the tail folded the same way (scalar_l2, :5-7);
+//   * weights (:69-73): w = 1 / (max(d, 1e-12f) as f64)^2, S = sum of the 8
+//     slots (unfilled slots are 0) from -0.0;
+//   * blend (:74-81): r_j = sum_k ((x_kj as f64) * w_k / S) from -0.0, to f32,
+//     q_j = q_j * (1 - r) + r_j * r in f32.
+#pragma once
+
+#include <cstdint>
+
+namespace vfr {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+constexpr unsigned long long kEmptyKey = ~0ull;
+
+// f32 -> u32 whose unsigned order is f32::total_cmp order.
+__device__ __forceinline__ uint32_t total_order_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float from_total_order_bits(uint32_t u) {
+    return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+// Neighbour key: distance in total order, then scan position (probe rank
+// major, storage row minor) -- the order in which the reference's insertion
+// top-8 keeps the earlier-scanned row on a distance tie.
+__device__ __forceinline__ unsigned long long make_key(float dist, uint32_t scan_pos) {
+    return (static_cast<unsigned long long>(total_order_bits(dist)) << 32) | scan_pos;
+}
+__device__ __forceinline__ float key_dist(unsigned long long key) {
+    return from_total_order_bits(static_cast<uint32_t>(key >> 32));
+}
+__device__ __forceinline__ uint32_t key_pos(unsigned long long key) { return static_cast<uint32_t>(key); }
+
+// Sorted ascending top-8 of keys held in registers by each thread.
+struct Top8 {
+    unsigned long long k[8];
+    __device__ __forceinline__ void init() {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) k[i] = kEmptyKey;
+    }
+    __device__ __forceinline__ void insert(unsigned long long key) {
+        if (key >= k[7]) return;
+        k[7] = key;
+#pragma unroll
+        for (int i = 7; i > 0; --i) {
+            if (k[i] < k[i - 1]) {
+                unsigned long long t = k[i];
+                k[i] = k[i - 1];
+                k[i - 1] = t;
+            }
+        }
+    }
+};
+
+// Squared L2 distance between q (shared memory) and x (global), computed by
+// the 8 threads of an "octet" (lanes 8o..8o+7 of a warp), in the AVX2 order.
+// All 8 threads return the same value.  `mask` covers the calling lanes.
+__device__ __forceinline__ float octet_l2(const float *__restrict__ q, const float *__restrict__ x, int d, int j,
+                                          int octet_base, unsigned mask) {
+    const int d8 = d & ~7;
+    float acc = 0.0f;  // _mm256_setzero_ps
+    for (int i = j; i < d8; i += 8) {
+        float t = __fsub_rn(q[i], __ldg(x + i));
+        acc = __fadd_rn(acc, __fmul_rn(t, t));
+    }
+    float s = -0.0f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(mask, acc, octet_base + l));
+    float tail = -0.0f;
+    for (int i = d8; i < d; ++i) {
+        float t = __fsub_rn(q[i], __ldg(x + i));
+        tail = __fadd_rn(tail, __fmul_rn(t, t));
+    }
+    return __fadd_rn(s, tail);
+}
+
+// The reference's f64 weights for `count` neighbours; returns S.
+__device__ __forceinline__ double reference_weights(const float *dist, int count, double *w) {
+    double sum = -0.0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        double wk = 0.0;
+        if (k < count) {
+            float s = fmaxf(dist[k], 1e-12f);  // f32::max: NaN yields the other operand
+            double sd = static_cast<double>(s);
+            wk = __ddiv_rn(1.0, __dmul_rn(sd, sd));
+        }
+        w[k] = wk;
+        sum = __dadd_rn(sum, wk);
+    }
+    return sum;
+}
+
+// One output element of the blend: retrieved from the gathered neighbour
+// values v[k] (k < count), then q*(1-r) + retrieved*r.
+__device__ __forceinline__ float reference_blend_element(float q, const float *v, const double *w, double sum,
+                                                         int count, float ratio) {
+    double acc = -0.0;
+    for (int k = 0; k < count; ++k) {
+        double t = __dmul_rn(static_cast<double>(v[k]), w[k]);
+        acc = __dadd_rn(acc, __ddiv_rn(t, sum));
+    }
+    float retrieved = __double2float_rn(acc);
+    return __fadd_rn(__fmul_rn(q, __fsub_rn(1.0f, ratio)), __fmul_rn(retrieved, ratio));
+}
+
+// index_rate as the reference CUDA kernels read it (retrieval_block.cuh:30-31):
+// clamped to [0, 1]; NaN reads as 0.
+__device__ __forceinline__ float load_ratio(const float *index_rate) {
+    return fminf(fmaxf(*index_rate, 0.0f), 1.0f);
+}
+
+}  // namespace vfr

@@ -1,0 +1,52 @@
+// Kernel launch interface between the C ABI (abi.cu) and the kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace vfr {
+
+constexpr int kTopK = 8;       // kTopK, crates/vocal-tensorrt/native/retrieval_kernels.cuh:8
+constexpr int kMaxProbe = 32;  // kMaxProbe, retrieval_kernels.cuh:7
+
+// Device diagnostic counters written by the kernels (one block per index).
+struct DeviceCounters {
+    unsigned long long empty_frames;      // frames whose probed lists held no row
+    unsigned long long fallback_frames;   // frames re-run by the exact scan
+    unsigned long long timeouts;          // bounded waits that gave up
+    unsigned long long candidate_frames;  // frames served by the tensor-core path
+};
+
+enum { kModeBlend = 0, kModeSearch = 1 };
+
+// Exact SIMT engine (exact_kernels.cu).
+struct ExactArgs {
+    int d;
+    int nlist;
+    int nprobe;
+    const float *centroids;
+    const int32_t *offsets;
+    const float *vectors;
+    const int32_t *ids;
+    const float *queries;
+    float *out;  // may alias queries
+    const float *index_rate;
+    int mode;
+    int k;
+    float *dist_out;
+    int64_t *label_out;
+    int64_t label_base;
+    DeviceCounters *counters;
+};
+void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream);
+
+// Sharded helpers (shard_kernels.cu).
+void launch_merge_topk(const float *dist, const int64_t *labels, int shards, long long frames, float *out_dist,
+                       int64_t *out_labels, cudaStream_t stream);
+void launch_gather_owned(const float *vectors, const int32_t *row_of_id, int64_t n, int64_t label_base, int d,
+                         const int64_t *labels, long long frames, float *out, cudaStream_t stream);
+void launch_blend_gathered(const float *queries, float *out, const float *dist, const float *neighbours,
+                           long long frames, int d, const float *index_rate, cudaStream_t stream);
+
+}  // namespace vfr

@@ -1,0 +1,16 @@
+// Tensor-core engine: bf16 shadow of the database, tcgen05/TMEM distance GEMM
+// with fused per-frame candidate selection, exact fp32 re-rank and blend.
+#pragma once
+
+#include "vfr_common.h"
+
+namespace vfr {
+
+void build_tc(VfrIndex *ix);                 // derived layout, at create time
+void release_tc(VfrIndex *ix) noexcept;      // frees what build_tc/reserve_tc made
+void reserve_tc(VfrIndex *ix, size_t frames);  // workspace for `frames` frames
+bool use_tc(const VfrIndex *ix, size_t frames);
+void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, int mode, int k, float *dist_out,
+            int64_t *label_out, size_t frames, cudaStream_t stream);
+
+}  // namespace vfr
