@@ -18,7 +18,7 @@ from parity_cases import make_scaled, reference_fixtures, scaled_configs, tie_fi
 pytestmark = pytest.mark.gpu
 
 THREADS = os.cpu_count() or 1
-ENGINES = ["exact", "auto"]
+ENGINES = ["exact", "auto", "tensor"]
 
 
 def _engine(name):

@@ -49,7 +49,7 @@ __device__ __forceinline__ unsigned long long warp_sort_u64(unsigned long long v
     return v;
 }
 
-__global__ void __launch_bounds__(kThreads) exact_kernel(ExactArgs a) {
+__device__ void exact_frame(const ExactArgs &a, const long long frame) {
     extern __shared__ float q[];  // [d] copy of the frame
     __shared__ unsigned long long probe_keys[kMaxProbe];
     __shared__ unsigned long long wave_keys[kOctets];
@@ -68,10 +68,10 @@ __global__ void __launch_bounds__(kThreads) exact_kernel(ExactArgs a) {
     const int j = tid & 7;
     const int octet_base = lane & ~7;
     const int d = a.d;
-    const long long frame = blockIdx.x;
     const float *src = a.queries + frame * d;
     float *dst = a.out + frame * d;
 
+    if (tid == 0 && a.frame_list && a.counters) atomicAdd(&a.counters->fallback_frames, 1ull);
     float ratio = 1.0f;
     if (a.mode == kModeBlend) {
         ratio = load_ratio(a.index_rate);
@@ -216,12 +216,28 @@ __global__ void __launch_bounds__(kThreads) exact_kernel(ExactArgs a) {
     }
 }
 
+// One CTA per frame, or, with a device frame list (the frames the
+// tensor-core engine could not certify), a fixed grid striding over it.
+__global__ void __launch_bounds__(kThreads) exact_kernel(ExactArgs a) {
+    if (a.frame_list) {
+        const int count = *a.frame_count;
+        for (int i = blockIdx.x; i < count; i += gridDim.x) {
+            exact_frame(a, a.frame_list[i]);
+            __syncthreads();
+        }
+    } else {
+        exact_frame(a, blockIdx.x);
+    }
+}
+
 }  // namespace
 
 void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream) {
     if (frames <= 0) return;
     size_t smem = static_cast<size_t>(args.d) * sizeof(float);
-    exact_kernel<<<static_cast<unsigned>(frames), kThreads, smem, stream>>>(args);
+    unsigned grid = static_cast<unsigned>(frames);
+    if (args.frame_list) grid = static_cast<unsigned>(frames < 1184 ? frames : 1184);
+    exact_kernel<<<grid, kThreads, smem, stream>>>(args);
 }
 
 }  // namespace vfr

@@ -38,7 +38,10 @@ struct ExactArgs {
     int64_t *label_out;
     int64_t label_base;
     DeviceCounters *counters;
+    const int32_t *frame_list;   // optional: frames to process (device)
+    const int32_t *frame_count;  // with frame_list: its length (device)
 };
+// frames: the frame count, or with a frame list the largest possible length.
 void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream);
 
 // Sharded helpers (shard_kernels.cu).

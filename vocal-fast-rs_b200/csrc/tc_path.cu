@@ -1,11 +1,882 @@
+// Tensor-core engine for flat indexes.
+//
+// Per call:
+//   1. prep_queries: fp32 frames -> fp16 (scaled by the index's power-of-two
+//      scale s), plus ||q||^2, ||q^|| and ||q - q^|| for the certificate.
+//   2. cand_kernel (persistent, warp-specialised, tcgen05 + TMA + TMEM): for
+//      each work item (128-frame tile, database segment) the approximate
+//      distance d~ = ||x||^2 - (2/s^2) * (q~ . x~) of every row is formed in the
+//      epilogue straight out of TMEM and filtered per frame against a running
+//      threshold into a shared-memory buffer; the item's 32 smallest
+//      (d~, row) keys per frame go to the workspace.  No frame x row matrix is
+//      written to HBM.
+//   3. merge_kernel: per frame, sort the items' keys, take the 64 smallest,
+//      re-rank them with exact fp32 distances in the reference AVX2 order
+//      (crates/vocal-cpu/src/retrieval.rs:10-26), keep the top 8 in scan
+//      order, and certify that no dropped row can beat the 8th: every dropped
+//      row has d~ >= T, and |d - (d~ + ||q||^2)| <= E with E from the fp16
+//      rounding residuals, fp32 accumulation and norm rounding.  Certified
+//      frames are blended (or their top-k written) exactly like the
+//      reference; the rest are listed for
+//   4. the exact SIMT kernel, which re-runs them.
+// The result is therefore the reference's result for every frame.
+#include <algorithm>
+#include <cmath>
+#include <limits>
+#include <mutex>
+
+#include "exact_common.cuh"
+#include "kernels.h"
 #include "tc_path.h"
+#include "tc_ptx.cuh"
 
 namespace vfr {
-void build_tc(VfrIndex *) {}
-void release_tc(VfrIndex *) noexcept {}
-void reserve_tc(VfrIndex *, size_t) {}
-bool use_tc(const VfrIndex *, size_t) { return false; }
-void run_tc(VfrIndex *, const float *, float *, const float *, int, int, float *, int64_t *, size_t, cudaStream_t) {
-    throw std::runtime_error("tensor-core engine not built");
+namespace {
+
+constexpr int kTileM = 128;  // frames per tile: TMEM lanes
+constexpr int kTileN = 256;  // rows per MMA / accumulator
+constexpr int kTileK = 64;   // fp16 elements per 128-byte swizzled row
+constexpr int kStages = 3;
+constexpr int kCap = 64;       // shared-memory candidate buffer per frame
+constexpr int kItemKeep = 32;  // candidates kept per frame per work item
+constexpr int kRerank = 64;    // candidates re-ranked exactly per frame
+constexpr int kMaxSegments = 256;
+constexpr int kThreadsTC = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr uint32_t kABytes = kTileM * kTileK * 2;
+constexpr uint32_t kBBytes = kTileN * kTileK * 2;
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kCandBytes = kCap * kTileM * 8;
+constexpr size_t kSmemTC = 1024 + kStages * kStageBytes + kCandBytes + 256;
+constexpr uint32_t kTmemCols = 512;  // two 128 x 256 fp32 accumulators
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint32_t kFormatF16 = 0;
+
+struct CandArgs {
+    int n_qtiles;
+    int segments;
+    int tiles_per_seg;
+    int ksteps;
+    int64_t n;
+    int64_t seg_rows;
+    const float *row_norms;
+    float coef;  // -2 / s^2
+    unsigned long long *out_keys;  // [item][kItemKeep][128]
+    int *out_count;                // [item][128]
+    float *out_thr;                // [item][128]
+    DeviceCounters *counters;
+};
+
+// Keeps the `keep` smallest of `count` keys in column r of buf ([slot][128]),
+// in slots 0..keep-1; returns the distance of the largest kept key.
+__device__ __forceinline__ float compact_keys(unsigned long long *buf, int r, int count, int keep) {
+    for (int i = 0; i < keep; ++i) {
+        int m = i;
+        unsigned long long mv = buf[i * kTileM + r];
+        for (int j = i + 1; j < count; ++j) {
+            unsigned long long v = buf[j * kTileM + r];
+            if (v < mv) {
+                mv = v;
+                m = j;
+            }
+        }
+        buf[m * kTileM + r] = buf[i * kTileM + r];
+        buf[i * kTileM + r] = mv;
+    }
+    return key_dist(buf[(keep - 1) * kTileM + r]);
 }
+
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    cand_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, CandArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned long long *cand = reinterpret_cast<unsigned long long *>(smem + kStages * kStageBytes);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes + kCandBytes);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + kStages;
+    uint64_t *acc_full = bars + 2 * kStages;
+    uint64_t *acc_empty = acc_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int items = a.segments * a.n_qtiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&acc_full[b], 1);
+            tc::mbar_init(&acc_empty[b], 4);
+        }
+        *abort_flag = 0;
+        tc::fence_mbarrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tc::tma_prefetch(&tmap_q);
+        tc::tma_prefetch(&tmap_x);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto fail = [&]() {
+        *abort_flag = 1;
+        if (a.counters) atomicAdd(&a.counters->timeouts, 1ull);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
+                const int qtile = item % a.n_qtiles;
+                const int seg = item / a.n_qtiles;
+                const int64_t row0 = seg * a.seg_rows;
+                const int64_t rows = min(a.seg_rows, a.n - row0);
+                const int tiles = static_cast<int>((rows + kTileN - 1) / kTileN);
+                for (int t = 0; t < tiles && !*abort_flag; ++t) {
+                    for (int k = 0; k < a.ksteps; ++k) {
+                        if (!tc::mbar_wait(&empty[stage], phase ^ 1, kWaitLimitNs)) {
+                            fail();
+                            break;
+                        }
+                        uint8_t *sa = smem + stage * kStageBytes;
+                        tc::mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                        tc::tma_load_2d(sa, &tmap_q, &full[stage], k * kTileK, qtile * kTileM);
+                        tc::tma_load_2d(sa + kABytes, &tmap_x, &full[stage], k * kTileK,
+                                        static_cast<int32_t>(row0 + t * kTileN));
+                        if (++stage == kStages) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                }
+            }
+            // let every issued copy land before the CTA can exit
+            for (int s = 0; s < kStages; ++s) {
+                if (!tc::mbar_wait(&empty[stage], phase ^ 1, kWaitLimitNs)) break;
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer (one thread)
+            const uint32_t idesc = tc::idesc_f16(kTileM, kTileN, kFormatF16);
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t acc_count = 0;
+            for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
+                const int seg = item / a.n_qtiles;
+                const int64_t row0 = seg * a.seg_rows;
+                const int64_t rows = min(a.seg_rows, a.n - row0);
+                const int tiles = static_cast<int>((rows + kTileN - 1) / kTileN);
+                for (int t = 0; t < tiles && !*abort_flag; ++t) {
+                    const uint32_t b = acc_count & 1;
+                    if (!tc::mbar_wait(&acc_empty[b], ((acc_count >> 1) & 1) ^ 1, kWaitLimitNs)) {
+                        fail();
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t d_tmem = tmem + b * kTileN;
+                    bool ok = true;
+                    for (int k = 0; k < a.ksteps; ++k) {
+                        if (!tc::mbar_wait(&full[stage], phase, kWaitLimitNs)) {
+                            fail();
+                            ok = false;
+                            break;
+                        }
+                        tc::tc_fence_after();
+                        const uint32_t sa = tc::smem_u32(smem + stage * kStageBytes);
+                        const uint32_t sb = sa + kABytes;
+#pragma unroll
+                        for (int kk = 0; kk < kTileK / 16; ++kk) {
+                            tc::mma_f16(d_tmem, tc::smem_desc_sw128(sa + kk * 32), tc::smem_desc_sw128(sb + kk * 32),
+                                        idesc, (k | kk) != 0);
+                        }
+                        tc::mma_commit(&empty[stage]);
+                        if (++stage == kStages) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                    if (!ok) break;
+                    tc::mma_commit(&acc_full[b]);
+                    ++acc_count;
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue: one thread per frame of the tile
+        const int quarter = warp & 3;  // TMEM lanes this warp may access
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        uint32_t acc_count = 0;
+        const float inf = __int_as_float(0x7f800000);
+        for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
+            const int seg = item / a.n_qtiles;
+            const int64_t row0 = seg * a.seg_rows;
+            const int64_t seg_end = min(row0 + a.seg_rows, a.n);
+            const int tiles = static_cast<int>((seg_end - row0 + kTileN - 1) / kTileN);
+            int cnt = 0;
+            float thr = inf;
+            bool aborted = false;
+            for (int t = 0; t < tiles; ++t) {
+                const uint32_t b = acc_count & 1;
+                // every lane polls; the outcome is made warp-uniform before the
+                // .sync.aligned TMEM loads
+                const bool ready = tc::mbar_wait(&acc_full[b], (acc_count >> 1) & 1, kWaitLimitNs);
+                if (!__all_sync(kFullMask, ready)) {
+                    if (lane == 0) fail();
+                    aborted = true;
+                    break;
+                }
+                tc::tc_fence_after();
+                const int64_t tile_row = row0 + static_cast<int64_t>(t) * kTileN;
+#pragma unroll 1
+                for (int c = 0; c < kTileN / 32; ++c) {
+                    float v[32];
+                    __syncwarp();
+                    tc::tmem_ld32(tmem + lane_addr + b * kTileN + c * 32, v);
+                    const int64_t base = tile_row + c * 32;
+                    const float4 *nrm4 = reinterpret_cast<const float4 *>(a.row_norms + base);
+#pragma unroll
+                    for (int e4 = 0; e4 < 8; ++e4) {
+                        const float4 nn = __ldg(nrm4 + e4);
+                        const float nv[4] = {nn.x, nn.y, nn.z, nn.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int e = e4 * 4 + u;
+                            const float dd = fmaf(a.coef, v[e], nv[u]);
+                            const int64_t row = base + e;
+                            if (dd < thr && row < seg_end) {
+                                cand[cnt * kTileM + r] = make_key(dd, static_cast<uint32_t>(row));
+                                if (++cnt == kCap) {
+                                    thr = compact_keys(cand, r, kCap, kItemKeep);
+                                    cnt = kItemKeep;
+                                }
+                            }
+                        }
+                    }
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
+                ++acc_count;
+            }
+            if (aborted) break;
+            if (cnt > kItemKeep) {
+                thr = compact_keys(cand, r, cnt, kItemKeep);
+                cnt = kItemKeep;
+            }
+            const size_t o = static_cast<size_t>(item) * kTileM + r;
+            for (int i = 0; i < cnt; ++i)
+                a.out_keys[(static_cast<size_t>(item) * kItemKeep + i) * kTileM + r] = cand[i * kTileM + r];
+            a.out_count[o] = cnt;
+            a.out_thr[o] = thr;
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------- queries
+__global__ void prep_queries_kernel(const float *__restrict__ q, __half *__restrict__ qh, float4 *__restrict__ stats,
+                                    long long frames, int d, int d_pad, float scale) {
+    const long long f = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (f >= frames) return;
+    const float inv = 1.0f / scale;  // exact: scale is a power of two
+    float qn2 = 0.f, hat2 = 0.f, res2 = 0.f;
+    for (int k = lane; k < d_pad; k += 32) {
+        float v = k < d ? q[f * d + k] : 0.f;
+        float sv = fminf(fmaxf(v * scale, -65504.f), 65504.f);
+        __half h = __float2half_rn(sv);
+        qh[f * d_pad + k] = h;
+        float back = __half2float(h) * inv;
+        float res = v - back;
+        qn2 = fmaf(v, v, qn2);
+        hat2 = fmaf(back, back, hat2);
+        res2 = fmaf(res, res, res2);
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+        qn2 += __shfl_xor_sync(kFullMask, qn2, s);
+        hat2 += __shfl_xor_sync(kFullMask, hat2, s);
+        res2 += __shfl_xor_sync(kFullMask, res2, s);
+    }
+    if (lane == 0) stats[f] = make_float4(qn2, sqrtf(hat2) * 1.00001f, sqrtf(res2) * 1.00001f, 0.f);
+}
+
+// ---------------------------------------------------------------- merge
+struct MergeArgs {
+    int d;
+    int n_qtiles;
+    int segments;
+    int sort_size;  // power of two >= segments * kItemKeep
+    const unsigned long long *keys;
+    const int *counts;
+    const float *thr;
+    const float4 *qstats;
+    const float *queries;
+    float *out;
+    const float *index_rate;
+    int mode;
+    int k;
+    float *dist_out;
+    int64_t *label_out;
+    int64_t label_base;
+    const float *vectors;
+    const int32_t *ids;
+    float max_norm, max_hat, max_residual;
+    float acc_rel;     // bound on the relative fp32 accumulation error of a dot product
+    float norm_rel;    // bound on the relative error of an fp32 squared norm
+    float exact_rel;   // bound on the relative error of the exact fp32 distance
+    int32_t *fallback_list;
+    int32_t *fallback_count;
+    DeviceCounters *counters;
+};
+
+constexpr int kMergeThreads = 256;
+
+__device__ __forceinline__ unsigned long long warp_min_key(unsigned long long v) {
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+        unsigned long long o = __shfl_xor_sync(kFullMask, v, s);
+        v = o < v ? o : v;
+    }
+    return v;
+}
+
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
+    extern __shared__ __align__(16) uint8_t msm[];
+    unsigned long long *keys = reinterpret_cast<unsigned long long *>(msm);
+    float *q = reinterpret_cast<float *>(msm + static_cast<size_t>(a.sort_size) * 8);
+    __shared__ unsigned long long octet_best[32 * 8];
+    __shared__ unsigned long long best[8];
+    __shared__ float red_f[8];
+    __shared__ int red_i[8];
+    __shared__ int certified_s;
+    __shared__ double weights[8];
+    __shared__ double weight_sum;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
+    const long long frame = blockIdx.x;
+    const int qtile = static_cast<int>(frame / kTileM), r = static_cast<int>(frame % kTileM);
+    const int d = a.d;
+    const float *src = a.queries + frame * d;
+    float *dst = a.out + frame * d;
+    const float inf = __int_as_float(0x7f800000);
+
+    float ratio = 1.f;
+    if (a.mode == kModeBlend) {
+        ratio = load_ratio(a.index_rate);
+        if (!(ratio > 0.f)) {
+            if (dst != src)
+                for (int i = tid; i < d; i += kMergeThreads) dst[i] = src[i];
+            return;
+        }
+    }
+    for (int i = tid; i < d; i += kMergeThreads) q[i] = src[i];
+    // gather the items' candidate keys for this frame
+    float tmin = inf;
+    int total = 0;
+    for (int s = tid; s < a.segments; s += kMergeThreads) {
+        const size_t o = (static_cast<size_t>(s) * a.n_qtiles + qtile) * kTileM + r;
+        tmin = fminf(tmin, a.thr[o]);
+        total += a.counts[o];
+    }
+    for (int i = tid; i < a.sort_size; i += kMergeThreads) {
+        const int s = i / kItemKeep, slot = i % kItemKeep;
+        unsigned long long key = kEmptyKey;
+        if (s < a.segments) {
+            const size_t item = static_cast<size_t>(s) * a.n_qtiles + qtile;
+            if (slot < a.counts[item * kTileM + r]) key = a.keys[(item * kItemKeep + slot) * kTileM + r];
+        }
+        keys[i] = key;
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+        tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, s));
+        total += __shfl_xor_sync(kFullMask, total, s);
+    }
+    if (lane == 0) {
+        red_f[warp] = tmin;
+        red_i[warp] = total;
+    }
+    __syncthreads();
+    tmin = inf;
+    total = 0;
+    for (int w = 0; w < kMergeThreads / 32; ++w) {
+        tmin = fminf(tmin, red_f[w]);
+        total += red_i[w];
+    }
+    // bitonic sort of the candidate keys (ascending)
+    for (int kk = 2; kk <= a.sort_size; kk <<= 1) {
+        for (int jj = kk >> 1; jj > 0; jj >>= 1) {
+            for (int i = tid; i < a.sort_size; i += kMergeThreads) {
+                const int ixj = i ^ jj;
+                if (ixj > i) {
+                    const unsigned long long x = keys[i], y = keys[ixj];
+                    const bool asc = (i & kk) == 0;
+                    if ((x > y) == asc) {
+                        keys[i] = y;
+                        keys[ixj] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    const int m = total < kRerank ? total : kRerank;
+    const float t_final = fminf(tmin, total > kRerank ? key_dist(keys[kRerank]) : inf);
+
+    // exact re-rank in the reference order; flat scan position == row
+    Top8 top;
+    top.init();
+    for (int c0 = 0; c0 < m; c0 += 32) {
+        const int c = c0 + octet;
+        const bool valid = c < m;
+        const uint32_t row = key_pos(keys[valid ? c : 0]);
+        const float dist = octet_l2(q, a.vectors + static_cast<size_t>(row) * d, d, j, lane & ~7, kFullMask);
+        if (valid && dist < inf) top.insert(make_key(dist, row));
+    }
+    if (j == 0)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) octet_best[octet * 8 + i] = top.k[i];
+    __syncthreads();
+    if (warp == 0) {
+        int head = 0;
+        for (int i = 0; i < 8; ++i) {
+            unsigned long long mine = head < 8 ? octet_best[lane * 8 + head] : kEmptyKey;
+            unsigned long long mn = warp_min_key(mine);
+            if (mine == mn && mn != kEmptyKey) ++head;
+            if (lane == 0) best[i] = mn;
+        }
+        if (lane == 0) {
+            int count = 0;
+            while (count < 8 && best[count] != kEmptyKey) ++count;
+            bool ok = true;
+            if (t_final < inf || t_final != t_final) {
+                // something was dropped: certify that it cannot reach the top 8
+                const float4 st = a.qstats[frame];
+                const float d8 = count == 8 ? key_dist(best[7]) : inf;
+                const float e = 2.f * (st.y * a.max_residual + st.z * a.max_norm) +
+                                2.f * a.acc_rel * st.y * a.max_hat +
+                                a.norm_rel * (a.max_norm * a.max_norm + st.x) +
+                                6e-8f * (a.max_norm * a.max_norm + 2.f * st.y * a.max_hat);
+                const float lower = t_final + st.x - e;
+                ok = lower > d8 * (1.f + 4.f * a.exact_rel) + 1e-30f;
+            }
+            certified_s = ok ? count + 1 : 0;  // 0 = not certified, else count + 1
+        }
+    }
+    __syncthreads();
+    const int cert = certified_s;
+    if (cert == 0) {
+        if (tid == 0) {
+            const int pos = atomicAdd(a.fallback_count, 1);
+            a.fallback_list[pos] = static_cast<int32_t>(frame);
+        }
+        return;
+    }
+    const int count = cert - 1;
+    if (tid == 0 && a.counters) atomicAdd(&a.counters->candidate_frames, 1ull);
+    if (a.mode == kModeSearch) {
+        if (tid < a.k) {
+            const bool have = tid < count;
+            a.dist_out[frame * a.k + tid] = have ? key_dist(best[tid]) : inf;
+            a.label_out[frame * a.k + tid] =
+                have ? static_cast<int64_t>(a.ids[key_pos(best[tid])]) + a.label_base : -1;
+        }
+        return;
+    }
+    if (count == 0) {
+        if (tid == 0 && a.counters) atomicAdd(&a.counters->empty_frames, 1ull);
+        if (dst != src)
+            for (int i = tid; i < d; i += kMergeThreads) dst[i] = q[i];
+        return;
+    }
+    if (tid == 0) {
+        float dist[8];
+        double w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dist[i] = key_dist(best[i]);
+        weight_sum = reference_weights(dist, count, w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) weights[i] = w[i];
+    }
+    __syncthreads();
+    double w[8];
+    uint32_t rows[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        w[i] = weights[i];
+        rows[i] = key_pos(best[i]);
+    }
+    const double sum = weight_sum;
+    for (int i = tid; i < d; i += kMergeThreads) {
+        float v[8];
+#pragma unroll
+        for (int kq = 0; kq < 8; ++kq)
+            v[kq] = kq < count ? __ldg(a.vectors + static_cast<size_t>(rows[kq]) * d + i) : 0.f;
+        dst[i] = reference_blend_element(q[i], v, w, sum, count, ratio);
+    }
+}
+
+// ---------------------------------------------------------------- index build
+__global__ void max_abs_kernel(const float *__restrict__ x, size_t count, unsigned int *out) {
+    float m = 0.f;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        float v = fabsf(x[i]);
+        m = v > m ? v : m;  // NaN never enters (the parser rejects non-finite values)
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, s));
+    if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+// One warp per row: fp16 shadow, fp32 squared norm, and the maxima of the
+// row norm, the fp16 row's norm and the rounding residual norm.
+__global__ void build_rows_kernel(const float *__restrict__ x, __half *__restrict__ xh, float *__restrict__ norms,
+                                  int64_t n, int d, int d_pad, float scale, unsigned int *maxima) {
+    const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    const float inv = 1.0f / scale;
+    float n2 = 0.f, hat2 = 0.f, res2 = 0.f;
+    for (int k = lane; k < d_pad; k += 32) {
+        float v = k < d ? x[row * d + k] : 0.f;
+        __half h = __float2half_rn(v * scale);
+        xh[row * d_pad + k] = h;
+        float back = __half2float(h) * inv;
+        float res = v - back;
+        n2 = fmaf(v, v, n2);
+        hat2 = fmaf(back, back, hat2);
+        res2 = fmaf(res, res, res2);
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+        n2 += __shfl_xor_sync(kFullMask, n2, s);
+        hat2 += __shfl_xor_sync(kFullMask, hat2, s);
+        res2 += __shfl_xor_sync(kFullMask, res2, s);
+    }
+    if (lane == 0) {
+        norms[row] = n2;
+        atomicMax(&maxima[0], __float_as_uint(sqrtf(n2)));
+        atomicMax(&maxima[1], __float_as_uint(sqrtf(hat2)));
+        atomicMax(&maxima[2], __float_as_uint(sqrtf(res2)));
+    }
+}
+
+__global__ void fill_kernel(float *p, size_t count, float value) {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        p[i] = value;
+}
+
+// ---------------------------------------------------------------- host helpers
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    require(fn != nullptr, "cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+// 2-D fp16 tensor map over a row-major [rows][cols] matrix, box [box_rows][64],
+// 128-byte swizzle; out-of-range rows read as zero.
+void encode_rows(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+    require(reinterpret_cast<uintptr_t>(base) % 16 == 0 && (cols * 2) % 16 == 0, "tensor map alignment");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult rc = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    require(rc == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed");
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Plan {
+    int n_qtiles, segments, tiles_per_seg;
+};
+
+Plan make_plan(size_t frames, int64_t n, int sms) {
+    Plan p{};
+    p.n_qtiles = static_cast<int>((frames + kTileM - 1) / kTileM);
+    const int64_t ntiles = (n + kTileN - 1) / kTileN;
+    const int64_t cap = std::max<int64_t>(static_cast<int64_t>(p.n_qtiles) * 16, static_cast<int64_t>(sms) * 8);
+    double best = 1e300;
+    p.segments = 1;
+    p.tiles_per_seg = static_cast<int>(ntiles);
+    for (int64_t s = 1; s <= std::min<int64_t>(kMaxSegments, ntiles); ++s) {
+        const int64_t tps = (ntiles + s - 1) / s;
+        const int64_t seg = (ntiles + tps - 1) / tps;
+        if (seg * p.n_qtiles > cap) break;
+        const int64_t waves = (seg * p.n_qtiles + sms - 1) / sms;
+        const double cost = static_cast<double>(waves * tps) + 0.02 * static_cast<double>(seg);
+        if (cost < best - 1e-9) {
+            best = cost;
+            p.segments = static_cast<int>(seg);
+            p.tiles_per_seg = static_cast<int>(tps);
+        }
+    }
+    return p;
+}
+
+int64_t items_cap(size_t frames, int sms) {
+    const int64_t qt = static_cast<int64_t>((frames + kTileM - 1) / kTileM);
+    return std::max<int64_t>(qt * 16, static_cast<int64_t>(sms) * 8);
+}
+
+struct WsLayout {
+    size_t q16, qstats, keys, counts, thr, flist, fcount, total;
+};
+
+WsLayout ws_layout(size_t frames, int d_pad, int sms) {
+    WsLayout l{};
+    const size_t fr = (frames + kTileM - 1) / kTileM * kTileM;
+    const size_t items = static_cast<size_t>(items_cap(frames, sms));
+    size_t off = 0;
+    l.q16 = off;
+    off = align256(off + fr * d_pad * sizeof(__half));
+    l.qstats = off;
+    off = align256(off + fr * sizeof(float4));
+    l.keys = off;
+    off = align256(off + items * kItemKeep * kTileM * sizeof(unsigned long long));
+    l.counts = off;
+    off = align256(off + items * kTileM * sizeof(int));
+    l.thr = off;
+    off = align256(off + items * kTileM * sizeof(float));
+    l.flist = off;
+    off = align256(off + fr * sizeof(int32_t));
+    l.fcount = off;
+    off = align256(off + 16);
+    l.total = off;
+    return l;
+}
+
+}  // namespace
+
+void build_tc(VfrIndex *ix) {
+    if (ix->nlist != 1) return;  // IVF indexes use the exact engine
+    int dev = 0;
+    cuda_check(cudaGetDevice(&dev));
+    cuda_check(cudaDeviceGetAttribute(&ix->sm_count, cudaDevAttrMultiProcessorCount, dev));
+    ix->d_pad = (ix->d + kTileK - 1) / kTileK * kTileK;
+    ix->n_pad = (ix->n + kTileN - 1) / kTileN * kTileN;
+    const size_t hbytes = static_cast<size_t>(ix->n_pad) * ix->d_pad * sizeof(__half);
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->vectors_h), hbytes), "cudaMalloc fp16 shadow");
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->row_norms), ix->n_pad * sizeof(float)), "cudaMalloc norms");
+    cuda_check(cudaMemset(ix->vectors_h, 0, hbytes));
+    unsigned int *maxima = nullptr;
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&maxima), 4 * sizeof(unsigned int)));
+    cuda_check(cudaMemset(maxima, 0, 4 * sizeof(unsigned int)));
+    const size_t values = static_cast<size_t>(ix->n) * ix->d;
+    max_abs_kernel<<<1024, 256>>>(ix->vectors, values, maxima + 3);
+    cuda_check(cudaGetLastError());
+    unsigned int maxabs_bits = 0;
+    cuda_check(cudaMemcpy(&maxabs_bits, maxima + 3, 4, cudaMemcpyDeviceToHost));
+    float maxabs;
+    std::memcpy(&maxabs, &maxabs_bits, 4);
+    // power-of-two scale keeping |s x| within [1, 8192] where possible, so
+    // frames up to 8x the database's magnitude still fit fp16
+    int e = 0;
+    if (maxabs > 0.f) {
+        const int ex = static_cast<int>(std::floor(std::log2(maxabs)));
+        if (ex > 13) e = 13 - ex;
+        if (ex < 0) e = -ex;
+    }
+    ix->tc_scale = std::ldexp(1.0f, e);
+    fill_kernel<<<64, 256>>>(ix->row_norms + ix->n, static_cast<size_t>(ix->n_pad - ix->n),
+                             std::numeric_limits<float>::infinity());
+    const long long warps = ix->n;
+    build_rows_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256>>>(
+        ix->vectors, ix->vectors_h, ix->row_norms, ix->n, ix->d, ix->d_pad, ix->tc_scale, maxima);
+    cuda_check(cudaGetLastError());
+    unsigned int m[3];
+    cuda_check(cudaMemcpy(m, maxima, sizeof(m), cudaMemcpyDeviceToHost));
+    cudaFree(maxima);
+    float mf[3];
+    std::memcpy(mf, m, sizeof(mf));
+    ix->max_row_norm = mf[0] * 1.0001f;
+    ix->max_row_hat = mf[1] * 1.0001f;
+    ix->max_row_residual = mf[2] * 1.0001f + 1e-30f;
+    if (!std::isfinite(ix->max_row_norm) || !std::isfinite(ix->max_row_hat)) {
+        // squared norms overflow fp32: the candidate bounds are meaningless,
+        // so this index stays on the exact engine
+        release_tc(ix);
+        return;
+    }
+    encode_rows(&ix->tmap_vectors, ix->vectors_h, ix->d_pad, ix->n_pad, kTileN);
+    cuda_check(cudaFuncSetAttribute(cand_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kSmemTC)));
+    cuda_check(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    ix->have_tc = true;
+}
+
+void release_tc(VfrIndex *ix) noexcept {
+    if (ix->vectors_h) cudaFree(ix->vectors_h);
+    if (ix->row_norms) cudaFree(ix->row_norms);
+    if (ix->ws.base) cudaFree(ix->ws.base);
+    ix->vectors_h = nullptr;
+    ix->row_norms = nullptr;
+    ix->ws = Workspace{};
+    ix->have_tc = false;
+}
+
+void reserve_tc(VfrIndex *ix, size_t frames) {
+    if (!ix->have_tc || frames <= ix->ws.frames) return;
+    const WsLayout l = ws_layout(frames, ix->d_pad, ix->sm_count);
+    void *p = nullptr;
+    cuda_check(cudaMalloc(&p, l.total), "cudaMalloc retrieval workspace");
+    if (ix->ws.base) {
+        cuda_check(cudaDeviceSynchronize());
+        cudaFree(ix->ws.base);
+    }
+    ix->ws.base = p;
+    ix->ws.bytes = l.total;
+    ix->ws.frames = frames;
+}
+
+bool use_tc(const VfrIndex *ix, size_t frames) {
+    if (!ix->have_tc || ix->engine == VFR_ENGINE_EXACT) return false;
+    if (ix->engine == VFR_ENGINE_TENSOR) return true;
+    // AUTO: tiny databases are cheaper on the exact engine alone
+    return ix->n >= 2048 && frames >= 1;
+}
+
+void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, int mode, int k, float *dist_out,
+            int64_t *label_out, size_t frames, cudaStream_t stream) {
+    if (frames > ix->ws.frames) {
+        cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+        cuda_check(cudaStreamIsCapturing(stream, &st));
+        require(st == cudaStreamCaptureStatusNone,
+                "retrieval workspace too small for this frame count during stream capture; call "
+                "vfr_retrieval_reserve first");
+        reserve_tc(ix, frames);
+    }
+    const WsLayout l = ws_layout(ix->ws.frames, ix->d_pad, ix->sm_count);
+    uint8_t *ws = static_cast<uint8_t *>(ix->ws.base);
+    __half *q16 = reinterpret_cast<__half *>(ws + l.q16);
+    float4 *qstats = reinterpret_cast<float4 *>(ws + l.qstats);
+    auto *keys = reinterpret_cast<unsigned long long *>(ws + l.keys);
+    int *counts = reinterpret_cast<int *>(ws + l.counts);
+    float *thr = reinterpret_cast<float *>(ws + l.thr);
+    int32_t *flist = reinterpret_cast<int32_t *>(ws + l.flist);
+    int32_t *fcount = reinterpret_cast<int32_t *>(ws + l.fcount);
+
+    const Plan p = make_plan(frames, ix->n, ix->sm_count);
+    const long long lanes = static_cast<long long>(frames) * 32;
+    prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
+        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale);
+    cuda_check(cudaGetLastError());
+    cuda_check(cudaMemsetAsync(fcount, 0, sizeof(int32_t), stream));
+
+    CUtensorMap tmap_q;
+    encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
+    CandArgs ca{};
+    ca.n_qtiles = p.n_qtiles;
+    ca.segments = p.segments;
+    ca.tiles_per_seg = p.tiles_per_seg;
+    ca.ksteps = ix->d_pad / kTileK;
+    ca.n = ix->n;
+    ca.seg_rows = static_cast<int64_t>(p.tiles_per_seg) * kTileN;
+    ca.row_norms = ix->row_norms;
+    ca.coef = -2.0f / (ix->tc_scale * ix->tc_scale);
+    ca.out_keys = keys;
+    ca.out_count = counts;
+    ca.out_thr = thr;
+    ca.counters = ix->counters;
+    const int items = p.segments * p.n_qtiles;
+    const int grid = std::min(items, ix->sm_count);
+    cand_kernel<<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    cuda_check(cudaGetLastError());
+
+    MergeArgs ma{};
+    ma.d = ix->d;
+    ma.n_qtiles = p.n_qtiles;
+    ma.segments = p.segments;
+    int sort = 32;
+    while (sort < p.segments * kItemKeep) sort <<= 1;
+    ma.sort_size = sort;
+    ma.keys = keys;
+    ma.counts = counts;
+    ma.thr = thr;
+    ma.qstats = qstats;
+    ma.queries = queries;
+    ma.out = out;
+    ma.index_rate = rate;
+    ma.mode = mode;
+    ma.k = k;
+    ma.dist_out = dist_out;
+    ma.label_out = label_out;
+    ma.label_base = ix->label_base;
+    ma.vectors = ix->vectors;
+    ma.ids = ix->ids;
+    ma.max_norm = ix->max_row_norm;
+    ma.max_hat = ix->max_row_hat;
+    ma.max_residual = ix->max_row_residual;
+    ma.acc_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -22);
+    ma.norm_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -23);
+    ma.exact_rel = static_cast<float>(ix->d / 8 + 9) * std::ldexp(1.0f, -24);
+    ma.fallback_list = flist;
+    ma.fallback_count = fcount;
+    ma.counters = ix->counters;
+    const size_t msmem = static_cast<size_t>(sort) * 8 + static_cast<size_t>(ix->d) * 4;
+    merge_kernel<<<static_cast<unsigned>(frames), kMergeThreads, msmem, stream>>>(ma);
+    cuda_check(cudaGetLastError());
+
+    // frames the certificate could not settle: exact re-run
+    ExactArgs ea{};
+    ea.d = ix->d;
+    ea.nlist = ix->nlist;
+    ea.nprobe = ix->nprobe;
+    ea.centroids = ix->centroids;
+    ea.offsets = ix->offsets;
+    ea.vectors = ix->vectors;
+    ea.ids = ix->ids;
+    ea.queries = queries;
+    ea.out = out;
+    ea.index_rate = rate;
+    ea.mode = mode;
+    ea.k = k;
+    ea.dist_out = dist_out;
+    ea.label_out = label_out;
+    ea.label_base = ix->label_base;
+    ea.counters = ix->counters;
+    ea.frame_list = flist;
+    ea.frame_count = fcount;
+    launch_exact(ea, static_cast<long long>(frames), stream);
+}
+
 }  // namespace vfr

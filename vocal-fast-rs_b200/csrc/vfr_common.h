@@ -3,7 +3,7 @@
 #pragma once
 
 #include <cuda.h>
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -87,20 +87,20 @@ struct VfrIndex {
     int32_t *row_of_id = nullptr;  // [n] inverse permutation of ids
     vfr::DeviceCounters *counters = nullptr;
     std::vector<int32_t> host_offsets;  // list bounds, for host-side dispatch
-    // Tensor-core layout (built when the engine uses tensor cores).
-    __nv_bfloat16 *vectors_bf16 = nullptr;    // [n_pad][d_pad] K-major, zero padded
-    __nv_bfloat16 *centroids_bf16 = nullptr;  // [nlist_pad][d_pad]
-    float *row_norms = nullptr;               // [n_pad] ||x||^2 (fp32 of the fp32 row), +inf on padding
-    float *centroid_norms = nullptr;          // [nlist_pad]
-    int32_t d_pad = 0;                        // d rounded up to 64
-    int64_t n_pad = 0;                        // n rounded up to 256
-    int32_t nlist_pad = 0;
-    float max_row_norm = 0.f;       // max ||x||
-    float max_row_residual = 0.f;   // max ||x - bf16(x)||
-    float max_centroid_norm = 0.f;
-    float max_centroid_residual = 0.f;
-    alignas(64) CUtensorMap tmap_vectors;    // bf16 rows, box [256][64]
-    alignas(64) CUtensorMap tmap_centroids;  // bf16 centroids, box [256][64]
+    // Tensor-core layout (built when the engine uses tensor cores): an fp16
+    // shadow of the rows scaled by a power of two, K-major with rows padded
+    // to 256 and width to 64, and per-row fp32 squared norms.
+    __half *vectors_h = nullptr;   // [n_pad][d_pad], zero padded
+    float *row_norms = nullptr;    // [n_pad] ||x||^2, +inf on padding rows
+    int32_t d_pad = 0;
+    int64_t n_pad = 0;
+    float tc_scale = 1.f;          // power of two applied before fp16 rounding
+    // Bounds used by the exactness certificate (host copies, rounded up).
+    float max_row_norm = 0.f;      // max ||x||
+    float max_row_hat = 0.f;       // max ||fp16(s x) / s||
+    float max_row_residual = 0.f;  // max ||x - fp16(s x) / s||
+    int sm_count = 148;
+    alignas(64) CUtensorMap tmap_vectors;  // fp16 rows, box [256 rows][64]
     bool have_tc = false;
     vfr::Workspace ws;
 };
