@@ -1,0 +1,418 @@
+#!/usr/bin/env python
+"""Benchmark of the feature-retrieval hot path (k=8 L2 search + inverse-square
+gather-blend) on B200, one process per GPU.
+
+Headline workload (`--workload c5`, default): flat index of N=4,000,000 x 768
+fp32 rows from a seeded 4,096-component Gaussian mixture, Q=30,000 query
+frames per step, k=8, blend at index_rate 0.75.  With --gpus N>1 the rows are
+sharded across ranks (NCCL all-gather of per-shard top-8 + merge + exact
+blend), so the total work per step is fixed (strong scaling).  A step is one
+blend of the Q frames (out of place, so every step sees the same inputs).
+
+Printed JSON line (rank 0): value = frames/s of the whole job over K timed
+steps (device time, max over ranks); e2e = the same metric through the
+drop-in C ABI (vocal_faiss_gpu_blend) with pinned host buffers and the
+host<->device copies inside the timed region; roofline = the candidate GEMM
+kernel (cand_kernel) timed with CUDA events on its stream during the timed
+steps; cpu_baseline = the CPU oracle (restatement of the reference's CPU
+retrieval) on a bounded sample of frames against the same database, all host
+cores; streaming = the c4 realtime config (Q=32 frames per block, N=100,000)
+replayed as a CUDA graph, p50/p95 per-block latency over 1,000 blocks.
+
+`--impl reference` times the reference's CPU retrieval (the oracle port; the
+Rust original cannot be built here) on the same workload instead.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "vocal-fast-rs_b200"), ROOT]
+
+METRIC = "kNN queries/s (768-d, k=8) at 1/2/4/8 B200; p50 per-block latency"
+UNIT = "queries/s"
+
+
+def args_parse():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["vfr", "reference"], default="vfr")
+    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c4", "c5"])
+    ap.add_argument("--queries", type=int, default=0, help="override frames per step")
+    ap.add_argument("--rows", type=int, default=0, help="override database rows (testing only)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-streaming", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self, devices):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in devices:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None, "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def dist_setup(gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------- reference arm
+def run_reference(a, world, rank):
+    if rank != 0:
+        return  # rank 0 alone runs the CPU reference
+    import numpy as np
+    import torch
+
+    from oracle import oracle
+    from vfr import synth
+
+    w = synth.CONFIGS[a.workload]
+    n = a.rows or w.n
+    dev = "cuda" if torch.cuda.is_available() else None
+    if dev:
+        arrays, queries = synth.make_torch(a.workload, dev, n=n, q=a.queries or w.q)
+        vectors = arrays["vectors"].cpu().numpy()
+        queries = queries.cpu().numpy()
+        del arrays
+        torch.cuda.empty_cache()
+    else:
+        ix, queries = synth.make_np(a.workload, n=n, q=a.queries or w.q)
+        vectors = ix.vectors
+    flat = synth.flat_arrays(vectors)
+    orc = oracle.OracleIndex.from_arrays(flat.centroids, flat.offsets, flat.vectors, flat.ids, 1)
+    cores = os.cpu_count() or 1
+    sample = max(cores, 8)
+    times = []
+    for step in range(a.warmup + a.steps):
+        s0 = (step * sample) % max(1, queries.shape[0] - sample)
+        t0 = time.perf_counter()
+        orc.blend(queries[s0:s0 + sample], w.ratio, threads=cores)
+        dt = time.perf_counter() - t0
+        if step >= a.warmup:
+            times.append(dt)
+    value = sample * len(times) / sum(times)
+    desc = f"{sample} frames per step against all {n} rows, {cores} threads, AVX2 order"
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(a, w, n, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(a, w, n, world):
+    return {"workload": f"{w.key} {w.name}: flat N={n} x {w.d} fp32, Q={a.queries or w.q} frames/step, k=8, "
+                        f"index_rate={w.ratio}",
+            "rows": n, "dims": w.d, "frames_per_step": a.queries or w.q, "k": 8, "index_rate": w.ratio,
+            "sharding": f"rows/{world}" if world > 1 else "none",
+            "l2": "inputs larger than L2 (fp16 row shadow alone exceeds 126 MB)"}
+
+
+# ---------------------------------------------------------------------------- our arm
+def cpu_baseline(vectors, queries, ratio, n):
+    from oracle import oracle
+    from vfr import synth
+
+    cores = os.cpu_count() or 1
+    flat = synth.flat_arrays(vectors)
+    orc = oracle.OracleIndex.from_arrays(flat.centroids, flat.offsets, flat.vectors, flat.ids, 1)
+    sample = max(cores, 8)
+    t0 = time.perf_counter()
+    orc.blend(queries[:sample], ratio, threads=cores)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"first {sample} frames against all {n} rows ({dt:.1f} s), AVX2-order C restatement, "
+                      f"{cores} threads"}
+
+
+def streaming(device):
+    """c4: Q=32-frame blocks against 100k rows, CUDA-graph replay, per-block latency."""
+    import numpy as np
+    import torch
+
+    from vfr import GpuRetrievalIndex, synth
+
+    w = synth.CONFIGS["c4"]
+    arrays, block0 = synth.make_torch("c4", device, q=w.q)
+    g = torch.Generator(device=device)
+    g.manual_seed(4004)
+    blocks = torch.empty((w.blocks, w.q, w.d), device=device)
+    blocks[0] = block0
+    for b in range(1, w.blocks):
+        blocks[b] = blocks[b - 1] + w.walk * torch.randn((w.q, w.d), generator=g, device=device)
+    idx = GpuRetrievalIndex.from_arrays(arrays["centroids"], arrays["offsets"], arrays["vectors"], arrays["ids"], 1,
+                                        max_frames=w.q)
+    del arrays
+    feats = torch.empty((w.q, w.d), device=device)
+    rate = torch.tensor([w.ratio], device=device)
+    s = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        feats.copy_(blocks[0])
+        idx.blend(feats, w.q, rate, stream=s)
+        graph = torch.cuda.CUDAGraph()
+        feats.copy_(blocks[0])
+        with torch.cuda.graph(graph, stream=s):
+            idx.blend(feats, w.q, rate, stream=s)
+        start = [torch.cuda.Event(enable_timing=True) for _ in range(w.blocks)]
+        end = [torch.cuda.Event(enable_timing=True) for _ in range(w.blocks)]
+        for b in range(20):
+            feats.copy_(blocks[b])
+            graph.replay()
+        for b in range(w.blocks):
+            feats.copy_(blocks[b])  # reset outside the events, as the reference benchmark does
+            start[b].record(s)
+            graph.replay()
+            end[b].record(s)
+    s.synchronize()
+    lat = sorted(start[b].elapsed_time(end[b]) for b in range(w.blocks))
+    diag = idx.diagnostics()
+    del graph
+    idx.close()
+    p50 = lat[len(lat) // 2]
+    hbm_bytes = 100_000 * 768 * 2 + 100_000 * 4 + w.q * 64 * 768 * 4
+    return {"workload": "c4 rvc-v2-stream-100k: flat N=100000 x 768, 1000 blocks of Q=32 (random walk), graph replay",
+            "p50_block_ms": p50, "p95_block_ms": lat[int(len(lat) * 0.95)], "mean_block_ms": sum(lat) / len(lat),
+            "blocks": w.blocks, "frames_per_s_at_p50": w.q / (p50 / 1000),
+            "hbm_bytes_per_block": hbm_bytes, "hbm_gbs_at_p50": hbm_bytes / (p50 / 1000) / 1e9,
+            "fallback_frames": diag["fallback_frames"]}
+
+
+def main():
+    a = args_parse()
+    world, rank, local = dist_setup(a.gpus)
+    if a.impl == "reference":
+        run_reference(a, world, rank)
+        return
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from vfr import GpuRetrievalIndex, synth
+    from vfr.sharded import LibraryOps, padded_frames, shard_rows, sharded_blend
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        group = dist.group.WORLD
+    w = synth.CONFIGS[a.workload]
+    n = a.rows or w.n
+    q = padded_frames(a.queries or w.q, world)
+    peaks, peak_kind = measured_peaks()
+
+    # ---- data (seeded, identical on every rank) and index
+    arrays, queries = synth.make_torch(a.workload, device, n=n, q=q)
+    lo, hi = shard_rows(n, world, rank)
+    host_vectors = arrays["vectors"][lo:hi].cpu().numpy()
+    full_host = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        full_host = host_vectors
+    del arrays
+    torch.cuda.empty_cache()
+    ops = LibraryOps(host_vectors, label_base=lo, max_frames=q)
+    if full_host is None:
+        del host_vectors
+    rate = torch.tensor([w.ratio], device=device)
+    out = torch.empty_like(queries)
+    s = torch.cuda.Stream(device)
+    torch.cuda.synchronize()
+
+    def step():
+        if world == 1:
+            ops.index.blend_from(queries, out, rate, stream=s)
+            return 4  # prep_queries, cand_kernel, merge_kernel, exact_kernel
+        sharded_blend(ops, queries, rate, group, world, rank, stream=s)
+        return 7  # + merge_topk, gather_owned, blend_gathered
+
+    with torch.cuda.stream(s):
+        for _ in range(a.warmup):
+            step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    launches = 0
+    ops.index.profile(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(a.steps):
+            launches += step()
+        e1.record(s)
+    torch.cuda.synchronize()
+    ms_local = e0.elapsed_time(e1)
+    prof = ops.index.profile(False)
+    clocks = sampler.stop(set(range(8))) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([ms_local], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = q * a.steps / (ms / 1000.0)
+
+    # ---- roofline of the dominant kernel (tensor-bound distance GEMM)
+    cand = prof["cand_kernel"]
+    n_local = hi - lo
+    flops_per_launch = 2.0 * q * n_local * w.d
+    cand_s = cand["ms"] / max(1, cand["launches"]) / 1000.0
+    achieved = flops_per_launch / cand_s / 1e12 if cand["launches"] else None
+    peak = peaks.get("bf16_tflops_sustained", 1400.0)
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            tj = json.load(f)
+        per_row = tj.get(f"cand_kernel/{a.workload}", {}).get("dram_bytes_per_frame_row")
+        if per_row:
+            traffic = per_row * q * n_local
+    roofline = {"bound": "tensor", "kernel": "cand_kernel", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak if achieved else None, "traffic": traffic,
+                "peak_source": f"{peak_kind} bf16_tflops_sustained (dense fp16 and bf16 share the rate)",
+                "algorithmic": f"2*Q*N*d = {flops_per_launch:.4g} FLOP per launch (Q={q}, N={n_local}, d={w.d})",
+                "kernel_ms": cand_s * 1000, "step_share": cand["ms"] / ms_local if ms_local else None,
+                "kernels_ms": {k: v["ms"] / max(1, v["launches"]) for k, v in prof.items()}}
+
+    # ---- e2e through the drop-in C ABI with pinned host buffers
+    e2e = None
+    if not a.no_e2e:
+        host_in = queries.cpu().pin_memory()
+        m = q // world
+        host_out = torch.empty((m if world > 1 else q, w.d), dtype=torch.float32).pin_memory()
+        feats = torch.empty_like(queries)
+
+        def e2e_step():
+            feats.copy_(host_in, non_blocking=True)
+            if world == 1:
+                ops.index.blend(feats, q, rate, stream=s)  # vocal_faiss_gpu_blend, in place
+                host_out.copy_(feats, non_blocking=True)
+            else:
+                o, _, _ = sharded_blend(ops, feats, rate, group, world, rank, stream=s)
+                host_out.copy_(o, non_blocking=True)
+
+        with torch.cuda.stream(s):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            f0.record(s)
+            for _ in range(a.steps):
+                e2e_step()
+            f1.record(s)
+        torch.cuda.synchronize()
+        te = torch.tensor([f0.elapsed_time(f1)], device=device)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": q * a.steps / (float(te.item()) / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": int(host_in.numel() * 4), "d2h_bytes_per_step": int(host_out.numel() * 4),
+               "api": "vocal_faiss_gpu_blend" if world == 1 else "vfr_retrieval_search + NCCL + vfr_blend_gathered"}
+
+    diag = ops.index.diagnostics()
+    extra = {}
+    if rank == 0 and world == 1 and not a.no_streaming:
+        extra["streaming"] = streaming(device)
+    cpu = None
+    if rank == 0 and world == 1 and full_host is not None:
+        cpu = cpu_baseline(full_host, queries.cpu().numpy(), w.ratio, n)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16 candidates, f32 exact distances, f64 weights", "data": "synthetic",
+        "config": workload_config(a, w, n, world), "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu,
+        "clocks": clocks, "gpu_launches": launches,
+        "exactness": {"fallback_frames": diag["fallback_frames"], "certified_frames": diag["candidate_frames"],
+                      "timeouts": diag["timeouts"]},
+    }
+    line.update(extra)
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -159,6 +159,13 @@ VFR_API int vfr_retrieval_blend_from(VfrIndex *index, const float *queries, floa
  * length bytes including NUL.  Synchronises the index's device. */
 VFR_API size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t length);
 
+/* Per-kernel timing with CUDA events recorded on the call's stream around
+ * every kernel the index launches (eager calls only; not during capture).
+ * enable = 1 clears and starts recording, enable = 0 stops.  Writes JSON
+ * {"kernel": {"launches": L, "ms": T}, ...} of what was recorded so far
+ * (synchronises the recorded events); returns the length needed. */
+VFR_API size_t vfr_retrieval_profile(VfrIndex *index, int32_t enable, char *json, size_t length);
+
 /* Row-sharded multi-GPU building blocks (one process per GPU; the exchange is
  * a collective of the caller's choice, NCCL all-gather in the Python host).
  *

@@ -1,0 +1,144 @@
+"""World-size-2 `gloo` test of the row-sharded choreography (vfr/sharded.py)
+on CPU: shard ranges, the all-gather of per-shard top-8 lists, the merge by
+(distance, global row), the owned-vector exchange whose -0.0 padding makes the
+reduce-scatter exact, and the per-rank output slices.  The per-rank compute is
+a test double over the CPU oracle; the CUDA kernels of the same steps are
+covered by tests/test_parity.py::test_row_sharded_blocks_reproduce_single_index.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class OracleOps:
+    """Test double of vfr.sharded.LibraryOps on CPU tensors."""
+
+    def __init__(self, vectors_slice, label_base):
+        import sys
+
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path[:0] = [os.path.join(root, "vocal-fast-rs_b200"), root]
+        from oracle import oracle
+        from vfr import synth
+
+        flat = synth.flat_arrays(vectors_slice)
+        self.ix = oracle.OracleIndex.from_arrays(flat.centroids, flat.offsets, flat.vectors, flat.ids, 1)
+        self.base = label_base
+        self.vectors = vectors_slice
+
+    def search(self, q, stream):
+        dist, rows, labels, _ = self.ix.search(q.numpy())
+        labels = np.where(labels >= 0, labels + self.base, -1)
+        return torch.from_numpy(dist), torch.from_numpy(labels)
+
+    def merge(self, dists, labels, stream):
+        D, L = dists.numpy(), labels.numpy()
+        shards, q, _ = D.shape
+        md = np.full((q, 8), np.inf, np.float32)
+        ml = np.full((q, 8), -1, np.int64)
+        for f in range(q):
+            cand = [(D[s, f, k], L[s, f, k]) for s in range(shards) for k in range(8) if L[s, f, k] >= 0]
+            cand.sort(key=lambda t: (float(t[0]), int(t[1])))
+            for k, (dd, ll) in enumerate(cand[:8]):
+                md[f, k], ml[f, k] = dd, ll
+        return torch.from_numpy(md), torch.from_numpy(ml)
+
+    def gather_owned(self, labels, stream):
+        L = labels.numpy()
+        out = np.full(L.shape + (self.vectors.shape[1],), -0.0, np.float32)
+        local = L - self.base
+        own = (L >= 0) & (local >= 0) & (local < len(self.vectors))
+        out[own] = self.vectors[local[own]]
+        return torch.from_numpy(out)
+
+    def blend(self, q, dist, neighbours, rate, stream):
+        """The reference's f64 weights + f32 blend in numpy (IEEE, same order)."""
+        qn, dn, nb = q.numpy(), dist.numpy(), neighbours.numpy()
+        r = np.float32(min(max(float(rate[0]), 0.0), 1.0))
+        out = qn.copy()
+        for f in range(qn.shape[0]):
+            count = int(np.argmax(~np.isfinite(np.append(dn[f], np.inf))))
+            if count == 0 or not r > 0:
+                continue
+            w = [1.0 / (float(max(dn[f, k], np.float32(1e-12))) ** 2) for k in range(count)] + [0.0] * (8 - count)
+            s = -0.0
+            for x in w:
+                s = s + x
+            acc = np.full(qn.shape[1], -0.0)
+            for k in range(count):
+                acc = acc + (nb[f, k].astype(np.float64) * w[k]) / s
+            out[f] = qn[f] * (np.float32(1) - r) + acc.astype(np.float32) * r
+        return torch.from_numpy(out)
+
+
+def _worker(rank, world, port, vectors, queries, ratio, results):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "vocal-fast-rs_b200"), root, os.path.join(root, "tests")]
+    import datetime
+
+    import torch.distributed as dist
+    from test_sharded_cpu import OracleOps
+    from vfr.sharded import shard_rows, sharded_blend
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    lo, hi = shard_rows(len(vectors), world, rank)
+    ops = OracleOps(vectors[lo:hi], lo)
+    out, md, ml = sharded_blend(ops, torch.from_numpy(queries), torch.tensor([ratio]), dist.group.WORLD, world, rank)
+    results[rank] = (out.numpy(), md.numpy(), ml.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_row_sharded_choreography_matches_single_index(oracle, world):
+    from vfr import synth
+
+    ix, q = synth.make_np("c1", n=3001, q=40)
+    q[3] = ix.vectors[17]  # exact match
+    ix.vectors[2999] = ix.vectors[5]  # duplicate rows in different shards: tie -> lower row
+    q[4] = ix.vectors[5]
+    ratio = 0.75
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, ix.vectors, q, ratio, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    orc = oracle.OracleIndex.from_arrays(ix.centroids, ix.offsets, ix.vectors, ix.ids, 1)
+    expected, status = orc.blend(q, ratio)
+    dist, rows, labels, _ = orc.search(q)
+    got = np.concatenate([results[r][0] for r in range(world)])
+    assert (status == 0).all()
+    assert np.array_equal(got.view(np.uint32), expected.view(np.uint32))
+    for r in range(world):
+        assert np.array_equal(results[r][2], labels)
+        assert np.array_equal(results[r][1].view(np.uint32), dist.view(np.uint32))
+    assert labels[4, 0] == 5 and labels[4, 1] == 2999
+
+
+def test_shard_rows_cover_everything():
+    from vfr.sharded import padded_frames, shard_rows
+
+    for n in (1, 7, 4_000_000):
+        for world in (1, 2, 3, 8):
+            spans = [shard_rows(n, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    assert padded_frames(30000, 8) == 30000 and padded_frames(30001, 8) == 30008

@@ -164,7 +164,9 @@ void blend_impl(VfrIndex *ix, const float *queries, float *out, size_t frames, i
     if (ix->have_tc && use_tc(ix, frames)) {
         run_tc(ix, queries, out, rate, kModeBlend, 8, nullptr, nullptr, frames, s);
     } else {
+        ix->prof.begin(kProfExact, s);
         launch_exact(exact_args(ix, queries, out, rate, kModeBlend), static_cast<long long>(frames), s);
+        ix->prof.end(s);
     }
     cuda_check(cudaGetLastError());
 }
@@ -272,6 +274,40 @@ extern "C" size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t 
         json[w] = 0;
     }
     return need;
+}
+
+extern "C" size_t vfr_retrieval_profile(VfrIndex *index, int32_t enable, char *json, size_t length) {
+    if (!index) return 0;
+    auto &p = index->prof;
+    static const char *names[vfr::kProfCount] = {"prep_queries", "cand_kernel", "merge_kernel", "exact_kernel"};
+    double ms[vfr::kProfCount] = {0, 0, 0, 0};
+    long long launches[vfr::kProfCount] = {0, 0, 0, 0};
+    for (auto &m : p.marks) {
+        if (m.second + 1 >= p.used) continue;
+        float t = 0.f;
+        cudaEventSynchronize(p.pool[m.second + 1]);
+        if (cudaEventElapsedTime(&t, p.pool[m.second], p.pool[m.second + 1]) == cudaSuccess) {
+            ms[m.first] += t;
+            launches[m.first] += 1;
+        }
+    }
+    std::string out = "{";
+    for (int k = 0; k < vfr::kProfCount; ++k) {
+        char buf[160];
+        std::snprintf(buf, sizeof(buf), "%s\"%s\":{\"launches\":%lld,\"ms\":%.6f}", k ? "," : "", names[k],
+                      launches[k], ms[k]);
+        out += buf;
+    }
+    out += "}";
+    p.marks.clear();
+    p.used = 0;
+    p.enabled = enable != 0;
+    if (json && length) {
+        size_t w = std::min(out.size(), length - 1);
+        std::memcpy(json, out.data(), w);
+        json[w] = 0;
+    }
+    return out.size();
 }
 
 extern "C" void vfr_free_error(char *message) { std::free(message); }

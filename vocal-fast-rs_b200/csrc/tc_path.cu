@@ -36,17 +36,15 @@ namespace {
 constexpr int kTileM = 128;  // frames per tile: TMEM lanes
 constexpr int kTileN = 256;  // rows per MMA / accumulator
 constexpr int kTileK = 64;   // fp16 elements per 128-byte swizzled row
-constexpr int kStages = 3;
-constexpr int kCap = 64;       // shared-memory candidate buffer per frame
-constexpr int kItemKeep = 32;  // candidates kept per frame per work item
+constexpr int kStages = 4;
+constexpr int kItemKeep = 16;  // candidates kept per frame per work item (registers)
 constexpr int kRerank = 64;    // candidates re-ranked exactly per frame
 constexpr int kMaxSegments = 256;
 constexpr int kThreadsTC = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t kABytes = kTileM * kTileK * 2;
 constexpr uint32_t kBBytes = kTileN * kTileK * 2;
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kCandBytes = kCap * kTileM * 8;
-constexpr size_t kSmemTC = 1024 + kStages * kStageBytes + kCandBytes + 256;
+constexpr size_t kSmemTC = 1024 + kStages * kStageBytes + 256;
 constexpr uint32_t kTmemCols = 512;  // two 128 x 256 fp32 accumulators
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kFormatF16 = 0;
@@ -66,31 +64,32 @@ struct CandArgs {
     DeviceCounters *counters;
 };
 
-// Keeps the `keep` smallest of `count` keys in column r of buf ([slot][128]),
-// in slots 0..keep-1; returns the distance of the largest kept key.
-__device__ __forceinline__ float compact_keys(unsigned long long *buf, int r, int count, int keep) {
-    for (int i = 0; i < keep; ++i) {
-        int m = i;
-        unsigned long long mv = buf[i * kTileM + r];
-        for (int j = i + 1; j < count; ++j) {
-            unsigned long long v = buf[j * kTileM + r];
-            if (v < mv) {
-                mv = v;
-                m = j;
-            }
-        }
-        buf[m * kTileM + r] = buf[i * kTileM + r];
-        buf[i * kTileM + r] = mv;
+// Sorted ascending list of the kItemKeep smallest keys seen, in registers.
+// Insertion is a fixed compare-exchange chain, so lanes of a warp that insert
+// in the same step execute it once together.
+struct TopList {
+    unsigned long long k[kItemKeep];
+    __device__ __forceinline__ void init() {
+#pragma unroll
+        for (int i = 0; i < kItemKeep; ++i) k[i] = kEmptyKey;
     }
-    return key_dist(buf[(keep - 1) * kTileM + r]);
-}
+    __device__ __forceinline__ void insert(unsigned long long key) {
+        k[kItemKeep - 1] = key;
+#pragma unroll
+        for (int i = kItemKeep - 1; i > 0; --i) {
+            const unsigned long long a = k[i - 1], b = k[i];
+            const bool swap = b < a;
+            k[i - 1] = swap ? b : a;
+            k[i] = swap ? a : b;
+        }
+    }
+};
 
 __global__ void __launch_bounds__(kThreadsTC, 1)
     cand_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, CandArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned long long *cand = reinterpret_cast<unsigned long long *>(smem + kStages * kStageBytes);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes + kCandBytes);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
     uint64_t *full = bars;
     uint64_t *empty = bars + kStages;
     uint64_t *acc_full = bars + 2 * kStages;
@@ -229,8 +228,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             const int64_t row0 = seg * a.seg_rows;
             const int64_t seg_end = min(row0 + a.seg_rows, a.n);
             const int tiles = static_cast<int>((seg_end - row0 + kTileN - 1) / kTileN);
-            int cnt = 0;
-            float thr = inf;
+            TopList top;
+            top.init();
+            float thr = inf;  // distance of the kItemKeep-th key; +inf until the list is full
             bool aborted = false;
             for (int t = 0; t < tiles; ++t) {
                 const uint32_t b = acc_count & 1;
@@ -244,6 +244,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 }
                 tc::tc_fence_after();
                 const int64_t tile_row = row0 + static_cast<int64_t>(t) * kTileN;
+                const int64_t left = seg_end - tile_row;
+                const int valid = left < kTileN ? static_cast<int>(left) : kTileN;
 #pragma unroll 1
                 for (int c = 0; c < kTileN / 32; ++c) {
                     float v[32];
@@ -251,6 +253,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     tc::tmem_ld32(tmem + lane_addr + b * kTileN + c * 32, v);
                     const int64_t base = tile_row + c * 32;
                     const float4 *nrm4 = reinterpret_cast<const float4 *>(a.row_norms + base);
+                    const int lim = valid - c * 32;  // columns >= lim belong to the next segment
 #pragma unroll
                     for (int e4 = 0; e4 < 8; ++e4) {
                         const float4 nn = __ldg(nrm4 + e4);
@@ -258,14 +261,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
                             const int e = e4 * 4 + u;
-                            const float dd = fmaf(a.coef, v[e], nv[u]);
-                            const int64_t row = base + e;
-                            if (dd < thr && row < seg_end) {
-                                cand[cnt * kTileM + r] = make_key(dd, static_cast<uint32_t>(row));
-                                if (++cnt == kCap) {
-                                    thr = compact_keys(cand, r, kCap, kItemKeep);
-                                    cnt = kItemKeep;
-                                }
+                            const float dd = fmaf(a.coef, v[e], e < lim ? nv[u] : inf);
+                            if (dd < thr) {
+                                top.insert(make_key(dd, static_cast<uint32_t>(base + e)));
+                                thr = key_dist(top.k[kItemKeep - 1]);
+                                if (top.k[kItemKeep - 1] == kEmptyKey) thr = inf;
                             }
                         }
                     }
@@ -276,15 +276,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 ++acc_count;
             }
             if (aborted) break;
-            if (cnt > kItemKeep) {
-                thr = compact_keys(cand, r, cnt, kItemKeep);
-                cnt = kItemKeep;
-            }
+            int cnt = 0;
+#pragma unroll
+            for (int i = 0; i < kItemKeep; ++i) cnt += top.k[i] != kEmptyKey;
             const size_t o = static_cast<size_t>(item) * kTileM + r;
-            for (int i = 0; i < cnt; ++i)
-                a.out_keys[(static_cast<size_t>(item) * kItemKeep + i) * kTileM + r] = cand[i * kTileM + r];
+#pragma unroll
+            for (int i = 0; i < kItemKeep; ++i)
+                if (i < cnt) a.out_keys[(static_cast<size_t>(item) * kItemKeep + i) * kTileM + r] = top.k[i];
             a.out_count[o] = cnt;
-            a.out_thr[o] = thr;
+            a.out_thr[o] = cnt == kItemKeep ? thr : inf;
         }
     }
     tc::tc_fence_before();
@@ -797,9 +797,11 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
 
     const Plan p = make_plan(frames, ix->n, ix->sm_count);
     const long long lanes = static_cast<long long>(frames) * 32;
+    ix->prof.begin(kProfPrep, stream);
     prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
         queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale);
     cuda_check(cudaGetLastError());
+    ix->prof.end(stream);
     cuda_check(cudaMemsetAsync(fcount, 0, sizeof(int32_t), stream));
 
     CUtensorMap tmap_q;
@@ -819,8 +821,10 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
     const int grid = std::min(items, ix->sm_count);
+    ix->prof.begin(kProfCand, stream);
     cand_kernel<<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
     cuda_check(cudaGetLastError());
+    ix->prof.end(stream);
 
     MergeArgs ma{};
     ma.d = ix->d;
@@ -853,8 +857,10 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ma.fallback_count = fcount;
     ma.counters = ix->counters;
     const size_t msmem = static_cast<size_t>(sort) * 8 + static_cast<size_t>(ix->d) * 4;
+    ix->prof.begin(kProfMerge, stream);
     merge_kernel<<<static_cast<unsigned>(frames), kMergeThreads, msmem, stream>>>(ma);
     cuda_check(cudaGetLastError());
+    ix->prof.end(stream);
 
     // frames the certificate could not settle: exact re-run
     ExactArgs ea{};
@@ -876,7 +882,9 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ea.counters = ix->counters;
     ea.frame_list = flist;
     ea.frame_count = fcount;
+    ix->prof.begin(kProfExact, stream);
     launch_exact(ea, static_cast<long long>(frames), stream);
+    ix->prof.end(stream);
 }
 
 }  // namespace vfr

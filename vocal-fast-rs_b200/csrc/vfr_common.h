@@ -61,6 +61,19 @@ HostIndex parse_faiss(const uint8_t *bytes, size_t length);
 bool find_vfrm_faiss(const uint8_t *image, size_t length, size_t *offset, size_t *size);
 
 // Workspace of the tensor-core path, sized for `frames` frames.
+// Event-pair timing of library kernels (bench instrumentation).
+struct Profiler {
+    bool enabled = false;
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+    std::vector<std::pair<int, size_t>> marks;  // (kernel id, start event index)
+    cudaEvent_t next(cudaStream_t s);
+    void begin(int kernel, cudaStream_t s);
+    void end(cudaStream_t s);
+    ~Profiler();
+};
+enum { kProfPrep = 0, kProfCand = 1, kProfMerge = 2, kProfExact = 3, kProfCount = 4 };
+
 struct Workspace {
     size_t frames = 0;
     void *base = nullptr;
@@ -103,6 +116,7 @@ struct VfrIndex {
     alignas(64) CUtensorMap tmap_vectors;  // fp16 rows, box [256 rows][64]
     bool have_tc = false;
     vfr::Workspace ws;
+    vfr::Profiler prof;
 };
 
 struct VfrHostIndex {

@@ -206,6 +206,16 @@ class GpuRetrievalIndex:
         L.vfr_retrieval_diagnostics(self._h, buf, need + 1)
         return json.loads(buf.value.decode())
 
+    def profile(self, enable: bool) -> dict:
+        """Per-kernel CUDA-event times recorded since the last call; `enable`
+        starts (True) or stops (False) recording from now on."""
+        L = load_library()
+        buf = ctypes.create_string_buffer(4096)  # one call: reading also resets
+        need = L.vfr_retrieval_profile(self._h, int(enable), buf, 4096)
+        if need >= 4096:
+            raise RuntimeError("profile report truncated")
+        return json.loads(buf.value.decode())
+
     # -- row-sharded helpers ----------------------------------------------------
     def gather_owned(self, labels, out, stream=None) -> None:
         L = load_library()
