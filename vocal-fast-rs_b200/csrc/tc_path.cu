@@ -44,7 +44,8 @@ constexpr int kThreadsTC = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t kABytes = kTileM * kTileK * 2;
 constexpr uint32_t kBBytes = kTileN * kTileK * 2;
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr size_t kSmemTC = 1024 + kStages * kStageBytes + 256;
+constexpr uint32_t kNormBytes = 4 * 2 * kTileN * sizeof(float);  // per epilogue warp, double buffered
+constexpr size_t kSmemTC = 1024 + kStages * kStageBytes + kNormBytes + 256;
 constexpr uint32_t kTmemCols = 512;  // two 128 x 256 fp32 accumulators
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kFormatF16 = 0;
@@ -64,23 +65,33 @@ struct CandArgs {
     DeviceCounters *counters;
 };
 
-// Sorted ascending list of the kItemKeep smallest keys seen, in registers.
-// Insertion is a fixed compare-exchange chain, so lanes of a warp that insert
-// in the same step execute it once together.
+// Sorted ascending list of the kItemKeep smallest approximate distances seen
+// (with their rows), in registers.  Insertion is a fixed compare-exchange
+// chain, so the lanes of a warp that insert in the same step share it.  Ties
+// between equal approximate distances may resolve either way: only "every
+// dropped row has d~ >= the threshold" matters to the exact stage.
 struct TopList {
-    unsigned long long k[kItemKeep];
+    float dist[kItemKeep];
+    uint32_t row[kItemKeep];
     __device__ __forceinline__ void init() {
 #pragma unroll
-        for (int i = 0; i < kItemKeep; ++i) k[i] = kEmptyKey;
+        for (int i = 0; i < kItemKeep; ++i) {
+            dist[i] = __int_as_float(0x7f800000);
+            row[i] = 0;
+        }
     }
-    __device__ __forceinline__ void insert(unsigned long long key) {
-        k[kItemKeep - 1] = key;
+    __device__ __forceinline__ void insert(float dd, uint32_t r) {
+        dist[kItemKeep - 1] = dd;
+        row[kItemKeep - 1] = r;
 #pragma unroll
         for (int i = kItemKeep - 1; i > 0; --i) {
-            const unsigned long long a = k[i - 1], b = k[i];
-            const bool swap = b < a;
-            k[i - 1] = swap ? b : a;
-            k[i] = swap ? a : b;
+            const bool swap = dist[i] < dist[i - 1];
+            const float lo = swap ? dist[i] : dist[i - 1], hi = swap ? dist[i - 1] : dist[i];
+            const uint32_t rl = swap ? row[i] : row[i - 1], rh = swap ? row[i - 1] : row[i];
+            dist[i - 1] = lo;
+            dist[i] = hi;
+            row[i - 1] = rl;
+            row[i] = rh;
         }
     }
 };
@@ -89,7 +100,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     cand_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, CandArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+    float *norm_smem = reinterpret_cast<float *>(smem + kStages * kStageBytes);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes + kNormBytes);
     uint64_t *full = bars;
     uint64_t *empty = bars + kStages;
     uint64_t *acc_full = bars + 2 * kStages;
@@ -230,10 +242,27 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             const int tiles = static_cast<int>((seg_end - row0 + kTileN - 1) / kTileN);
             TopList top;
             top.init();
-            float thr = inf;  // distance of the kItemKeep-th key; +inf until the list is full
             bool aborted = false;
+            // This warp's copy of the row norms, one tile ahead: lane l holds
+            // norms [8l, 8l+8) of the next tile in registers until the current
+            // tile is done, then stores them into the other buffer.
+            float *nbuf = norm_smem + quarter * 2 * kTileN;
+            {
+                const float4 *src = reinterpret_cast<const float4 *>(a.row_norms + row0) + lane * 2;
+                const float4 x0 = __ldg(src), x1 = __ldg(src + 1);
+                reinterpret_cast<float4 *>(nbuf)[lane * 2] = x0;
+                reinterpret_cast<float4 *>(nbuf)[lane * 2 + 1] = x1;
+                __syncwarp();
+            }
             for (int t = 0; t < tiles; ++t) {
                 const uint32_t b = acc_count & 1;
+                const uint32_t tile_row = static_cast<uint32_t>(row0 + static_cast<int64_t>(t) * kTileN);
+                float4 pre0 = make_float4(0.f, 0.f, 0.f, 0.f), pre1 = pre0;
+                if (t + 1 < tiles) {
+                    const float4 *src = reinterpret_cast<const float4 *>(a.row_norms + tile_row + kTileN) + lane * 2;
+                    pre0 = __ldg(src);
+                    pre1 = __ldg(src + 1);
+                }
                 // every lane polls; the outcome is made warp-uniform before the
                 // .sync.aligned TMEM loads
                 const bool ready = tc::mbar_wait(&acc_full[b], (acc_count >> 1) & 1, kWaitLimitNs);
@@ -243,48 +272,68 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     break;
                 }
                 tc::tc_fence_after();
-                const int64_t tile_row = row0 + static_cast<int64_t>(t) * kTileN;
-                const int64_t left = seg_end - tile_row;
-                const int valid = left < kTileN ? static_cast<int>(left) : kTileN;
-#pragma unroll 1
-                for (int c = 0; c < kTileN / 32; ++c) {
-                    float v[32];
-                    __syncwarp();
-                    tc::tmem_ld32(tmem + lane_addr + b * kTileN + c * 32, v);
-                    const int64_t base = tile_row + c * 32;
-                    const float4 *nrm4 = reinterpret_cast<const float4 *>(a.row_norms + base);
-                    const int lim = valid - c * 32;  // columns >= lim belong to the next segment
+                // Segments start on tile boundaries and rows past n carry +inf
+                // norms, so every column of the tile can be filtered as is.
+                const float *cur_norms = nbuf + (t & 1) * kTileN;
+                const uint32_t tcol = tmem + lane_addr + b * kTileN;
+                float v[2][16];
+                __syncwarp();
+                tc::tmem_ld16(tcol, v[0]);
+#pragma unroll 2
+                for (int c = 0; c < kTileN / 16; ++c) {
+                    const int cur = c & 1;
+                    if (c + 1 < kTileN / 16) {
+                        __syncwarp();
+                        tc::tmem_ld16_nowait(tcol + (c + 1) * 16, v[cur ^ 1]);
+                    }
+                    // branch-free filter against the threshold at chunk start
+                    float dd[16];
+                    uint32_t mask = 0;
+                    const float thr = top.dist[kItemKeep - 1];
 #pragma unroll
-                    for (int e4 = 0; e4 < 8; ++e4) {
-                        const float4 nn = __ldg(nrm4 + e4);
+                    for (int e4 = 0; e4 < 4; ++e4) {
+                        const float4 nn = reinterpret_cast<const float4 *>(cur_norms + c * 16)[e4];
                         const float nv[4] = {nn.x, nn.y, nn.z, nn.w};
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
                             const int e = e4 * 4 + u;
-                            const float dd = fmaf(a.coef, v[e], e < lim ? nv[u] : inf);
-                            if (dd < thr) {
-                                top.insert(make_key(dd, static_cast<uint32_t>(base + e)));
-                                thr = key_dist(top.k[kItemKeep - 1]);
-                                if (top.k[kItemKeep - 1] == kEmptyKey) thr = inf;
-                            }
+                            dd[e] = fmaf(a.coef, v[cur][e], nv[u]);
+                            mask |= (dd[e] < thr ? 1u : 0u) << e;
                         }
                     }
+                    // rare: insert the survivors (re-checked, the threshold drops)
+                    while (mask) {
+                        const int e = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        float x = dd[0];
+#pragma unroll
+                        for (int i = 1; i < 16; ++i) x = e == i ? dd[i] : x;
+                        if (x < top.dist[kItemKeep - 1]) top.insert(x, tile_row + c * 16 + e);
+                    }
+                    if (c + 1 < kTileN / 16) tc::tmem_wait_ld(v[cur ^ 1]);
                 }
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
                 ++acc_count;
+                if (t + 1 < tiles) {
+                    float4 *dst = reinterpret_cast<float4 *>(nbuf + ((t + 1) & 1) * kTileN);
+                    dst[lane * 2] = pre0;
+                    dst[lane * 2 + 1] = pre1;
+                    __syncwarp();
+                }
             }
             if (aborted) break;
             int cnt = 0;
 #pragma unroll
-            for (int i = 0; i < kItemKeep; ++i) cnt += top.k[i] != kEmptyKey;
+            for (int i = 0; i < kItemKeep; ++i) cnt += top.dist[i] < inf;
             const size_t o = static_cast<size_t>(item) * kTileM + r;
 #pragma unroll
             for (int i = 0; i < kItemKeep; ++i)
-                if (i < cnt) a.out_keys[(static_cast<size_t>(item) * kItemKeep + i) * kTileM + r] = top.k[i];
+                if (i < cnt)
+                    a.out_keys[(static_cast<size_t>(item) * kItemKeep + i) * kTileM + r] = make_key(top.dist[i], top.row[i]);
             a.out_count[o] = cnt;
-            a.out_thr[o] = cnt == kItemKeep ? thr : inf;
+            a.out_thr[o] = cnt == kItemKeep ? top.dist[kItemKeep - 1] : inf;
         }
     }
     tc::tc_fence_before();
@@ -643,7 +692,9 @@ Plan make_plan(size_t frames, int64_t n, int sms) {
         const int64_t seg = (ntiles + tps - 1) / tps;
         if (seg * p.n_qtiles > cap) break;
         const int64_t waves = (seg * p.n_qtiles + sms - 1) / sms;
-        const double cost = static_cast<double>(waves * tps) + 0.02 * static_cast<double>(seg);
+        // each item restarts its per-frame top list (a burst of insertions
+        // worth ~2 tiles of epilogue work) and adds keys to the merge
+        const double cost = static_cast<double>(waves * (tps + 2)) + 0.02 * static_cast<double>(seg);
         if (cost < best - 1e-9) {
             best = cost;
             p.segments = static_cast<int>(seg);

@@ -13,7 +13,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/vfr_retrieval.h"
+#include "vfr_retrieval.h"  // include/, on the compiler search path
 #include "kernels.h"
 
 namespace vfr {
