@@ -159,6 +159,21 @@ VFR_API int vfr_retrieval_blend_from(VfrIndex *index, const float *queries, floa
  * length bytes including NUL.  Synchronises the index's device. */
 VFR_API size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t length);
 
+/* In-place blend that allocates no device memory, for callers that must not
+ * call cudaMalloc during a call: a realtime audio callback (cudaMalloc and
+ * cudaFree can synchronise the device and take driver locks, an unbounded
+ * stall inside a hard deadline) or a host whose device memory budget is fixed
+ * up front.  No counterpart in the reference: it is an addition of this
+ * library.  Same arguments, checks and results as vocal_faiss_gpu_blend, for
+ * an index with the tensor-core layout (flat, engine auto or tensor), at most
+ * 256 frames per call and feature width up to 1024.  Its working memory is a
+ * 5.4 MiB static device array that every GPU loading the library holds until
+ * exit; the first call on a device looks up that array's address, so make it
+ * before any stream capture.  All calls share the array: calls whose kernels
+ * overlap on the GPU race and must be serialised by the caller. */
+VFR_API int vfr_retrieval_blend_noalloc(VfrIndex *index, float *features, size_t frames, int32_t width,
+                                        const float *index_rate, VfrStream *stream, char **error);
+
 /* Per-kernel timing with CUDA events recorded on the call's stream around
  * every kernel the index launches (eager calls only; not during capture).
  * enable = 1 clears and starts recording, enable = 0 stops.  Writes JSON

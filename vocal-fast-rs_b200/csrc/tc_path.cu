@@ -938,4 +938,191 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ix->prof.end(stream);
 }
 
+// ---------------------------------------------------------------- no-allocation blend
+//
+// vfr_retrieval_blend_noalloc: the tensor-core blend of vocal_faiss_gpu_blend
+// for callers that must not allocate device memory during a call -- for
+// example a realtime audio callback, where cudaMalloc/cudaFree can
+// synchronise the device and take driver locks (an unbounded stall inside a
+// hard deadline), or a host whose device memory budget is fixed up front.
+// Its working memory is the file-scope array below, sized for at most
+// kNoAllocMaxFrames frames of width <= kNoAllocMaxWidth (5.4 MiB, held by
+// every GPU that loads the library until the process exits).  The array's
+// device address is looked up once per device (cudaGetSymbolAddress) on the
+// first call made on that device, so that first call should come before any
+// stream capture.  All calls share the array and it keeps the last call's
+// contents (each call overwrites what it reads and clears its fallback
+// counter), so calls whose kernels overlap on the GPU -- on different streams,
+// or on several indexes of one device -- race and must be serialised by the
+// caller.
+namespace {
+
+constexpr size_t kNoAllocMaxFrames = 256;
+constexpr int kNoAllocMaxWidth = 1024;  // d_pad limit: covers RVC v1 (256) and v2 (768)
+constexpr int kNoAllocMaxItems = 296;   // two frame tiles x 148 database segments
+constexpr size_t kNoAllocQ16 = 0;
+constexpr size_t kNoAllocQStats = kNoAllocQ16 + kNoAllocMaxFrames * kNoAllocMaxWidth * sizeof(__half);
+constexpr size_t kNoAllocKeys = kNoAllocQStats + kNoAllocMaxFrames * sizeof(float4);
+constexpr size_t kNoAllocCounts =
+    kNoAllocKeys + static_cast<size_t>(kNoAllocMaxItems) * kItemKeep * kTileM * sizeof(unsigned long long);
+constexpr size_t kNoAllocThr = kNoAllocCounts + static_cast<size_t>(kNoAllocMaxItems) * kTileM * sizeof(int);
+constexpr size_t kNoAllocList = kNoAllocThr + static_cast<size_t>(kNoAllocMaxItems) * kTileM * sizeof(float);
+constexpr size_t kNoAllocCount = kNoAllocList + kNoAllocMaxFrames * sizeof(int32_t);
+constexpr size_t kNoAllocBytes = kNoAllocCount + 256;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::once_flag g_noalloc_once[kNoAllocMaxDevices];
+void *g_noalloc_addr[kNoAllocMaxDevices];
+cudaError_t g_noalloc_status[kNoAllocMaxDevices];
+
+// Host-side address of the scratch array on `device` (which is current).
+void *noalloc_scratch(int device) {
+    require(device >= 0 && device < kNoAllocMaxDevices, "device ordinal out of range for the no-allocation path");
+    std::call_once(g_noalloc_once[device], [device] {
+        g_noalloc_status[device] = cudaGetSymbolAddress(&g_noalloc_addr[device], g_noalloc_scratch);
+    });
+    cuda_check(g_noalloc_status[device], "cudaGetSymbolAddress(no-allocation scratch)");
+    return g_noalloc_addr[device];
+}
+
+// make_plan restricted to kNoAllocMaxItems work items.
+Plan make_plan_noalloc(size_t frames, int64_t n, int sms) {
+    Plan p{};
+    p.n_qtiles = static_cast<int>((frames + kTileM - 1) / kTileM);
+    const int64_t ntiles = (n + kTileN - 1) / kTileN;
+    double best = 1e300;
+    p.segments = 0;
+    for (int64_t s = 1; s <= std::min<int64_t>(kMaxSegments, ntiles); ++s) {
+        const int64_t tps = (ntiles + s - 1) / s;
+        const int64_t seg = (ntiles + tps - 1) / tps;
+        if (seg * p.n_qtiles > kNoAllocMaxItems) break;
+        const int64_t waves = (seg * p.n_qtiles + sms - 1) / sms;
+        const double cost = static_cast<double>(waves * (tps + 2)) + 0.02 * static_cast<double>(seg);
+        if (cost < best - 1e-9) {
+            best = cost;
+            p.segments = static_cast<int>(seg);
+            p.tiles_per_seg = static_cast<int>(tps);
+        }
+    }
+    return p;
+}
+
+}  // namespace
+
+void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t frames, cudaStream_t stream) {
+    uint8_t *ws = static_cast<uint8_t *>(noalloc_scratch(ix->device));
+    __half *q16 = reinterpret_cast<__half *>(ws + kNoAllocQ16);
+    float4 *qstats = reinterpret_cast<float4 *>(ws + kNoAllocQStats);
+    auto *keys = reinterpret_cast<unsigned long long *>(ws + kNoAllocKeys);
+    int *counts = reinterpret_cast<int *>(ws + kNoAllocCounts);
+    float *thr = reinterpret_cast<float *>(ws + kNoAllocThr);
+    int32_t *flist = reinterpret_cast<int32_t *>(ws + kNoAllocList);
+    int32_t *fcount = reinterpret_cast<int32_t *>(ws + kNoAllocCount);
+
+    const Plan p = make_plan_noalloc(frames, ix->n, ix->sm_count);
+    require(p.segments > 0, "no-allocation scratch cannot hold this plan");
+    const long long lanes = static_cast<long long>(frames) * 32;
+    prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
+        features, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale);
+    cuda_check(cudaGetLastError());
+    cuda_check(cudaMemsetAsync(fcount, 0, sizeof(int32_t), stream));
+
+    CUtensorMap tmap_q;
+    encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
+    CandArgs ca{};
+    ca.n_qtiles = p.n_qtiles;
+    ca.segments = p.segments;
+    ca.tiles_per_seg = p.tiles_per_seg;
+    ca.ksteps = ix->d_pad / kTileK;
+    ca.n = ix->n;
+    ca.seg_rows = static_cast<int64_t>(p.tiles_per_seg) * kTileN;
+    ca.row_norms = ix->row_norms;
+    ca.coef = -2.0f / (ix->tc_scale * ix->tc_scale);
+    ca.out_keys = keys;
+    ca.out_count = counts;
+    ca.out_thr = thr;
+    ca.counters = ix->counters;
+    const int items = p.segments * p.n_qtiles;
+    cand_kernel<<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    cuda_check(cudaGetLastError());
+
+    MergeArgs ma{};
+    ma.d = ix->d;
+    ma.n_qtiles = p.n_qtiles;
+    ma.segments = p.segments;
+    int sort = 32;
+    while (sort < p.segments * kItemKeep) sort <<= 1;
+    ma.sort_size = sort;
+    ma.keys = keys;
+    ma.counts = counts;
+    ma.thr = thr;
+    ma.qstats = qstats;
+    ma.queries = features;
+    ma.out = features;
+    ma.index_rate = rate;
+    ma.mode = kModeBlend;
+    ma.k = 8;
+    ma.label_base = ix->label_base;
+    ma.vectors = ix->vectors;
+    ma.ids = ix->ids;
+    ma.max_norm = ix->max_row_norm;
+    ma.max_hat = ix->max_row_hat;
+    ma.max_residual = ix->max_row_residual;
+    ma.acc_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -22);
+    ma.norm_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -23);
+    ma.exact_rel = static_cast<float>(ix->d / 8 + 9) * std::ldexp(1.0f, -24);
+    ma.fallback_list = flist;
+    ma.fallback_count = fcount;
+    ma.counters = ix->counters;
+    const size_t msmem = static_cast<size_t>(sort) * 8 + static_cast<size_t>(ix->d) * 4;
+    merge_kernel<<<static_cast<unsigned>(frames), kMergeThreads, msmem, stream>>>(ma);
+    cuda_check(cudaGetLastError());
+
+    ExactArgs ea{};
+    ea.d = ix->d;
+    ea.nlist = ix->nlist;
+    ea.nprobe = ix->nprobe;
+    ea.centroids = ix->centroids;
+    ea.offsets = ix->offsets;
+    ea.vectors = ix->vectors;
+    ea.ids = ix->ids;
+    ea.queries = features;
+    ea.out = features;
+    ea.index_rate = rate;
+    ea.mode = kModeBlend;
+    ea.k = 8;
+    ea.label_base = ix->label_base;
+    ea.counters = ix->counters;
+    ea.frame_list = flist;
+    ea.frame_count = fcount;
+    launch_exact(ea, static_cast<long long>(frames), stream);
+    cuda_check(cudaGetLastError());
+}
+
 }  // namespace vfr
+
+extern "C" int vfr_retrieval_blend_noalloc(VfrIndex *index, float *features, size_t frames, int32_t width,
+                                           const float *index_rate, VfrStream *stream, char **error) {
+    return vfr::guarded(error, [&] {
+        vfr::require(index && features && frames > 0 && index_rate, "invalid FAISS GPU blend arguments");
+        vfr::require(width == index->d, "FAISS feature width mismatch");
+        vfr::require(stream && stream->stream, "invalid FAISS CUDA stream");
+        vfr::require(index->have_tc,
+                     "no-allocation blend needs the tensor-core layout (flat index, tensor or auto engine)");
+        vfr::require(frames <= vfr::kNoAllocMaxFrames,
+                     "no-allocation blend takes at most 256 frames per call");
+        vfr::require(index->d_pad <= vfr::kNoAllocMaxWidth, "no-allocation blend takes feature widths up to 1024");
+        int previous = 0;
+        vfr::cuda_check(cudaGetDevice(&previous));
+        if (previous != index->device) vfr::cuda_check(cudaSetDevice(index->device));
+        try {
+            vfr::run_tc_noalloc(index, features, index_rate, frames, static_cast<cudaStream_t>(stream->stream));
+        } catch (...) {
+            if (previous != index->device) cudaSetDevice(previous);
+            throw;
+        }
+        if (previous != index->device) vfr::cuda_check(cudaSetDevice(previous));
+    });
+}

@@ -13,4 +13,8 @@ bool use_tc(const VfrIndex *ix, size_t frames);
 void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, int mode, int k, float *dist_out,
             int64_t *label_out, size_t frames, cudaStream_t stream);
 
+// In-place tensor-core blend using the library's static scratch array
+// instead of the index workspace (vfr_retrieval_blend_noalloc).
+void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t frames, cudaStream_t stream);
+
 }  // namespace vfr

@@ -81,6 +81,7 @@ def load_library(path: str | None = None):
         "vfr_retrieval_search": ([vp, vp, sz, i32, i32, vp, vp, P(Stream), err], ctypes.c_int),
         "vfr_retrieval_blend_from": ([vp, vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
         "vfr_retrieval_diagnostics": ([vp, ctypes.c_char_p, sz], sz),
+        "vfr_retrieval_blend_noalloc": ([vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
         "vfr_retrieval_profile": ([vp, i32, ctypes.c_char_p, sz], sz),
         "vfr_merge_topk": ([vp, vp, i32, sz, vp, vp, P(Stream), err], ctypes.c_int),
         "vfr_gather_owned": ([vp, vp, sz, vp, P(Stream), err], ctypes.c_int),
