@@ -338,14 +338,13 @@ def main():
     cand_s = cand["ms"] / max(1, cand["launches"]) / 1000.0
     achieved = flops_per_launch / cand_s / 1e12 if cand["launches"] else None
     peak = peaks.get("bf16_tflops_sustained", 1400.0)
-    traffic = None
+    traffic = None  # DRAM bytes of one full-size launch, when profiles/traffic.json has a capture of it
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            tj = json.load(f)
-        per_row = tj.get(f"cand_kernel/{a.workload}", {}).get("dram_bytes_per_frame_row")
-        if per_row:
-            traffic = per_row * q * n_local
+            tj = json.load(f).get(f"cand_kernel/{a.workload}", {})
+        if tj.get("captured_rows") == n_local and tj.get("captured_frames") == q:
+            traffic = tj["dram_bytes_read"] + tj["dram_bytes_write"]
     roofline = {"bound": "tensor", "kernel": "cand_kernel", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak if achieved else None, "traffic": traffic,
                 "peak_source": f"{peak_kind} bf16_tflops_sustained (dense fp16 and bf16 share the rate)",
