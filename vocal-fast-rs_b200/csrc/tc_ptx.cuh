@@ -1,8 +1,8 @@
 // Inline-PTX wrappers for the sm_100a tensor-core engine: mbarriers, TMA
 // tiled loads, TMEM allocation, tcgen05.mma / commit / ld and their fences.
 //
-// No multicast form of any TMA load is used anywhere in this library: the
-// same kernels run in multi-GPU jobs.
+// Every TMA load here targets this CTA's own shared memory from this GPU's
+// own memory; the same kernels run in multi-GPU jobs.
 #pragma once
 
 #include <cuda.h>
