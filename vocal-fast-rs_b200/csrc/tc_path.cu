@@ -38,7 +38,8 @@ constexpr int kTileN = 256;  // rows per MMA / accumulator
 constexpr int kTileK = 64;   // fp16 elements per 128-byte swizzled row
 constexpr int kStages = 4;
 constexpr int kItemKeep = 16;  // candidates kept per frame per work item (registers)
-constexpr int kRerank = 64;    // candidates re-ranked exactly per frame
+constexpr int kRerank = 64;     // candidates re-ranked exactly per frame (more on distance ties)
+constexpr int kRerankMax = 128;
 constexpr int kMaxSegments = 256;
 constexpr int kThreadsTC = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t kABytes = kTileM * kTileK * 2;
@@ -421,6 +422,10 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
     __shared__ float red_f[8];
     __shared__ int red_i[8];
     __shared__ int certified_s;
+    __shared__ unsigned int hist[256];
+    __shared__ uint32_t sel_prefix, sel_rank;
+    __shared__ int sel_count;
+    __shared__ unsigned long long sel_keys[kRerankMax];
     __shared__ double weights[8];
     __shared__ double weight_sum;
 
@@ -475,25 +480,74 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
         tmin = fminf(tmin, red_f[w]);
         total += red_i[w];
     }
-    // bitonic sort of the candidate keys (ascending)
-    for (int kk = 2; kk <= a.sort_size; kk <<= 1) {
-        for (int jj = kk >> 1; jj > 0; jj >>= 1) {
+    // Choose the keys to re-rank without sorting them: radix-select (4 passes
+    // of 8 bits over the distance bits) the kRerank-th smallest distance V,
+    // then keep every key whose distance bits are <= V.  Every dropped key has
+    // a larger approximate distance, so V's distance bounds them for the
+    // certificate.  Ties at V can push the set past kRerank; up to
+    // kRerankMax are re-ranked, beyond that the frame goes to the exact path.
+    if (tid == 0) {
+        sel_prefix = 0u;
+        sel_rank = kRerank;
+        sel_count = 0;
+    }
+    __syncthreads();
+    uint32_t vbits = 0xffffffffu;  // all keys when nothing needs dropping
+    if (total > kRerank) {
+        uint32_t mask_bits = 0;
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            hist[tid] = 0;
+            __syncthreads();
+            const uint32_t prefix = sel_prefix;
             for (int i = tid; i < a.sort_size; i += kMergeThreads) {
-                const int ixj = i ^ jj;
-                if (ixj > i) {
-                    const unsigned long long x = keys[i], y = keys[ixj];
-                    const bool asc = (i & kk) == 0;
-                    if ((x > y) == asc) {
-                        keys[i] = y;
-                        keys[ixj] = x;
+                const unsigned long long key = keys[i];
+                const uint32_t bits = static_cast<uint32_t>(key >> 32);
+                if (key != kEmptyKey && (bits & mask_bits) == prefix) atomicAdd(&hist[(bits >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            if (warp == 0) {
+                uint32_t c[8], sum = 0;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    c[k] = hist[lane * 8 + k];
+                    sum += c[k];
+                }
+                uint32_t incl = sum;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const uint32_t up = __shfl_up_sync(kFullMask, incl, off);
+                    if (lane >= off) incl += up;
+                }
+                const uint32_t want = sel_rank;
+                uint32_t acc = incl - sum;
+                if (acc < want && want <= incl) {
+                    for (int k = 0; k < 8; ++k) {
+                        if (acc + c[k] >= want) {
+                            sel_rank = want - acc;
+                            sel_prefix = prefix | (static_cast<uint32_t>(lane * 8 + k) << shift);
+                            break;
+                        }
+                        acc += c[k];
                     }
                 }
             }
+            mask_bits |= 0xffu << shift;
             __syncthreads();
         }
+        vbits = sel_prefix;
     }
-    const int m = total < kRerank ? total : kRerank;
-    const float t_final = fminf(tmin, total > kRerank ? key_dist(keys[kRerank]) : inf);
+    for (int i = tid; i < a.sort_size; i += kMergeThreads) {
+        const unsigned long long key = keys[i];
+        if (key != kEmptyKey && static_cast<uint32_t>(key >> 32) <= vbits) {
+            const int pos = atomicAdd(&sel_count, 1);
+            if (pos < kRerankMax) sel_keys[pos] = key;
+        }
+    }
+    __syncthreads();
+    const int selected = sel_count;
+    const int m = selected < kRerankMax ? selected : kRerankMax;
+    const bool too_many_ties = selected > kRerankMax;
+    const float t_final = fminf(tmin, selected < total ? from_total_order_bits(vbits) : inf);
 
     // exact re-rank in the reference order; flat scan position == row
     Top8 top;
@@ -501,7 +555,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
     for (int c0 = 0; c0 < m; c0 += 32) {
         const int c = c0 + octet;
         const bool valid = c < m;
-        const uint32_t row = key_pos(keys[valid ? c : 0]);
+        const uint32_t row = key_pos(sel_keys[valid ? c : 0]);
         const float dist = octet_l2(q, a.vectors + static_cast<size_t>(row) * d, d, j, lane & ~7, kFullMask);
         if (valid && dist < inf) top.insert(make_key(dist, row));
     }
@@ -532,6 +586,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
                 const float lower = t_final + st.x - e;
                 ok = lower > d8 * (1.f + 4.f * a.exact_rel) + 1e-30f;
             }
+            if (too_many_ties) ok = false;
             certified_s = ok ? count + 1 : 0;  // 0 = not certified, else count + 1
         }
     }
