@@ -71,7 +71,7 @@ __device__ __forceinline__ float octet_l2(const float *__restrict__ q, const flo
     float acc = 0.0f;  // _mm256_setzero_ps
     // unrolled so several independent row loads are in flight; the
     // accumulation order per lane is unchanged
-#pragma unroll 8
+#pragma unroll 16
     for (int i = j; i < d8; i += 8) {
         float t = __fsub_rn(q[i], __ldg(x + i));
         acc = __fadd_rn(acc, __fmul_rn(t, t));

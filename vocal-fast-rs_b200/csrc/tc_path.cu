@@ -41,17 +41,20 @@ constexpr int kItemKeep = 16;  // candidates kept per frame per work item (regis
 constexpr int kRerank = 64;     // candidates re-ranked exactly per frame (more on distance ties)
 constexpr int kRerankMax = 128;
 constexpr int kMaxSegments = 256;
-constexpr int kThreadsTC = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kEpiWarps = 8;     // two per TMEM lane quarter, each on half of a tile's columns
+constexpr int kHalves = 2;       // candidate lists per (work item, frame)
+constexpr int kThreadsTC = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr uint32_t kABytes = kTileM * kTileK * 2;
 constexpr uint32_t kBBytes = kTileN * kTileK * 2;
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kNormBytes = 4 * 2 * kTileN * sizeof(float);  // per epilogue warp, double buffered
+constexpr uint32_t kNormBytes = kEpiWarps * 2 * (kTileN / kHalves) * sizeof(float);  // per warp, double buffered
 constexpr size_t kSmemTC = 1024 + kStages * kStageBytes + kNormBytes + 256;
 constexpr uint32_t kTmemCols = 512;  // two 128 x 256 fp32 accumulators
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kFormatF16 = 0;
 
 struct CandArgs {
+    int frames;  // rows of the query matrix (padding rows past it are skipped)
     int n_qtiles;
     int segments;
     int tiles_per_seg;
@@ -60,9 +63,9 @@ struct CandArgs {
     int64_t seg_rows;
     const float *row_norms;
     float coef;  // -2 / s^2
-    unsigned long long *out_keys;  // [item][kItemKeep][128]
-    int *out_count;                // [item][128]
-    float *out_thr;                // [item][128]
+    unsigned long long *out_keys;  // [list][kItemKeep][128], list = (seg * kHalves + half) * n_qtiles + qtile
+    int *out_count;                // [list][128]
+    float *out_thr;                // [list][128]
     DeviceCounters *counters;
 };
 
@@ -79,6 +82,56 @@ struct TopList {
         for (int i = 0; i < kItemKeep; ++i) {
             dist[i] = __int_as_float(0x7f800000);
             row[i] = 0;
+        }
+    }
+    // Replaces the list with the kItemKeep smallest of (list U chunk): sorts
+    // the 16 chunk values with a bitonic network, takes the elementwise
+    // minimum against the list reversed (a bitonic sequence holding the 16
+    // smallest of both), and cleans it.  Cheaper than one insertion per value
+    // once more than a few values of the chunk pass the threshold.
+    __device__ __forceinline__ void merge16(float (&cd)[16], uint32_t (&cr)[16]) {
+        static_assert(kItemKeep == 16, "merge16 keeps 16");
+#pragma unroll
+        for (int k = 2; k <= 16; k <<= 1) {
+#pragma unroll
+            for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int l = i ^ j;
+                    if (l > i) {
+                        const bool asc = (i & k) == 0;
+                        const bool swap = asc ? (cd[l] < cd[i]) : (cd[i] < cd[l]);
+                        const float a0 = cd[i], a1 = cd[l];
+                        const uint32_t b0 = cr[i], b1 = cr[l];
+                        cd[i] = swap ? a1 : a0;
+                        cd[l] = swap ? a0 : a1;
+                        cr[i] = swap ? b1 : b0;
+                        cr[l] = swap ? b0 : b1;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const bool take = cd[15 - i] < dist[i];
+            dist[i] = take ? cd[15 - i] : dist[i];
+            row[i] = take ? cr[15 - i] : row[i];
+        }
+#pragma unroll
+        for (int j = 8; j > 0; j >>= 1) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const bool swap = dist[l] < dist[i];
+                    const float a0 = dist[i], a1 = dist[l];
+                    const uint32_t b0 = row[i], b1 = row[l];
+                    dist[i] = swap ? a1 : a0;
+                    dist[l] = swap ? a0 : a1;
+                    row[i] = swap ? b1 : b0;
+                    row[l] = swap ? b0 : b1;
+                }
+            }
         }
     }
     __device__ __forceinline__ void insert(float dd, uint32_t r) {
@@ -121,7 +174,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&acc_full[b], 1);
-            tc::mbar_init(&acc_empty[b], 4);
+            tc::mbar_init(&acc_empty[b], kEpiWarps);
         }
         *abort_flag = 0;
         tc::fence_mbarrier_init();
@@ -230,14 +283,19 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             }
         }
     } else {
-        // ---------------- epilogue: one thread per frame of the tile
+        // ---------------- epilogue: one thread per frame of the tile; the two
+        // warps of a TMEM lane quarter split each tile's columns in halves
+        const int ew = warp - 2;
         const int quarter = warp & 3;  // TMEM lanes this warp may access
+        const int half = ew >> 2;
+        constexpr int kHalfCols = kTileN / kHalves;
         const int r = quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         uint32_t acc_count = 0;
         const float inf = __int_as_float(0x7f800000);
         for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
             const int seg = item / a.n_qtiles;
+            const int qtile_row = (item % a.n_qtiles) * kTileM;
             const int64_t row0 = seg * a.seg_rows;
             const int64_t seg_end = min(row0 + a.seg_rows, a.n);
             const int tiles = static_cast<int>((seg_end - row0 + kTileN - 1) / kTileN);
@@ -247,23 +305,19 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             // This warp's copy of the row norms, one tile ahead: lane l holds
             // norms [8l, 8l+8) of the next tile in registers until the current
             // tile is done, then stores them into the other buffer.
-            float *nbuf = norm_smem + quarter * 2 * kTileN;
+            float *nbuf = norm_smem + ew * 2 * kHalfCols;
             {
-                const float4 *src = reinterpret_cast<const float4 *>(a.row_norms + row0) + lane * 2;
-                const float4 x0 = __ldg(src), x1 = __ldg(src + 1);
-                reinterpret_cast<float4 *>(nbuf)[lane * 2] = x0;
-                reinterpret_cast<float4 *>(nbuf)[lane * 2 + 1] = x1;
+                const float4 x0 = __ldg(reinterpret_cast<const float4 *>(a.row_norms + row0 + half * kHalfCols) + lane);
+                reinterpret_cast<float4 *>(nbuf)[lane] = x0;
                 __syncwarp();
             }
             for (int t = 0; t < tiles; ++t) {
                 const uint32_t b = acc_count & 1;
                 const uint32_t tile_row = static_cast<uint32_t>(row0 + static_cast<int64_t>(t) * kTileN);
-                float4 pre0 = make_float4(0.f, 0.f, 0.f, 0.f), pre1 = pre0;
-                if (t + 1 < tiles) {
-                    const float4 *src = reinterpret_cast<const float4 *>(a.row_norms + tile_row + kTileN) + lane * 2;
-                    pre0 = __ldg(src);
-                    pre1 = __ldg(src + 1);
-                }
+                float4 pre0 = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (t + 1 < tiles)
+                    pre0 = __ldg(reinterpret_cast<const float4 *>(a.row_norms + tile_row + kTileN + half * kHalfCols) +
+                                 lane);
                 // every lane polls; the outcome is made warp-uniform before the
                 // .sync.aligned TMEM loads
                 const bool ready = tc::mbar_wait(&acc_full[b], (acc_count >> 1) & 1, kWaitLimitNs);
@@ -273,17 +327,27 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     break;
                 }
                 tc::tc_fence_after();
+                if (quarter * 32 >= a.frames - qtile_row) {
+                    // every TMEM lane of this warp is a padding row of a partial
+                    // frame tile: release the accumulator without reading it
+                    tc::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
+                    ++acc_count;
+                    continue;
+                }
                 // Segments start on tile boundaries and rows past n carry +inf
                 // norms, so every column of the tile can be filtered as is.
-                const float *cur_norms = nbuf + (t & 1) * kTileN;
-                const uint32_t tcol = tmem + lane_addr + b * kTileN;
+                const float *cur_norms = nbuf + (t & 1) * kHalfCols;
+                const uint32_t tcol = tmem + lane_addr + b * kTileN + half * kHalfCols;
+                const uint32_t col_row = tile_row + half * kHalfCols;
                 float v[2][16];
                 __syncwarp();
                 tc::tmem_ld16(tcol, v[0]);
 #pragma unroll 2
-                for (int c = 0; c < kTileN / 16; ++c) {
+                for (int c = 0; c < kHalfCols / 16; ++c) {
                     const int cur = c & 1;
-                    if (c + 1 < kTileN / 16) {
+                    if (c + 1 < kHalfCols / 16) {
                         __syncwarp();
                         tc::tmem_ld16_nowait(tcol + (c + 1) * 16, v[cur ^ 1]);
                     }
@@ -302,25 +366,32 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                             mask |= (dd[e] < thr ? 1u : 0u) << e;
                         }
                     }
-                    // rare: insert the survivors (re-checked, the threshold drops)
+                    // many survivors (the start of an item): one bulk merge for
+                    // the warp; otherwise insert the few survivors one by one
+                    // (re-checked, the threshold drops as they go in)
+                    if (__reduce_max_sync(kFullMask, static_cast<unsigned>(__popc(mask))) >= 6u) {
+                        uint32_t cr[16];
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) cr[e] = col_row + c * 16 + e;
+                        top.merge16(dd, cr);
+                        mask = 0;
+                    }
                     while (mask) {
                         const int e = __ffs(mask) - 1;
                         mask &= mask - 1;
                         float x = dd[0];
 #pragma unroll
                         for (int i = 1; i < 16; ++i) x = e == i ? dd[i] : x;
-                        if (x < top.dist[kItemKeep - 1]) top.insert(x, tile_row + c * 16 + e);
+                        if (x < top.dist[kItemKeep - 1]) top.insert(x, col_row + c * 16 + e);
                     }
-                    if (c + 1 < kTileN / 16) tc::tmem_wait_ld(v[cur ^ 1]);
+                    if (c + 1 < kHalfCols / 16) tc::tmem_wait_ld(v[cur ^ 1]);
                 }
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
                 ++acc_count;
                 if (t + 1 < tiles) {
-                    float4 *dst = reinterpret_cast<float4 *>(nbuf + ((t + 1) & 1) * kTileN);
-                    dst[lane * 2] = pre0;
-                    dst[lane * 2 + 1] = pre1;
+                    reinterpret_cast<float4 *>(nbuf + ((t + 1) & 1) * kHalfCols)[lane] = pre0;
                     __syncwarp();
                 }
             }
@@ -328,11 +399,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             int cnt = 0;
 #pragma unroll
             for (int i = 0; i < kItemKeep; ++i) cnt += top.dist[i] < inf;
-            const size_t o = static_cast<size_t>(item) * kTileM + r;
+            const size_t list = (static_cast<size_t>(seg) * kHalves + half) * a.n_qtiles + item % a.n_qtiles;
+            const size_t o = list * kTileM + r;
 #pragma unroll
             for (int i = 0; i < kItemKeep; ++i)
-                if (i < cnt)
-                    a.out_keys[(static_cast<size_t>(item) * kItemKeep + i) * kTileM + r] = make_key(top.dist[i], top.row[i]);
+                if (i < cnt) a.out_keys[(list * kItemKeep + i) * kTileM + r] = make_key(top.dist[i], top.row[i]);
             a.out_count[o] = cnt;
             a.out_thr[o] = cnt == kItemKeep ? top.dist[kItemKeep - 1] : inf;
         }
@@ -378,7 +449,7 @@ struct MergeArgs {
     int d;
     int n_qtiles;
     int segments;
-    int sort_size;  // power of two >= segments * kItemKeep
+    int sort_size;  // key slots per frame: segments * kItemKeep rounded up to 32
     const unsigned long long *keys;
     const int *counts;
     const float *thr;
@@ -771,7 +842,7 @@ struct WsLayout {
 WsLayout ws_layout(size_t frames, int d_pad, int sms) {
     WsLayout l{};
     const size_t fr = (frames + kTileM - 1) / kTileM * kTileM;
-    const size_t items = static_cast<size_t>(items_cap(frames, sms));
+    const size_t items = static_cast<size_t>(items_cap(frames, sms)) * kHalves;  // candidate lists
     size_t off = 0;
     l.q16 = off;
     off = align256(off + fr * d_pad * sizeof(__half));
@@ -913,6 +984,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     CUtensorMap tmap_q;
     encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
     CandArgs ca{};
+    ca.frames = static_cast<int>(frames);
     ca.n_qtiles = p.n_qtiles;
     ca.segments = p.segments;
     ca.tiles_per_seg = p.tiles_per_seg;
@@ -935,9 +1007,8 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     MergeArgs ma{};
     ma.d = ix->d;
     ma.n_qtiles = p.n_qtiles;
-    ma.segments = p.segments;
-    int sort = 32;
-    while (sort < p.segments * kItemKeep) sort <<= 1;
+    ma.segments = p.segments * kHalves;  // candidate lists per frame tile
+    const int sort = (ma.segments * kItemKeep + 31) / 32 * 32;  // key slots per frame
     ma.sort_size = sort;
     ma.keys = keys;
     ma.counts = counts;
@@ -1014,14 +1085,14 @@ namespace {
 
 constexpr size_t kNoAllocMaxFrames = 256;
 constexpr int kNoAllocMaxWidth = 1024;  // d_pad limit: covers RVC v1 (256) and v2 (768)
-constexpr int kNoAllocMaxItems = 296;   // two frame tiles x 148 database segments
+constexpr int kNoAllocMaxItems = 148;   // work items; each writes kHalves candidate lists
 constexpr size_t kNoAllocQ16 = 0;
 constexpr size_t kNoAllocQStats = kNoAllocQ16 + kNoAllocMaxFrames * kNoAllocMaxWidth * sizeof(__half);
 constexpr size_t kNoAllocKeys = kNoAllocQStats + kNoAllocMaxFrames * sizeof(float4);
-constexpr size_t kNoAllocCounts =
-    kNoAllocKeys + static_cast<size_t>(kNoAllocMaxItems) * kItemKeep * kTileM * sizeof(unsigned long long);
-constexpr size_t kNoAllocThr = kNoAllocCounts + static_cast<size_t>(kNoAllocMaxItems) * kTileM * sizeof(int);
-constexpr size_t kNoAllocList = kNoAllocThr + static_cast<size_t>(kNoAllocMaxItems) * kTileM * sizeof(float);
+constexpr size_t kNoAllocLists = static_cast<size_t>(kNoAllocMaxItems) * kHalves;
+constexpr size_t kNoAllocCounts = kNoAllocKeys + kNoAllocLists * kItemKeep * kTileM * sizeof(unsigned long long);
+constexpr size_t kNoAllocThr = kNoAllocCounts + kNoAllocLists * kTileM * sizeof(int);
+constexpr size_t kNoAllocList = kNoAllocThr + kNoAllocLists * kTileM * sizeof(float);
 constexpr size_t kNoAllocCount = kNoAllocList + kNoAllocMaxFrames * sizeof(int32_t);
 constexpr size_t kNoAllocBytes = kNoAllocCount + 256;
 
@@ -1087,6 +1158,7 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     CUtensorMap tmap_q;
     encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
     CandArgs ca{};
+    ca.frames = static_cast<int>(frames);
     ca.n_qtiles = p.n_qtiles;
     ca.segments = p.segments;
     ca.tiles_per_seg = p.tiles_per_seg;
@@ -1106,9 +1178,8 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     MergeArgs ma{};
     ma.d = ix->d;
     ma.n_qtiles = p.n_qtiles;
-    ma.segments = p.segments;
-    int sort = 32;
-    while (sort < p.segments * kItemKeep) sort <<= 1;
+    ma.segments = p.segments * kHalves;  // candidate lists per frame tile
+    const int sort = (ma.segments * kItemKeep + 31) / 32 * 32;  // key slots per frame
     ma.sort_size = sort;
     ma.keys = keys;
     ma.counts = counts;
