@@ -262,3 +262,17 @@ def test_row_sharded_blocks_reproduce_single_index(cuda, oracle, engine):
     assert np.array_equal(md.cpu().numpy().view(np.uint32), dist.view(np.uint32))
     expected, status = oracle_index(oracle, ix).blend(q, ratio, threads=THREADS)
     assert_blend_parity(expected, status, out.cpu().numpy(), q)
+
+
+@pytest.mark.parametrize("key", ["c1", "c3-np1", "c3-np8"])
+def test_tensor_core_stage_serves_the_frames(cuda, oracle, key):
+    """The certified tensor-core stage (not the exact re-run) settles the
+    frames of the seeded configs, flat and IVF, and stays bit-exact."""
+    ix, q, ratio = make_scaled(key)
+    g = gpu_index(ix, "tensor")
+    expected, status = oracle_index(oracle, ix).blend(q, ratio, threads=THREADS)
+    assert_blend_parity(expected, status, gpu_blend(cuda, g, q, ratio), q)
+    diag = g.diagnostics()
+    assert diag["tensor_cores"]
+    assert diag["candidate_frames"] >= 0.95 * len(q)
+    assert diag["candidate_frames"] + diag["fallback_frames"] == len(q)

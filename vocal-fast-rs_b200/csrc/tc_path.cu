@@ -67,7 +67,54 @@ struct CandArgs {
     int *out_count;                // [list][128]
     float *out_thr;                // [list][128]
     DeviceCounters *counters;
+    // IVF fine stage only: work items (list, frame tile within the list's
+    // pairs) from a device table; A rows are the (frame, probe) pairs of the
+    // list in list order, B rows the list's rows.
+    const int2 *items;
+    const int *item_count;
+    const int32_t *list_offsets;  // database row offsets [nlist + 1]
+    const int32_t *list_start;    // pair offsets [nlist + 1]
+    int pair_stride;              // output stride: pairs capacity
 };
+
+// One work item: A rows [a_row0, a_row0 + a_rows) against database rows
+// [b_row0, b_end), in `tiles` tiles of kTileN rows.
+struct Item {
+    int a_row0;
+    int a_rows;
+    int64_t b_row0;
+    int64_t b_end;
+    int tiles;
+    int seg;  // flat only
+};
+
+template <bool kIvf>
+__device__ __forceinline__ int item_total(const CandArgs &a) {
+    if constexpr (kIvf) return *a.item_count;
+    else return a.segments * a.n_qtiles;
+}
+
+template <bool kIvf>
+__device__ __forceinline__ Item item_at(const CandArgs &a, int item) {
+    Item it{};
+    if constexpr (kIvf) {
+        const int2 e = a.items[item];
+        it.a_row0 = a.list_start[e.x] + e.y * kTileM;
+        it.a_rows = min(kTileM, a.list_start[e.x + 1] - it.a_row0);
+        it.b_row0 = a.list_offsets[e.x];
+        it.b_end = a.list_offsets[e.x + 1];
+        it.seg = 0;
+    } else {
+        const int qtile = item % a.n_qtiles;
+        it.seg = item / a.n_qtiles;
+        it.a_row0 = qtile * kTileM;
+        it.a_rows = min(kTileM, a.frames - it.a_row0);
+        it.b_row0 = it.seg * a.seg_rows;
+        it.b_end = min(it.b_row0 + a.seg_rows, a.n);
+    }
+    it.tiles = static_cast<int>((it.b_end - it.b_row0 + kTileN - 1) / kTileN);
+    return it;
+}
 
 // Sorted ascending list of the kItemKeep smallest approximate distances seen
 // (with their rows), in registers.  Insertion is a fixed compare-exchange
@@ -150,6 +197,15 @@ struct TopList {
     }
 };
 
+// Four consecutive row norms.  Flat segments start on tile boundaries, so the
+// address is 16-byte aligned; IVF lists start anywhere.
+template <bool kIvf>
+__device__ __forceinline__ float4 load_norms4(const float *p) {
+    if constexpr (kIvf) return make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
+    else return __ldg(reinterpret_cast<const float4 *>(p));
+}
+
+template <bool kIvf>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     cand_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, CandArgs a) {
     extern __shared__ uint8_t smem_raw[];
@@ -165,7 +221,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int items = a.segments * a.n_qtiles;
+    const int items = item_total<kIvf>(a);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -203,12 +259,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             int stage = 0;
             uint32_t phase = 0;
             for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
-                const int qtile = item % a.n_qtiles;
-                const int seg = item / a.n_qtiles;
-                const int64_t row0 = seg * a.seg_rows;
-                const int64_t rows = min(a.seg_rows, a.n - row0);
-                const int tiles = static_cast<int>((rows + kTileN - 1) / kTileN);
-                for (int t = 0; t < tiles && !*abort_flag; ++t) {
+                const Item it = item_at<kIvf>(a, item);
+                for (int t = 0; t < it.tiles && !*abort_flag; ++t) {
                     for (int k = 0; k < a.ksteps; ++k) {
                         if (!tc::mbar_wait(&empty[stage], phase ^ 1, kWaitLimitNs)) {
                             fail();
@@ -216,9 +268,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                         }
                         uint8_t *sa = smem + stage * kStageBytes;
                         tc::mbar_arrive_expect_tx(&full[stage], kStageBytes);
-                        tc::tma_load_2d(sa, &tmap_q, &full[stage], k * kTileK, qtile * kTileM);
+                        tc::tma_load_2d(sa, &tmap_q, &full[stage], k * kTileK, it.a_row0);
                         tc::tma_load_2d(sa + kABytes, &tmap_x, &full[stage], k * kTileK,
-                                        static_cast<int32_t>(row0 + t * kTileN));
+                                        static_cast<int32_t>(it.b_row0 + t * kTileN));
                         if (++stage == kStages) {
                             stage = 0;
                             phase ^= 1;
@@ -243,11 +295,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             uint32_t phase = 0;
             uint32_t acc_count = 0;
             for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
-                const int seg = item / a.n_qtiles;
-                const int64_t row0 = seg * a.seg_rows;
-                const int64_t rows = min(a.seg_rows, a.n - row0);
-                const int tiles = static_cast<int>((rows + kTileN - 1) / kTileN);
-                for (int t = 0; t < tiles && !*abort_flag; ++t) {
+                const Item it = item_at<kIvf>(a, item);
+                for (int t = 0; t < it.tiles && !*abort_flag; ++t) {
                     const uint32_t b = acc_count & 1;
                     if (!tc::mbar_wait(&acc_empty[b], ((acc_count >> 1) & 1) ^ 1, kWaitLimitNs)) {
                         fail();
@@ -294,11 +343,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         uint32_t acc_count = 0;
         const float inf = __int_as_float(0x7f800000);
         for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
-            const int seg = item / a.n_qtiles;
-            const int qtile_row = (item % a.n_qtiles) * kTileM;
-            const int64_t row0 = seg * a.seg_rows;
-            const int64_t seg_end = min(row0 + a.seg_rows, a.n);
-            const int tiles = static_cast<int>((seg_end - row0 + kTileN - 1) / kTileN);
+            const Item it = item_at<kIvf>(a, item);
+            const int64_t row0 = it.b_row0;
+            const int tiles = it.tiles;
             TopList top;
             top.init();
             bool aborted = false;
@@ -307,17 +354,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             // tile is done, then stores them into the other buffer.
             float *nbuf = norm_smem + ew * 2 * kHalfCols;
             {
-                const float4 x0 = __ldg(reinterpret_cast<const float4 *>(a.row_norms + row0 + half * kHalfCols) + lane);
-                reinterpret_cast<float4 *>(nbuf)[lane] = x0;
+                reinterpret_cast<float4 *>(nbuf)[lane] = load_norms4<kIvf>(a.row_norms + row0 + half * kHalfCols + lane * 4);
                 __syncwarp();
             }
             for (int t = 0; t < tiles; ++t) {
                 const uint32_t b = acc_count & 1;
                 const uint32_t tile_row = static_cast<uint32_t>(row0 + static_cast<int64_t>(t) * kTileN);
                 float4 pre0 = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (t + 1 < tiles)
-                    pre0 = __ldg(reinterpret_cast<const float4 *>(a.row_norms + tile_row + kTileN + half * kHalfCols) +
-                                 lane);
+                if (t + 1 < tiles) pre0 = load_norms4<kIvf>(a.row_norms + tile_row + kTileN + half * kHalfCols + lane * 4);
                 // every lane polls; the outcome is made warp-uniform before the
                 // .sync.aligned TMEM loads
                 const bool ready = tc::mbar_wait(&acc_full[b], (acc_count >> 1) & 1, kWaitLimitNs);
@@ -327,7 +371,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     break;
                 }
                 tc::tc_fence_after();
-                if (quarter * 32 >= a.frames - qtile_row) {
+                if (quarter * 32 >= it.a_rows) {
                     // every TMEM lane of this warp is a padding row of a partial
                     // frame tile: release the accumulator without reading it
                     tc::tc_fence_before();
@@ -355,6 +399,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     float dd[16];
                     uint32_t mask = 0;
                     const float thr = top.dist[kItemKeep - 1];
+                    // IVF: rows past the list's end belong to the next list
+                    const int64_t lim = kIvf ? it.b_end - (static_cast<int64_t>(col_row) + c * 16) : 16;
 #pragma unroll
                     for (int e4 = 0; e4 < 4; ++e4) {
                         const float4 nn = reinterpret_cast<const float4 *>(cur_norms + c * 16)[e4];
@@ -363,6 +409,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                         for (int u = 0; u < 4; ++u) {
                             const int e = e4 * 4 + u;
                             dd[e] = fmaf(a.coef, v[cur][e], nv[u]);
+                            if constexpr (kIvf) dd[e] = e < lim ? dd[e] : inf;
                             mask |= (dd[e] < thr ? 1u : 0u) << e;
                         }
                     }
@@ -399,13 +446,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             int cnt = 0;
 #pragma unroll
             for (int i = 0; i < kItemKeep; ++i) cnt += top.dist[i] < inf;
-            const size_t list = (static_cast<size_t>(seg) * kHalves + half) * a.n_qtiles + item % a.n_qtiles;
-            const size_t o = list * kTileM + r;
+            if constexpr (kIvf) {
+                if (r < it.a_rows) {
+                    const size_t pos = static_cast<size_t>(it.a_row0) + r;
+                    const size_t stride = static_cast<size_t>(a.pair_stride);
 #pragma unroll
-            for (int i = 0; i < kItemKeep; ++i)
-                if (i < cnt) a.out_keys[(list * kItemKeep + i) * kTileM + r] = make_key(top.dist[i], top.row[i]);
-            a.out_count[o] = cnt;
-            a.out_thr[o] = cnt == kItemKeep ? top.dist[kItemKeep - 1] : inf;
+                    for (int i = 0; i < kItemKeep; ++i)
+                        if (i < cnt) a.out_keys[(half * kItemKeep + i) * stride + pos] = make_key(top.dist[i], top.row[i]);
+                    a.out_count[half * stride + pos] = cnt;
+                    a.out_thr[half * stride + pos] = cnt == kItemKeep ? top.dist[kItemKeep - 1] : inf;
+                }
+            } else {
+                const size_t list = (static_cast<size_t>(it.seg) * kHalves + half) * a.n_qtiles + item % a.n_qtiles;
+                const size_t o = list * kTileM + r;
+#pragma unroll
+                for (int i = 0; i < kItemKeep; ++i)
+                    if (i < cnt) a.out_keys[(list * kItemKeep + i) * kTileM + r] = make_key(top.dist[i], top.row[i]);
+                a.out_count[o] = cnt;
+                a.out_thr[o] = cnt == kItemKeep ? top.dist[kItemKeep - 1] : inf;
+            }
         }
     }
     tc::tc_fence_before();
@@ -475,13 +534,145 @@ struct MergeArgs {
 
 constexpr int kMergeThreads = 256;
 
-__device__ __forceinline__ unsigned long long warp_min_key(unsigned long long v) {
+
+// Shared state of select_rerank (one per CTA, in shared memory).
+struct SelectState {
+    unsigned int hist[256];
+    uint32_t prefix, rank;
+    int count;
+    float red_f[kMergeThreads / 32];
+    int red_i[kMergeThreads / 32];
+};
+
+// Block-wide min of `tmin` and sum of `total` (all threads get the result).
+__device__ __forceinline__ void block_min_sum(float &tmin, int &total, SelectState &st) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) {
-        unsigned long long o = __shfl_xor_sync(kFullMask, v, s);
-        v = o < v ? o : v;
+        tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, s));
+        total += __shfl_xor_sync(kFullMask, total, s);
     }
-    return v;
+    if (lane == 0) {
+        st.red_f[warp] = tmin;
+        st.red_i[warp] = total;
+    }
+    __syncthreads();
+    tmin = __int_as_float(0x7f800000);
+    total = 0;
+    for (int w = 0; w < kMergeThreads / 32; ++w) {
+        tmin = fminf(tmin, st.red_f[w]);
+        total += st.red_i[w];
+    }
+}
+
+// Chooses the keys to re-rank among keys[0 .. slots) (total real keys, the
+// rest kEmptyKey) without sorting them: radix-select (4 passes of 8 bits over
+// the distance bits) the kRerank-th smallest distance V, then keep every key
+// whose distance bits are <= V.  Every dropped key has a larger approximate
+// distance, so V's distance bounds them for the certificate.  Ties at V can
+// push the set past kRerank; up to kRerankMax are kept and `too_many` reports
+// an overflow.  Returns the number of keys written to sel_keys; `bound` is the
+// distance every dropped key reaches or exceeds (+inf when none is dropped).
+// Called by every thread of the CTA.
+__device__ int select_rerank(const unsigned long long *keys, int slots, int total, unsigned long long *sel_keys,
+                             SelectState &st, float &bound, bool &too_many) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        st.prefix = 0u;
+        st.rank = kRerank;
+        st.count = 0;
+    }
+    __syncthreads();
+    uint32_t vbits = 0xffffffffu;  // all keys when nothing needs dropping
+    if (total > kRerank) {
+        uint32_t mask_bits = 0;
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            st.hist[tid] = 0;
+            __syncthreads();
+            const uint32_t prefix = st.prefix;
+            for (int i = tid; i < slots; i += kMergeThreads) {
+                const unsigned long long key = keys[i];
+                const uint32_t bits = static_cast<uint32_t>(key >> 32);
+                if (key != kEmptyKey && (bits & mask_bits) == prefix) atomicAdd(&st.hist[(bits >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            if (warp == 0) {
+                uint32_t c[8], sum = 0;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    c[k] = st.hist[lane * 8 + k];
+                    sum += c[k];
+                }
+                uint32_t incl = sum;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const uint32_t up = __shfl_up_sync(kFullMask, incl, off);
+                    if (lane >= off) incl += up;
+                }
+                const uint32_t want = st.rank;
+                uint32_t acc = incl - sum;
+                if (acc < want && want <= incl) {
+                    for (int k = 0; k < 8; ++k) {
+                        if (acc + c[k] >= want) {
+                            st.rank = want - acc;
+                            st.prefix = prefix | (static_cast<uint32_t>(lane * 8 + k) << shift);
+                            break;
+                        }
+                        acc += c[k];
+                    }
+                }
+            }
+            mask_bits |= 0xffu << shift;
+            __syncthreads();
+        }
+        vbits = st.prefix;
+    }
+    for (int i = tid; i < slots; i += kMergeThreads) {
+        const unsigned long long key = keys[i];
+        if (key != kEmptyKey && static_cast<uint32_t>(key >> 32) <= vbits) {
+            const int pos = atomicAdd(&st.count, 1);
+            if (pos < kRerankMax) sel_keys[pos] = key;
+        }
+    }
+    __syncthreads();
+    const int selected = st.count;
+    too_many = selected > kRerankMax;
+    bound = selected < total ? from_total_order_bits(vbits) : __int_as_float(0x7f800000);
+    return selected < kRerankMax ? selected : kRerankMax;
+}
+
+// Reduces the octets' sorted top-8 lists (octet_best[32][8]) to the CTA's
+// top-8 keys in best[0..8); warp 0 does the work, then the CTA syncs.
+__device__ __forceinline__ void merge_octet_lists(const unsigned long long *octet_best, unsigned long long *best) {
+    const int lane = threadIdx.x & 31;
+    if ((threadIdx.x >> 5) == 0) {
+        int head = 0;
+        for (int i = 0; i < 8; ++i) {
+            unsigned long long mine = head < 8 ? octet_best[lane * 8 + head] : kEmptyKey;
+            unsigned long long mn = mine;
+#pragma unroll
+            for (int s = 16; s > 0; s >>= 1) {
+                unsigned long long o = __shfl_xor_sync(kFullMask, mn, s);
+                mn = o < mn ? o : mn;
+            }
+            if (mine == mn && mn != kEmptyKey) ++head;
+            if (lane == 0) best[i] = mn;
+        }
+    }
+    __syncthreads();
+}
+
+// The frame's exactness certificate: every dropped candidate has an
+// approximate distance >= bound; qs = (||q||^2, ||q^||, ||q - q^||); the
+// database bounds are max ||x||, max ||x^||, max ||x - x^||.  True when no
+// dropped candidate can reach (or tie) the `rank`-th exact distance dk.
+__device__ __forceinline__ bool certify(float bound, float dk, float4 qs, float max_norm, float max_hat,
+                                        float max_residual, float acc_rel, float norm_rel, float exact_rel) {
+    if (!(bound < __int_as_float(0x7f800000)) && bound == bound) return true;  // nothing was dropped
+    const float e = 2.f * (qs.y * max_residual + qs.z * max_norm) + 2.f * acc_rel * qs.y * max_hat +
+                    norm_rel * (max_norm * max_norm + qs.x) + 6e-8f * (max_norm * max_norm + 2.f * qs.y * max_hat);
+    const float lower = bound + qs.x - e;
+    return lower > dk * (1.f + 4.f * exact_rel) + 1e-30f;
 }
 
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
@@ -490,17 +681,13 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
     float *q = reinterpret_cast<float *>(msm + static_cast<size_t>(a.sort_size) * 8);
     __shared__ unsigned long long octet_best[32 * 8];
     __shared__ unsigned long long best[8];
-    __shared__ float red_f[8];
-    __shared__ int red_i[8];
     __shared__ int certified_s;
-    __shared__ unsigned int hist[256];
-    __shared__ uint32_t sel_prefix, sel_rank;
-    __shared__ int sel_count;
+    __shared__ SelectState sel;
     __shared__ unsigned long long sel_keys[kRerankMax];
     __shared__ double weights[8];
     __shared__ double weight_sum;
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
+    const int tid = threadIdx.x, lane = tid & 31, octet = tid >> 3, j = tid & 7;
     const long long frame = blockIdx.x;
     const int qtile = static_cast<int>(frame / kTileM), r = static_cast<int>(frame % kTileM);
     const int d = a.d;
@@ -535,90 +722,11 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
         }
         keys[i] = key;
     }
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) {
-        tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, s));
-        total += __shfl_xor_sync(kFullMask, total, s);
-    }
-    if (lane == 0) {
-        red_f[warp] = tmin;
-        red_i[warp] = total;
-    }
-    __syncthreads();
-    tmin = inf;
-    total = 0;
-    for (int w = 0; w < kMergeThreads / 32; ++w) {
-        tmin = fminf(tmin, red_f[w]);
-        total += red_i[w];
-    }
-    // Choose the keys to re-rank without sorting them: radix-select (4 passes
-    // of 8 bits over the distance bits) the kRerank-th smallest distance V,
-    // then keep every key whose distance bits are <= V.  Every dropped key has
-    // a larger approximate distance, so V's distance bounds them for the
-    // certificate.  Ties at V can push the set past kRerank; up to
-    // kRerankMax are re-ranked, beyond that the frame goes to the exact path.
-    if (tid == 0) {
-        sel_prefix = 0u;
-        sel_rank = kRerank;
-        sel_count = 0;
-    }
-    __syncthreads();
-    uint32_t vbits = 0xffffffffu;  // all keys when nothing needs dropping
-    if (total > kRerank) {
-        uint32_t mask_bits = 0;
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            hist[tid] = 0;
-            __syncthreads();
-            const uint32_t prefix = sel_prefix;
-            for (int i = tid; i < a.sort_size; i += kMergeThreads) {
-                const unsigned long long key = keys[i];
-                const uint32_t bits = static_cast<uint32_t>(key >> 32);
-                if (key != kEmptyKey && (bits & mask_bits) == prefix) atomicAdd(&hist[(bits >> shift) & 255u], 1u);
-            }
-            __syncthreads();
-            if (warp == 0) {
-                uint32_t c[8], sum = 0;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    c[k] = hist[lane * 8 + k];
-                    sum += c[k];
-                }
-                uint32_t incl = sum;
-#pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                    const uint32_t up = __shfl_up_sync(kFullMask, incl, off);
-                    if (lane >= off) incl += up;
-                }
-                const uint32_t want = sel_rank;
-                uint32_t acc = incl - sum;
-                if (acc < want && want <= incl) {
-                    for (int k = 0; k < 8; ++k) {
-                        if (acc + c[k] >= want) {
-                            sel_rank = want - acc;
-                            sel_prefix = prefix | (static_cast<uint32_t>(lane * 8 + k) << shift);
-                            break;
-                        }
-                        acc += c[k];
-                    }
-                }
-            }
-            mask_bits |= 0xffu << shift;
-            __syncthreads();
-        }
-        vbits = sel_prefix;
-    }
-    for (int i = tid; i < a.sort_size; i += kMergeThreads) {
-        const unsigned long long key = keys[i];
-        if (key != kEmptyKey && static_cast<uint32_t>(key >> 32) <= vbits) {
-            const int pos = atomicAdd(&sel_count, 1);
-            if (pos < kRerankMax) sel_keys[pos] = key;
-        }
-    }
-    __syncthreads();
-    const int selected = sel_count;
-    const int m = selected < kRerankMax ? selected : kRerankMax;
-    const bool too_many_ties = selected > kRerankMax;
-    const float t_final = fminf(tmin, selected < total ? from_total_order_bits(vbits) : inf);
+    block_min_sum(tmin, total, sel);
+    float cut;
+    bool too_many_ties;
+    const int m = select_rerank(keys, a.sort_size, total, sel_keys, sel, cut, too_many_ties);
+    const float t_final = fminf(tmin, cut);
 
     // exact re-rank in the reference order; flat scan position == row
     Top8 top;
@@ -634,32 +742,14 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) octet_best[octet * 8 + i] = top.k[i];
     __syncthreads();
-    if (warp == 0) {
-        int head = 0;
-        for (int i = 0; i < 8; ++i) {
-            unsigned long long mine = head < 8 ? octet_best[lane * 8 + head] : kEmptyKey;
-            unsigned long long mn = warp_min_key(mine);
-            if (mine == mn && mn != kEmptyKey) ++head;
-            if (lane == 0) best[i] = mn;
-        }
-        if (lane == 0) {
-            int count = 0;
-            while (count < 8 && best[count] != kEmptyKey) ++count;
-            bool ok = true;
-            if (t_final < inf || t_final != t_final) {
-                // something was dropped: certify that it cannot reach the top 8
-                const float4 st = a.qstats[frame];
-                const float d8 = count == 8 ? key_dist(best[7]) : inf;
-                const float e = 2.f * (st.y * a.max_residual + st.z * a.max_norm) +
-                                2.f * a.acc_rel * st.y * a.max_hat +
-                                a.norm_rel * (a.max_norm * a.max_norm + st.x) +
-                                6e-8f * (a.max_norm * a.max_norm + 2.f * st.y * a.max_hat);
-                const float lower = t_final + st.x - e;
-                ok = lower > d8 * (1.f + 4.f * a.exact_rel) + 1e-30f;
-            }
-            if (too_many_ties) ok = false;
-            certified_s = ok ? count + 1 : 0;  // 0 = not certified, else count + 1
-        }
+    merge_octet_lists(octet_best, best);
+    if (tid == 0) {
+        int count = 0;
+        while (count < 8 && best[count] != kEmptyKey) ++count;
+        const float d8 = count == 8 ? key_dist(best[7]) : inf;
+        const bool ok = !too_many_ties && certify(t_final, d8, a.qstats[frame], a.max_norm, a.max_hat,
+                                                  a.max_residual, a.acc_rel, a.norm_rel, a.exact_rel);
+        certified_s = ok ? count + 1 : 0;  // 0 = not certified, else count + 1
     }
     __syncthreads();
     const int cert = certified_s;
@@ -862,31 +952,492 @@ WsLayout ws_layout(size_t frames, int d_pad, int sms) {
     return l;
 }
 
+// ================================================================ IVF-Flat
+//
+// Coarse stage: cand_kernel<false> over the fp16 centroid shadow gives each
+// frame candidate lists of centroids; coarse_select_kernel re-ranks them with
+// exact fp32 distances in the reference order, keeps the first nprobe by
+// (distance total order, list id) -- crates/vocal-cpu/src/retrieval.rs:45-51 --
+// and certifies that no dropped centroid could enter them.  Fine stage: the
+// (frame, probe) pairs are bucketed by list, their fp16 frames gathered into
+// list order, cand_kernel<true> scans each list's rows for its pairs, and
+// ivf_merge_kernel re-ranks per frame with the scan position (probe rank,
+// storage row) as the tie order -- :52-64 -- then certifies and blends.
+// Frames left uncertified by either stage are re-run by the exact engine.
+
+constexpr int kIvfMaxProbe = 8;
+
+struct CoarseArgs {
+    int d;
+    int nlist;
+    int nprobe;
+    int n_qtiles;
+    int lists;  // coarse candidate lists per frame tile
+    int slots;  // lists * kItemKeep rounded up to 32
+    const unsigned long long *keys;
+    const int *counts;
+    const float *thr;
+    const float4 *qstats;
+    const float *queries;
+    float *out;
+    const float *index_rate;
+    int mode;
+    const float *centroids;  // fp32 [nlist][d]
+    float max_norm, max_hat, max_residual, acc_rel, norm_rel, exact_rel;  // centroid bounds
+    int32_t *probes;      // [frames][nprobe] list ids, coarse rank order
+    int32_t *probe_ok;    // [frames] 1 when the fine stage handles the frame
+    int32_t *list_count;  // [nlist] pairs per list (atomic)
+    int32_t *fallback_list;
+    int32_t *fallback_count;
+};
+
+__global__ void __launch_bounds__(kMergeThreads) coarse_select_kernel(CoarseArgs a) {
+    extern __shared__ __align__(16) uint8_t csm[];
+    unsigned long long *keys = reinterpret_cast<unsigned long long *>(csm);
+    float *q = reinterpret_cast<float *>(csm + static_cast<size_t>(a.slots) * 8);
+    __shared__ SelectState sel;
+    __shared__ unsigned long long sel_keys[kRerankMax];
+    __shared__ unsigned long long exact_keys[kRerankMax];
+    __shared__ unsigned long long top_keys[kIvfMaxProbe];
+    __shared__ int ok_s;
+    const int tid = threadIdx.x, lane = tid & 31, octet = tid >> 3, j = tid & 7;
+    const long long frame = blockIdx.x;
+    const int qtile = static_cast<int>(frame / kTileM), r = static_cast<int>(frame % kTileM);
+    const int d = a.d, P = a.nprobe;
+    const float *src = a.queries + frame * d;
+    const float inf = __int_as_float(0x7f800000);
+    if (a.mode == kModeBlend && !(load_ratio(a.index_rate) > 0.f)) {
+        // r <= 0: the frame is left as is (copied when out of place)
+        float *dst = a.out + frame * d;
+        if (dst != src)
+            for (int i = tid; i < d; i += kMergeThreads) dst[i] = src[i];
+        if (tid == 0) a.probe_ok[frame] = 0;
+        return;
+    }
+    for (int i = tid; i < d; i += kMergeThreads) q[i] = src[i];
+    float tmin = inf;
+    int total = 0;
+    for (int s = tid; s < a.lists; s += kMergeThreads) {
+        const size_t o = (static_cast<size_t>(s) * a.n_qtiles + qtile) * kTileM + r;
+        tmin = fminf(tmin, a.thr[o]);
+        total += a.counts[o];
+    }
+    for (int i = tid; i < a.slots; i += kMergeThreads) {
+        const int s = i / kItemKeep, slot = i % kItemKeep;
+        unsigned long long key = kEmptyKey;
+        if (s < a.lists) {
+            const size_t item = static_cast<size_t>(s) * a.n_qtiles + qtile;
+            if (slot < a.counts[item * kTileM + r]) key = a.keys[(item * kItemKeep + slot) * kTileM + r];
+        }
+        keys[i] = key;
+    }
+    block_min_sum(tmin, total, sel);
+    float cut;
+    bool too_many;
+    const int m = select_rerank(keys, a.slots, total, sel_keys, sel, cut, too_many);
+    const float bound = fminf(tmin, cut);
+    // exact centroid distances; every centroid takes part, as in the
+    // reference's sort (no +inf filter here)
+    for (int c0 = 0; c0 < m; c0 += 32) {
+        const int c = c0 + octet;
+        const bool valid = c < m;
+        const uint32_t list = key_pos(sel_keys[valid ? c : 0]);
+        const float dist = octet_l2(q, a.centroids + static_cast<size_t>(list) * d, d, j, lane & ~7, kFullMask);
+        if (valid && j == 0) exact_keys[c] = make_key(dist, list);
+    }
+    __syncthreads();
+    // rank selection of the first P keys (keys are distinct: list ids are)
+    for (int c = tid; c < m; c += kMergeThreads) {
+        const unsigned long long kc = exact_keys[c];
+        int rank = 0;
+        for (int i = 0; i < m; ++i) rank += exact_keys[i] < kc;
+        if (rank < P) top_keys[rank] = kc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        bool ok = !too_many && m >= P;
+        if (ok) {
+            const float dp = key_dist(top_keys[P - 1]);
+            ok = certify(bound, dp, a.qstats[frame], a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel,
+                         a.exact_rel);
+        }
+        ok_s = ok;
+        a.probe_ok[frame] = ok ? 1 : 0;
+        if (!ok) {
+            const int pos = atomicAdd(a.fallback_count, 1);
+            a.fallback_list[pos] = static_cast<int32_t>(frame);
+        }
+    }
+    __syncthreads();
+    if (ok_s && tid < P) {
+        const int32_t list = static_cast<int32_t>(key_pos(top_keys[tid]));
+        a.probes[frame * P + tid] = list;
+        atomicAdd(&a.list_count[list], 1);
+    }
+}
+
+// One CTA of 1024 threads: pair offsets per list (exclusive scan of
+// list_count), reset of the scatter cursors, and the fine-stage work items
+// (list, frame tile within the list's pairs).
+__global__ void __launch_bounds__(1024) bucket_scan_kernel(const int32_t *__restrict__ list_count, int nlist,
+                                                           int32_t *__restrict__ list_start,
+                                                           int32_t *__restrict__ list_cursor, int2 *__restrict__ items,
+                                                           int *__restrict__ item_count) {
+    __shared__ int warp_pairs[32], warp_items[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (nlist + 1023) / 1024;
+    const int l0 = min(nlist, tid * per), l1 = min(nlist, l0 + per);
+    int pairs = 0, tiles = 0;
+    for (int l = l0; l < l1; ++l) {
+        const int c = list_count[l];
+        pairs += c;
+        tiles += (c + kTileM - 1) / kTileM;
+    }
+    int ip = pairs, it = tiles;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int up = __shfl_up_sync(kFullMask, ip, off), ut = __shfl_up_sync(kFullMask, it, off);
+        if (lane >= off) {
+            ip += up;
+            it += ut;
+        }
+    }
+    if (lane == 31) {
+        warp_pairs[warp] = ip;
+        warp_items[warp] = it;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int wp = warp_pairs[lane], wi = warp_items[lane];
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int up = __shfl_up_sync(kFullMask, wp, off), ut = __shfl_up_sync(kFullMask, wi, off);
+            if (lane >= off) {
+                wp += up;
+                wi += ut;
+            }
+        }
+        warp_pairs[lane] = wp;
+        warp_items[lane] = wi;
+    }
+    __syncthreads();
+    int pbase = ip - pairs + (warp > 0 ? warp_pairs[warp - 1] : 0);
+    int ibase = it - tiles + (warp > 0 ? warp_items[warp - 1] : 0);
+    for (int l = l0; l < l1; ++l) {
+        const int c = list_count[l];
+        list_start[l] = pbase;
+        list_cursor[l] = 0;
+        const int nt = (c + kTileM - 1) / kTileM;
+        for (int t = 0; t < nt; ++t) items[ibase + t] = make_int2(l, t);
+        pbase += c;
+        ibase += nt;
+    }
+    if (tid == 1023) {
+        list_start[nlist] = warp_pairs[31];
+        *item_count = warp_items[31];
+    }
+}
+
+__global__ void bucket_scatter_kernel(const int32_t *__restrict__ probes, const int32_t *__restrict__ probe_ok,
+                                      long long frames, int P, const int32_t *__restrict__ list_start,
+                                      int32_t *__restrict__ list_cursor, int32_t *__restrict__ pair_frame,
+                                      int32_t *__restrict__ pair_slot) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= frames * P) return;
+    const long long f = i / P;
+    if (!probe_ok[f]) return;
+    const int32_t list = probes[i];
+    const int32_t pos = list_start[list] + atomicAdd(&list_cursor[list], 1);
+    pair_frame[pos] = static_cast<int32_t>(f);
+    pair_slot[i] = pos;
+}
+
+// One warp per pair: its frame's fp16 row into list order.
+__global__ void gather_pairs_kernel(const __half *__restrict__ q16, int d_pad, const int32_t *__restrict__ pair_frame,
+                                    const int32_t *__restrict__ pair_total, __half *__restrict__ qp,
+                                    long long max_pairs) {
+    const long long pos = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (pos >= max_pairs || pos >= *pair_total) return;
+    const uint4 *src = reinterpret_cast<const uint4 *>(q16 + static_cast<size_t>(pair_frame[pos]) * d_pad);
+    uint4 *dst = reinterpret_cast<uint4 *>(qp + static_cast<size_t>(pos) * d_pad);
+    for (int i = lane; i < d_pad / 8; i += 32) dst[i] = src[i];
+}
+
+struct IvfMergeArgs {
+    int d;
+    int nprobe;
+    int pair_stride;
+    const int32_t *probes;
+    const int32_t *probe_ok;
+    const int32_t *pair_slot;
+    const int32_t *offsets;
+    const unsigned long long *keys;  // [kHalves * kItemKeep][pair_stride]
+    const int *counts;               // [kHalves][pair_stride]
+    const float *thr;
+    const float4 *qstats;
+    const float *queries;
+    float *out;
+    const float *index_rate;
+    int mode;
+    int k;
+    float *dist_out;
+    int64_t *label_out;
+    int64_t label_base;
+    const float *vectors;
+    const int32_t *ids;
+    float max_norm, max_hat, max_residual, acc_rel, norm_rel, exact_rel;
+    int32_t *fallback_list;
+    int32_t *fallback_count;
+    DeviceCounters *counters;
+};
+
+__global__ void __launch_bounds__(kMergeThreads) ivf_merge_kernel(IvfMergeArgs a) {
+    constexpr int kSlots = kIvfMaxProbe * kHalves * kItemKeep;
+    extern __shared__ __align__(16) float iq[];  // [d]
+    __shared__ unsigned long long keys[kSlots];
+    __shared__ SelectState sel;
+    __shared__ unsigned long long sel_keys[kRerankMax];
+    __shared__ unsigned long long octet_best[32 * 8];
+    __shared__ unsigned long long best[8];
+    __shared__ int32_t pstart[kIvfMaxProbe], pend[kIvfMaxProbe];
+    __shared__ uint32_t pbase[kIvfMaxProbe + 1];
+    __shared__ int certified_s;
+    __shared__ int32_t best_row[8];
+    __shared__ double weights[8];
+    __shared__ double weight_sum;
+    const int tid = threadIdx.x, lane = tid & 31, octet = tid >> 3, j = tid & 7;
+    const long long frame = blockIdx.x;
+    if (!a.probe_ok[frame]) return;  // r <= 0 (handled) or exact re-run
+    const int d = a.d, P = a.nprobe;
+    const size_t stride = static_cast<size_t>(a.pair_stride);
+    const float *src = a.queries + frame * d;
+    float *dst = a.out + frame * d;
+    const float inf = __int_as_float(0x7f800000);
+    const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
+    for (int i = tid; i < d; i += kMergeThreads) iq[i] = src[i];
+    if (tid == 0) {
+        uint32_t acc = 0;
+        for (int p = 0; p < P; ++p) {
+            const int32_t list = a.probes[frame * P + p];
+            pstart[p] = a.offsets[list];
+            pend[p] = a.offsets[list + 1];
+            pbase[p] = acc;
+            acc += static_cast<uint32_t>(pend[p] - pstart[p]);
+        }
+        pbase[P] = acc;
+    }
+    float tmin = inf;
+    int total = 0;
+    for (int i = tid; i < kSlots; i += kMergeThreads) {
+        const int p = i / (kHalves * kItemKeep), h = (i / kItemKeep) % kHalves, slot = i % kItemKeep;
+        unsigned long long key = kEmptyKey;
+        if (p < P) {
+            const size_t pos = static_cast<size_t>(a.pair_slot[frame * P + p]);
+            const int cnt = a.counts[h * stride + pos];
+            if (slot == 0) {
+                tmin = fminf(tmin, a.thr[h * stride + pos]);
+                total += cnt;
+            }
+            if (slot < cnt) key = a.keys[(h * kItemKeep + slot) * stride + pos];
+        }
+        keys[i] = key;
+    }
+    block_min_sum(tmin, total, sel);
+    float cut;
+    bool too_many;
+    const int m = select_rerank(keys, kSlots, total, sel_keys, sel, cut, too_many);
+    const float bound = fminf(tmin, cut);
+    // exact re-rank; the key's position is the reference's scan position
+    Top8 top;
+    top.init();
+    for (int c0 = 0; c0 < m; c0 += 32) {
+        const int c = c0 + octet;
+        const bool valid = c < m;
+        const uint32_t row = key_pos(sel_keys[valid ? c : 0]);
+        const float dist = octet_l2(iq, a.vectors + static_cast<size_t>(row) * d, d, j, lane & ~7, kFullMask);
+        if (valid && dist < inf) {
+            int p = 0;
+            while (p + 1 < P && !(static_cast<int32_t>(row) >= pstart[p] && static_cast<int32_t>(row) < pend[p])) ++p;
+            top.insert(make_key(dist, pbase[p] + (row - static_cast<uint32_t>(pstart[p]))));
+        }
+    }
+    if (j == 0)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) octet_best[octet * 8 + i] = top.k[i];
+    __syncthreads();
+    merge_octet_lists(octet_best, best);
+    if (tid == 0) {
+        int count = 0;
+        while (count < 8 && best[count] != kEmptyKey) ++count;
+        const float d8 = count == 8 ? key_dist(best[7]) : inf;
+        const bool ok = !too_many && certify(bound, d8, a.qstats[frame], a.max_norm, a.max_hat, a.max_residual,
+                                             a.acc_rel, a.norm_rel, a.exact_rel);
+        certified_s = ok ? count + 1 : 0;
+    }
+    if (tid < 8) {
+        int32_t row = -1;
+        const unsigned long long key = best[tid];
+        if (key != kEmptyKey) {
+            const uint32_t pos = key_pos(key);
+            int p = 0;
+            while (p + 1 < P && pbase[p + 1] <= pos) ++p;
+            row = pstart[p] + static_cast<int32_t>(pos - pbase[p]);
+        }
+        best_row[tid] = row;
+    }
+    __syncthreads();
+    const int cert = certified_s;
+    if (cert == 0) {
+        if (tid == 0) {
+            const int pos = atomicAdd(a.fallback_count, 1);
+            a.fallback_list[pos] = static_cast<int32_t>(frame);
+        }
+        return;
+    }
+    const int count = cert - 1;
+    if (tid == 0 && a.counters) atomicAdd(&a.counters->candidate_frames, 1ull);
+    if (a.mode == kModeSearch) {
+        if (tid < a.k) {
+            const bool have = tid < count;
+            a.dist_out[frame * a.k + tid] = have ? key_dist(best[tid]) : inf;
+            a.label_out[frame * a.k + tid] = have ? static_cast<int64_t>(a.ids[best_row[tid]]) + a.label_base : -1;
+        }
+        return;
+    }
+    if (count == 0) {
+        if (tid == 0 && a.counters) atomicAdd(&a.counters->empty_frames, 1ull);
+        if (dst != src)
+            for (int i = tid; i < d; i += kMergeThreads) dst[i] = iq[i];
+        return;
+    }
+    if (tid == 0) {
+        float dist[8];
+        double w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dist[i] = key_dist(best[i]);
+        weight_sum = reference_weights(dist, count, w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) weights[i] = w[i];
+    }
+    __syncthreads();
+    double w[8];
+    int32_t rows[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        w[i] = weights[i];
+        rows[i] = best_row[i];
+    }
+    const double sum = weight_sum;
+    for (int i = tid; i < d; i += kMergeThreads) {
+        float v[8];
+#pragma unroll
+        for (int kq = 0; kq < 8; ++kq)
+            v[kq] = kq < count ? __ldg(a.vectors + static_cast<size_t>(rows[kq]) * d + i) : 0.f;
+        dst[i] = reference_blend_element(iq[i], v, w, sum, count, ratio);
+    }
+}
+
+struct IvfWs {
+    size_t q16, qstats, ckeys, ccounts, cthr, probes, probe_ok, list_count, list_cursor, list_start, items, item_count,
+        pair_frame, pair_slot, qp, fkeys, fcounts, fthr, flist, fcount, total;
+};
+
+IvfWs ivf_ws_layout(size_t frames, int d_pad, int nlist, int nprobe, int sms) {
+    IvfWs l{};
+    const size_t fr = (frames + kTileM - 1) / kTileM * kTileM;
+    const size_t clists = static_cast<size_t>(items_cap(frames, sms)) * kHalves;
+    const size_t pairs = frames * static_cast<size_t>(nprobe);
+    const size_t max_items = (pairs + kTileM - 1) / kTileM + static_cast<size_t>(nlist);
+    size_t off = 0;
+    auto take = [&](size_t &field, size_t bytes) {
+        field = off;
+        off = align256(off + bytes);
+    };
+    take(l.q16, fr * d_pad * sizeof(__half));
+    take(l.qstats, fr * sizeof(float4));
+    take(l.ckeys, clists * kItemKeep * kTileM * sizeof(unsigned long long));
+    take(l.ccounts, clists * kTileM * sizeof(int));
+    take(l.cthr, clists * kTileM * sizeof(float));
+    take(l.probes, pairs * sizeof(int32_t));
+    take(l.probe_ok, fr * sizeof(int32_t));
+    take(l.list_count, static_cast<size_t>(nlist) * sizeof(int32_t));
+    take(l.list_cursor, static_cast<size_t>(nlist) * sizeof(int32_t));
+    take(l.list_start, static_cast<size_t>(nlist + 1) * sizeof(int32_t));
+    take(l.items, max_items * sizeof(int2));
+    take(l.item_count, 16);
+    take(l.pair_frame, pairs * sizeof(int32_t));
+    take(l.pair_slot, pairs * sizeof(int32_t));
+    take(l.qp, pairs * d_pad * sizeof(__half));
+    take(l.fkeys, static_cast<size_t>(kHalves) * kItemKeep * pairs * sizeof(unsigned long long));
+    take(l.fcounts, kHalves * pairs * sizeof(int));
+    take(l.fthr, kHalves * pairs * sizeof(float));
+    take(l.flist, fr * sizeof(int32_t));
+    take(l.fcount, 16);
+    l.total = off;
+    return l;
+}
+
+}  // namespace
+
+namespace {
+
+// fp16 shadow + squared norms + bounds of `rows` fp32 rows into `xh`/`norms`
+// (already allocated, rows_pad rows); returns {max ||x||, max ||x^||, max ||x - x^||}.
+void build_shadow(const float *x, int64_t rows, int64_t rows_pad, int d, int d_pad, float scale, __half *xh,
+                  float *norms, float out[3]) {
+    cuda_check(cudaMemset(xh, 0, static_cast<size_t>(rows_pad) * d_pad * sizeof(__half)));
+    unsigned int *maxima = nullptr;
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&maxima), 4 * sizeof(unsigned int)));
+    cuda_check(cudaMemset(maxima, 0, 4 * sizeof(unsigned int)));
+    fill_kernel<<<64, 256>>>(norms + rows, static_cast<size_t>(rows_pad - rows), std::numeric_limits<float>::infinity());
+    build_rows_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256>>>(x, xh, norms, rows, d, d_pad, scale,
+                                                                             maxima);
+    cudaError_t rc = cudaGetLastError();
+    unsigned int m[3] = {0, 0, 0};
+    if (rc == cudaSuccess) rc = cudaMemcpy(m, maxima, sizeof(m), cudaMemcpyDeviceToHost);
+    cudaFree(maxima);
+    cuda_check(rc);
+    std::memcpy(out, m, sizeof(m));
+    out[0] *= 1.0001f;
+    out[1] *= 1.0001f;
+    out[2] = out[2] * 1.0001f + 1e-30f;
+}
+
+float max_abs(const float *x, size_t count) {
+    unsigned int *m = nullptr;
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&m), sizeof(unsigned int)));
+    cuda_check(cudaMemset(m, 0, sizeof(unsigned int)));
+    max_abs_kernel<<<1024, 256>>>(x, count, m);
+    cudaError_t rc = cudaGetLastError();
+    unsigned int bits = 0;
+    if (rc == cudaSuccess) rc = cudaMemcpy(&bits, m, 4, cudaMemcpyDeviceToHost);
+    cudaFree(m);
+    cuda_check(rc);
+    float v;
+    std::memcpy(&v, &bits, 4);
+    return v;
+}
+
 }  // namespace
 
 void build_tc(VfrIndex *ix) {
-    if (ix->nlist != 1) return;  // IVF indexes use the exact engine
+    const bool ivf = ix->nlist > 1;
+    if (ivf && ix->nprobe > kIvfMaxProbe) return;  // wide probes use the exact engine
     int dev = 0;
     cuda_check(cudaGetDevice(&dev));
     cuda_check(cudaDeviceGetAttribute(&ix->sm_count, cudaDevAttrMultiProcessorCount, dev));
     ix->d_pad = (ix->d + kTileK - 1) / kTileK * kTileK;
-    ix->n_pad = (ix->n + kTileN - 1) / kTileN * kTileN;
-    const size_t hbytes = static_cast<size_t>(ix->n_pad) * ix->d_pad * sizeof(__half);
-    cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->vectors_h), hbytes), "cudaMalloc fp16 shadow");
+    // IVF lists start anywhere, so a list's last tile can reach 255 rows past n
+    ix->n_pad = (ix->n + kTileN - 1) / kTileN * kTileN + (ivf ? kTileN : 0);
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->vectors_h),
+                          static_cast<size_t>(ix->n_pad) * ix->d_pad * sizeof(__half)),
+               "cudaMalloc fp16 shadow");
     cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->row_norms), ix->n_pad * sizeof(float)), "cudaMalloc norms");
-    cuda_check(cudaMemset(ix->vectors_h, 0, hbytes));
-    unsigned int *maxima = nullptr;
-    cuda_check(cudaMalloc(reinterpret_cast<void **>(&maxima), 4 * sizeof(unsigned int)));
-    cuda_check(cudaMemset(maxima, 0, 4 * sizeof(unsigned int)));
-    const size_t values = static_cast<size_t>(ix->n) * ix->d;
-    max_abs_kernel<<<1024, 256>>>(ix->vectors, values, maxima + 3);
-    cuda_check(cudaGetLastError());
-    unsigned int maxabs_bits = 0;
-    cuda_check(cudaMemcpy(&maxabs_bits, maxima + 3, 4, cudaMemcpyDeviceToHost));
-    float maxabs;
-    std::memcpy(&maxabs, &maxabs_bits, 4);
     // power-of-two scale keeping |s x| within [1, 8192] where possible, so
     // frames up to 8x the database's magnitude still fit fp16
+    float maxabs = max_abs(ix->vectors, static_cast<size_t>(ix->n) * ix->d);
+    if (ivf) maxabs = std::max(maxabs, max_abs(ix->centroids, static_cast<size_t>(ix->nlist) * ix->d));
     int e = 0;
     if (maxabs > 0.f) {
         const int ex = static_cast<int>(std::floor(std::log2(maxabs)));
@@ -894,36 +1445,49 @@ void build_tc(VfrIndex *ix) {
         if (ex < 0) e = -ex;
     }
     ix->tc_scale = std::ldexp(1.0f, e);
-    fill_kernel<<<64, 256>>>(ix->row_norms + ix->n, static_cast<size_t>(ix->n_pad - ix->n),
-                             std::numeric_limits<float>::infinity());
-    const long long warps = ix->n;
-    build_rows_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256>>>(
-        ix->vectors, ix->vectors_h, ix->row_norms, ix->n, ix->d, ix->d_pad, ix->tc_scale, maxima);
-    cuda_check(cudaGetLastError());
-    unsigned int m[3];
-    cuda_check(cudaMemcpy(m, maxima, sizeof(m), cudaMemcpyDeviceToHost));
-    cudaFree(maxima);
-    float mf[3];
-    std::memcpy(mf, m, sizeof(mf));
-    ix->max_row_norm = mf[0] * 1.0001f;
-    ix->max_row_hat = mf[1] * 1.0001f;
-    ix->max_row_residual = mf[2] * 1.0001f + 1e-30f;
-    if (!std::isfinite(ix->max_row_norm) || !std::isfinite(ix->max_row_hat)) {
+    float m[3];
+    build_shadow(ix->vectors, ix->n, ix->n_pad, ix->d, ix->d_pad, ix->tc_scale, ix->vectors_h, ix->row_norms, m);
+    ix->max_row_norm = m[0];
+    ix->max_row_hat = m[1];
+    ix->max_row_residual = m[2];
+    bool finite = std::isfinite(ix->max_row_norm) && std::isfinite(ix->max_row_hat);
+    if (ivf && finite) {
+        ix->nlist_pad = (ix->nlist + kTileN - 1) / kTileN * kTileN;
+        cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->centroids_h),
+                              static_cast<size_t>(ix->nlist_pad) * ix->d_pad * sizeof(__half)));
+        cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->centroid_norms), ix->nlist_pad * sizeof(float)));
+        build_shadow(ix->centroids, ix->nlist, ix->nlist_pad, ix->d, ix->d_pad, ix->tc_scale, ix->centroids_h,
+                     ix->centroid_norms, m);
+        ix->max_cent_norm = m[0];
+        ix->max_cent_hat = m[1];
+        ix->max_cent_residual = m[2];
+        finite = std::isfinite(ix->max_cent_norm) && std::isfinite(ix->max_cent_hat);
+    }
+    if (!finite) {
         // squared norms overflow fp32: the candidate bounds are meaningless,
         // so this index stays on the exact engine
         release_tc(ix);
         return;
     }
     encode_rows(&ix->tmap_vectors, ix->vectors_h, ix->d_pad, ix->n_pad, kTileN);
-    cuda_check(cudaFuncSetAttribute(cand_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (ivf) encode_rows(&ix->tmap_centroids, ix->centroids_h, ix->d_pad, ix->nlist_pad, kTileN);
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kSmemTC)));
+    cuda_check(cudaFuncSetAttribute(cand_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kSmemTC)));
     cuda_check(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    cuda_check(cudaFuncSetAttribute(coarse_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    cuda_check(cudaDeviceSynchronize());
     ix->have_tc = true;
 }
 
 void release_tc(VfrIndex *ix) noexcept {
     if (ix->vectors_h) cudaFree(ix->vectors_h);
     if (ix->row_norms) cudaFree(ix->row_norms);
+    if (ix->centroids_h) cudaFree(ix->centroids_h);
+    if (ix->centroid_norms) cudaFree(ix->centroid_norms);
+    ix->centroids_h = nullptr;
+    ix->centroid_norms = nullptr;
     if (ix->ws.base) cudaFree(ix->ws.base);
     ix->vectors_h = nullptr;
     ix->row_norms = nullptr;
@@ -933,15 +1497,17 @@ void release_tc(VfrIndex *ix) noexcept {
 
 void reserve_tc(VfrIndex *ix, size_t frames) {
     if (!ix->have_tc || frames <= ix->ws.frames) return;
-    const WsLayout l = ws_layout(frames, ix->d_pad, ix->sm_count);
+    const size_t bytes = ix->nlist > 1
+                             ? ivf_ws_layout(frames, ix->d_pad, ix->nlist, ix->nprobe, ix->sm_count).total
+                             : ws_layout(frames, ix->d_pad, ix->sm_count).total;
     void *p = nullptr;
-    cuda_check(cudaMalloc(&p, l.total), "cudaMalloc retrieval workspace");
+    cuda_check(cudaMalloc(&p, bytes), "cudaMalloc retrieval workspace");
     if (ix->ws.base) {
         cuda_check(cudaDeviceSynchronize());
         cudaFree(ix->ws.base);
     }
     ix->ws.base = p;
-    ix->ws.bytes = l.total;
+    ix->ws.bytes = bytes;
     ix->ws.frames = frames;
 }
 
@@ -952,6 +1518,206 @@ bool use_tc(const VfrIndex *ix, size_t frames) {
     return ix->n >= 2048 && frames >= 1;
 }
 
+namespace {
+
+// IVF-Flat: coarse candidates + certified probe selection, bucketing of the
+// (frame, probe) pairs by list, per-list candidates, exact merge, and the
+// exact engine for uncertified frames.  Workspace from ivf_ws_layout.
+void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, int mode, int k, float *dist_out,
+             int64_t *label_out, size_t frames, cudaStream_t stream) {
+    const int P = ix->nprobe;
+    const IvfWs l = ivf_ws_layout(ix->ws.frames, ix->d_pad, ix->nlist, P, ix->sm_count);
+    uint8_t *ws = static_cast<uint8_t *>(ix->ws.base);
+    __half *q16 = reinterpret_cast<__half *>(ws + l.q16);
+    float4 *qstats = reinterpret_cast<float4 *>(ws + l.qstats);
+    auto *ckeys = reinterpret_cast<unsigned long long *>(ws + l.ckeys);
+    int *ccounts = reinterpret_cast<int *>(ws + l.ccounts);
+    float *cthr = reinterpret_cast<float *>(ws + l.cthr);
+    int32_t *probes = reinterpret_cast<int32_t *>(ws + l.probes);
+    int32_t *probe_ok = reinterpret_cast<int32_t *>(ws + l.probe_ok);
+    int32_t *list_count = reinterpret_cast<int32_t *>(ws + l.list_count);
+    int32_t *list_cursor = reinterpret_cast<int32_t *>(ws + l.list_cursor);
+    int32_t *list_start = reinterpret_cast<int32_t *>(ws + l.list_start);
+    int2 *items = reinterpret_cast<int2 *>(ws + l.items);
+    int *item_count = reinterpret_cast<int *>(ws + l.item_count);
+    int32_t *pair_frame = reinterpret_cast<int32_t *>(ws + l.pair_frame);
+    int32_t *pair_slot = reinterpret_cast<int32_t *>(ws + l.pair_slot);
+    __half *qp = reinterpret_cast<__half *>(ws + l.qp);
+    auto *fkeys = reinterpret_cast<unsigned long long *>(ws + l.fkeys);
+    int *fcounts = reinterpret_cast<int *>(ws + l.fcounts);
+    float *fthr = reinterpret_cast<float *>(ws + l.fthr);
+    int32_t *flist = reinterpret_cast<int32_t *>(ws + l.flist);
+    int32_t *fcount = reinterpret_cast<int32_t *>(ws + l.fcount);
+    const size_t pair_cap = ix->ws.frames * static_cast<size_t>(P);
+    const float coef = -2.0f / (ix->tc_scale * ix->tc_scale);
+    const float acc_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -22);
+    const float norm_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -23);
+    const float exact_rel = static_cast<float>(ix->d / 8 + 9) * std::ldexp(1.0f, -24);
+
+    // 1. frames -> fp16
+    const long long lanes = static_cast<long long>(frames) * 32;
+    ix->prof.begin(kProfPrep, stream);
+    prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
+        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale);
+    cuda_check(cudaGetLastError());
+    ix->prof.end(stream);
+    cuda_check(cudaMemsetAsync(fcount, 0, sizeof(int32_t), stream));
+    cuda_check(cudaMemsetAsync(list_count, 0, static_cast<size_t>(ix->nlist) * sizeof(int32_t), stream));
+
+    // 2. coarse candidates over the centroids
+    const Plan pc = make_plan(frames, ix->nlist, ix->sm_count);
+    CUtensorMap tmap_q;
+    encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
+    CandArgs ca{};
+    ca.frames = static_cast<int>(frames);
+    ca.n_qtiles = pc.n_qtiles;
+    ca.segments = pc.segments;
+    ca.tiles_per_seg = pc.tiles_per_seg;
+    ca.ksteps = ix->d_pad / kTileK;
+    ca.n = ix->nlist;
+    ca.seg_rows = static_cast<int64_t>(pc.tiles_per_seg) * kTileN;
+    ca.row_norms = ix->centroid_norms;
+    ca.coef = coef;
+    ca.out_keys = ckeys;
+    ca.out_count = ccounts;
+    ca.out_thr = cthr;
+    ca.counters = ix->counters;
+    ix->prof.begin(kProfCand, stream);
+    cand_kernel<false><<<std::min(pc.segments * pc.n_qtiles, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(
+        tmap_q, ix->tmap_centroids, ca);
+    cuda_check(cudaGetLastError());
+    ix->prof.end(stream);
+
+    // 3. certified probe lists
+    CoarseArgs cs{};
+    cs.d = ix->d;
+    cs.nlist = ix->nlist;
+    cs.nprobe = P;
+    cs.n_qtiles = pc.n_qtiles;
+    cs.lists = pc.segments * kHalves;
+    cs.slots = (cs.lists * kItemKeep + 31) / 32 * 32;
+    cs.keys = ckeys;
+    cs.counts = ccounts;
+    cs.thr = cthr;
+    cs.qstats = qstats;
+    cs.queries = queries;
+    cs.out = out;
+    cs.index_rate = rate;
+    cs.mode = mode;
+    cs.centroids = ix->centroids;
+    cs.max_norm = ix->max_cent_norm;
+    cs.max_hat = ix->max_cent_hat;
+    cs.max_residual = ix->max_cent_residual;
+    cs.acc_rel = acc_rel;
+    cs.norm_rel = norm_rel;
+    cs.exact_rel = exact_rel;
+    cs.probes = probes;
+    cs.probe_ok = probe_ok;
+    cs.list_count = list_count;
+    cs.fallback_list = flist;
+    cs.fallback_count = fcount;
+    ix->prof.begin(kProfMerge, stream);
+    coarse_select_kernel<<<static_cast<unsigned>(frames), kMergeThreads,
+                           static_cast<size_t>(cs.slots) * 8 + static_cast<size_t>(ix->d) * 4, stream>>>(cs);
+    cuda_check(cudaGetLastError());
+    // 4. pairs bucketed by list, frames gathered into list order
+    bucket_scan_kernel<<<1, 1024, 0, stream>>>(list_count, ix->nlist, list_start, list_cursor, items, item_count);
+    cuda_check(cudaGetLastError());
+    const long long npairs = static_cast<long long>(frames) * P;
+    bucket_scatter_kernel<<<static_cast<unsigned>((npairs + 255) / 256), 256, 0, stream>>>(
+        probes, probe_ok, static_cast<long long>(frames), P, list_start, list_cursor, pair_frame, pair_slot);
+    cuda_check(cudaGetLastError());
+    gather_pairs_kernel<<<static_cast<unsigned>((npairs * 32 + 255) / 256), 256, 0, stream>>>(
+        q16, ix->d_pad, pair_frame, list_start + ix->nlist, qp, npairs);
+    cuda_check(cudaGetLastError());
+    ix->prof.end(stream);
+
+    // 5. per-list candidates
+    CUtensorMap tmap_qp;
+    encode_rows(&tmap_qp, qp, ix->d_pad, pair_cap, kTileM);
+    CandArgs cf{};
+    cf.ksteps = ix->d_pad / kTileK;
+    cf.n = ix->n;
+    cf.row_norms = ix->row_norms;
+    cf.coef = coef;
+    cf.out_keys = fkeys;
+    cf.out_count = fcounts;
+    cf.out_thr = fthr;
+    cf.counters = ix->counters;
+    cf.items = items;
+    cf.item_count = item_count;
+    cf.list_offsets = ix->offsets;
+    cf.list_start = list_start;
+    cf.pair_stride = static_cast<int>(pair_cap);
+    ix->prof.begin(kProfCand, stream);
+    cand_kernel<true><<<ix->sm_count, kThreadsTC, kSmemTC, stream>>>(tmap_qp, ix->tmap_vectors, cf);
+    cuda_check(cudaGetLastError());
+    ix->prof.end(stream);
+
+    // 6. exact merge, certificate, blend / search output
+    IvfMergeArgs im{};
+    im.d = ix->d;
+    im.nprobe = P;
+    im.pair_stride = static_cast<int>(pair_cap);
+    im.probes = probes;
+    im.probe_ok = probe_ok;
+    im.pair_slot = pair_slot;
+    im.offsets = ix->offsets;
+    im.keys = fkeys;
+    im.counts = fcounts;
+    im.thr = fthr;
+    im.qstats = qstats;
+    im.queries = queries;
+    im.out = out;
+    im.index_rate = rate;
+    im.mode = mode;
+    im.k = k;
+    im.dist_out = dist_out;
+    im.label_out = label_out;
+    im.label_base = ix->label_base;
+    im.vectors = ix->vectors;
+    im.ids = ix->ids;
+    im.max_norm = ix->max_row_norm;
+    im.max_hat = ix->max_row_hat;
+    im.max_residual = ix->max_row_residual;
+    im.acc_rel = acc_rel;
+    im.norm_rel = norm_rel;
+    im.exact_rel = exact_rel;
+    im.fallback_list = flist;
+    im.fallback_count = fcount;
+    im.counters = ix->counters;
+    ix->prof.begin(kProfMerge, stream);
+    ivf_merge_kernel<<<static_cast<unsigned>(frames), kMergeThreads, static_cast<size_t>(ix->d) * 4, stream>>>(im);
+    cuda_check(cudaGetLastError());
+    ix->prof.end(stream);
+
+    // 7. frames either certificate left open: exact re-run
+    ExactArgs ea{};
+    ea.d = ix->d;
+    ea.nlist = ix->nlist;
+    ea.nprobe = ix->nprobe;
+    ea.centroids = ix->centroids;
+    ea.offsets = ix->offsets;
+    ea.vectors = ix->vectors;
+    ea.ids = ix->ids;
+    ea.queries = queries;
+    ea.out = out;
+    ea.index_rate = rate;
+    ea.mode = mode;
+    ea.k = k;
+    ea.dist_out = dist_out;
+    ea.label_out = label_out;
+    ea.label_base = ix->label_base;
+    ea.counters = ix->counters;
+    ea.frame_list = flist;
+    ea.frame_count = fcount;
+    ix->prof.begin(kProfExact, stream);
+    launch_exact(ea, static_cast<long long>(frames), stream);
+    ix->prof.end(stream);
+}
+
+}  // namespace
+
 void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, int mode, int k, float *dist_out,
             int64_t *label_out, size_t frames, cudaStream_t stream) {
     if (frames > ix->ws.frames) {
@@ -961,6 +1727,10 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
                 "retrieval workspace too small for this frame count during stream capture; call "
                 "vfr_retrieval_reserve first");
         reserve_tc(ix, frames);
+    }
+    if (ix->nlist > 1) {
+        run_ivf(ix, queries, out, rate, mode, k, dist_out, label_out, frames, stream);
+        return;
     }
     const WsLayout l = ws_layout(ix->ws.frames, ix->d_pad, ix->sm_count);
     uint8_t *ws = static_cast<uint8_t *>(ix->ws.base);
@@ -1000,7 +1770,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     const int items = p.segments * p.n_qtiles;
     const int grid = std::min(items, ix->sm_count);
     ix->prof.begin(kProfCand, stream);
-    cand_kernel<<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    cand_kernel<false><<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
 
@@ -1172,7 +1942,7 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ca.out_thr = thr;
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
-    cand_kernel<<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    cand_kernel<false><<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
     cuda_check(cudaGetLastError());
 
     MergeArgs ma{};
@@ -1235,7 +2005,7 @@ extern "C" int vfr_retrieval_blend_noalloc(VfrIndex *index, float *features, siz
         vfr::require(index && features && frames > 0 && index_rate, "invalid FAISS GPU blend arguments");
         vfr::require(width == index->d, "FAISS feature width mismatch");
         vfr::require(stream && stream->stream, "invalid FAISS CUDA stream");
-        vfr::require(index->have_tc,
+        vfr::require(index->have_tc && index->nlist == 1,
                      "no-allocation blend needs the tensor-core layout (flat index, tensor or auto engine)");
         vfr::require(frames <= vfr::kNoAllocMaxFrames,
                      "no-allocation blend takes at most 256 frames per call");

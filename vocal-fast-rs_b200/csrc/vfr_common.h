@@ -113,6 +113,12 @@ struct VfrIndex {
     float max_row_hat = 0.f;       // max ||fp16(s x) / s||
     float max_row_residual = 0.f;  // max ||x - fp16(s x) / s||
     int sm_count = 148;
+    // IVF: the same layout for the coarse centroids (nlist_pad rows).
+    __half *centroids_h = nullptr;
+    float *centroid_norms = nullptr;
+    int32_t nlist_pad = 0;
+    float max_cent_norm = 0.f, max_cent_hat = 0.f, max_cent_residual = 0.f;
+    alignas(64) CUtensorMap tmap_centroids;
     alignas(64) CUtensorMap tmap_vectors;  // fp16 rows, box [256 rows][64]
     bool have_tc = false;
     vfr::Workspace ws;
