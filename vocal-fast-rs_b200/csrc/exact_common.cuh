@@ -87,6 +87,39 @@ __device__ __forceinline__ float octet_l2(const float *__restrict__ q, const flo
     return __fadd_rn(s, tail);
 }
 
+// octet_l2 for N rows at once: N independent accumulation chains per lane
+// (each in the reference order), so N times as many row loads are in flight.
+// out[k] is the distance to x[k]; all 8 threads get the same values.
+template <int N>
+__device__ __forceinline__ void octet_l2n(const float *__restrict__ q, const float *const (&x)[N], int d, int j,
+                                          int octet_base, unsigned mask, float (&out)[N]) {
+    const int d8 = d & ~7;
+    float acc[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) acc[k] = 0.0f;
+#pragma unroll 4
+    for (int i = j; i < d8; i += 8) {
+        const float qi = q[i];
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            const float t = __fsub_rn(qi, __ldg(x[k] + i));
+            acc[k] = __fadd_rn(acc[k], __fmul_rn(t, t));
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        float s = -0.0f;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(mask, acc[k], octet_base + l));
+        float tail = -0.0f;
+        for (int i = d8; i < d; ++i) {
+            const float t = __fsub_rn(q[i], __ldg(x[k] + i));
+            tail = __fadd_rn(tail, __fmul_rn(t, t));
+        }
+        out[k] = __fadd_rn(s, tail);
+    }
+}
+
 // The reference's f64 weights for `count` neighbours; returns S.
 __device__ __forceinline__ double reference_weights(const float *dist, int count, double *w) {
     double sum = -0.0;

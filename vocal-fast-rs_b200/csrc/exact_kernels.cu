@@ -137,14 +137,22 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame) {
         const int begin = a.offsets[list];
         const int end = a.offsets[list + 1];
         const uint32_t base = probe_base[r];
-        for (int row0 = begin; row0 < end; row0 += kOctets) {
-            const int row = row0 + octet;
-            const bool valid = row < end;
-            const int rr = valid ? row : begin;
-            float dist = octet_l2(q, a.vectors + static_cast<size_t>(rr) * d, d, j, octet_base, kFullMask);
-            // the reference never admits +inf (best starts at +inf, `>=` rejects)
-            if (valid && dist < __int_as_float(0x7f800000))
-                top.insert(make_key(dist, base + static_cast<uint32_t>(row - begin)));
+        for (int row0 = begin; row0 < end; row0 += 4 * kOctets) {
+            const float *xs[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int row = row0 + octet + k * kOctets;
+                xs[k] = a.vectors + static_cast<size_t>(row < end ? row : begin) * d;
+            }
+            float dist[4];
+            octet_l2n<4>(q, xs, d, j, octet_base, kFullMask, dist);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int row = row0 + octet + k * kOctets;
+                // the reference never admits +inf (best starts at +inf, `>=` rejects)
+                if (row < end && dist[k] < __int_as_float(0x7f800000))
+                    top.insert(make_key(dist[k], base + static_cast<uint32_t>(row - begin)));
+            }
         }
     }
     if (j == 0)

@@ -37,7 +37,13 @@ constexpr int kTileM = 128;  // frames per tile: TMEM lanes
 constexpr int kTileN = 256;  // rows per MMA / accumulator
 constexpr int kTileK = 64;   // fp16 elements per 128-byte swizzled row
 constexpr int kStages = 4;
-constexpr int kItemKeep = 16;  // candidates kept per frame per work item (registers)
+// Candidates kept per frame per candidate list (in registers).  Flat work
+// items are random slices of the database, so a frame's neighbours spread
+// over many lists and 8 suffice; IVF lists (and the coarse centroid lists)
+// hold a frame's neighbours together and keep 16.
+constexpr int kFlatKeep = 8;
+constexpr int kIvfKeep = 16;
+constexpr int kItemKeep = kIvfKeep;  // largest list size (shared-memory sizing)
 constexpr int kRerank = 64;     // candidates re-ranked exactly per frame (more on distance ties)
 constexpr int kRerankMax = 128;
 constexpr int kMaxSegments = 256;
@@ -121,6 +127,7 @@ __device__ __forceinline__ Item item_at(const CandArgs &a, int item) {
 // chain, so the lanes of a warp that insert in the same step share it.  Ties
 // between equal approximate distances may resolve either way: only "every
 // dropped row has d~ >= the threshold" matters to the exact stage.
+template <int kItemKeep>
 struct TopList {
     float dist[kItemKeep];
     uint32_t row[kItemKeep];
@@ -133,11 +140,12 @@ struct TopList {
     }
     // Replaces the list with the kItemKeep smallest of (list U chunk): sorts
     // the 16 chunk values with a bitonic network, takes the elementwise
-    // minimum against the list reversed (a bitonic sequence holding the 16
-    // smallest of both), and cleans it.  Cheaper than one insertion per value
-    // once more than a few values of the chunk pass the threshold.
+    // minimum of the list and the chunk's kItemKeep smallest reversed (a
+    // bitonic sequence holding the kItemKeep smallest of both), and cleans it.
+    // Cheaper than one insertion per value once many values of the chunk pass
+    // the threshold.
     __device__ __forceinline__ void merge16(float (&cd)[16], uint32_t (&cr)[16]) {
-        static_assert(kItemKeep == 16, "merge16 keeps 16");
+        static_assert(kItemKeep <= 16 && (kItemKeep & (kItemKeep - 1)) == 0, "power of two up to 16");
 #pragma unroll
         for (int k = 2; k <= 16; k <<= 1) {
 #pragma unroll
@@ -159,15 +167,15 @@ struct TopList {
             }
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const bool take = cd[15 - i] < dist[i];
-            dist[i] = take ? cd[15 - i] : dist[i];
-            row[i] = take ? cr[15 - i] : row[i];
+        for (int i = 0; i < kItemKeep; ++i) {
+            const bool take = cd[kItemKeep - 1 - i] < dist[i];
+            dist[i] = take ? cd[kItemKeep - 1 - i] : dist[i];
+            row[i] = take ? cr[kItemKeep - 1 - i] : row[i];
         }
 #pragma unroll
-        for (int j = 8; j > 0; j >>= 1) {
+        for (int j = kItemKeep / 2; j > 0; j >>= 1) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < kItemKeep; ++i) {
                 const int l = i ^ j;
                 if (l > i) {
                     const bool swap = dist[l] < dist[i];
@@ -205,7 +213,7 @@ __device__ __forceinline__ float4 load_norms4(const float *p) {
     else return __ldg(reinterpret_cast<const float4 *>(p));
 }
 
-template <bool kIvf>
+template <bool kIvf, int K>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     cand_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, CandArgs a) {
     extern __shared__ uint8_t smem_raw[];
@@ -346,7 +354,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             const Item it = item_at<kIvf>(a, item);
             const int64_t row0 = it.b_row0;
             const int tiles = it.tiles;
-            TopList top;
+            TopList<K> top;
             top.init();
             bool aborted = false;
             // This warp's copy of the row norms, one tile ahead: lane l holds
@@ -398,7 +406,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     // branch-free filter against the threshold at chunk start
                     float dd[16];
                     uint32_t mask = 0;
-                    const float thr = top.dist[kItemKeep - 1];
+                    const float thr = top.dist[K - 1];
                     // IVF: rows past the list's end belong to the next list
                     const int64_t lim = kIvf ? it.b_end - (static_cast<int64_t>(col_row) + c * 16) : 16;
 #pragma unroll
@@ -429,7 +437,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                         float x = dd[0];
 #pragma unroll
                         for (int i = 1; i < 16; ++i) x = e == i ? dd[i] : x;
-                        if (x < top.dist[kItemKeep - 1]) top.insert(x, col_row + c * 16 + e);
+                        if (x < top.dist[K - 1]) top.insert(x, col_row + c * 16 + e);
                     }
                     if (c + 1 < kHalfCols / 16) tc::tmem_wait_ld(v[cur ^ 1]);
                 }
@@ -445,25 +453,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             if (aborted) break;
             int cnt = 0;
 #pragma unroll
-            for (int i = 0; i < kItemKeep; ++i) cnt += top.dist[i] < inf;
+            for (int i = 0; i < K; ++i) cnt += top.dist[i] < inf;
             if constexpr (kIvf) {
                 if (r < it.a_rows) {
                     const size_t pos = static_cast<size_t>(it.a_row0) + r;
                     const size_t stride = static_cast<size_t>(a.pair_stride);
 #pragma unroll
-                    for (int i = 0; i < kItemKeep; ++i)
-                        if (i < cnt) a.out_keys[(half * kItemKeep + i) * stride + pos] = make_key(top.dist[i], top.row[i]);
+                    for (int i = 0; i < K; ++i)
+                        if (i < cnt) a.out_keys[(half * K + i) * stride + pos] = make_key(top.dist[i], top.row[i]);
                     a.out_count[half * stride + pos] = cnt;
-                    a.out_thr[half * stride + pos] = cnt == kItemKeep ? top.dist[kItemKeep - 1] : inf;
+                    a.out_thr[half * stride + pos] = cnt == K ? top.dist[K - 1] : inf;
                 }
             } else {
                 const size_t list = (static_cast<size_t>(it.seg) * kHalves + half) * a.n_qtiles + item % a.n_qtiles;
                 const size_t o = list * kTileM + r;
 #pragma unroll
-                for (int i = 0; i < kItemKeep; ++i)
-                    if (i < cnt) a.out_keys[(list * kItemKeep + i) * kTileM + r] = make_key(top.dist[i], top.row[i]);
+                for (int i = 0; i < K; ++i)
+                    if (i < cnt) a.out_keys[(list * K + i) * kTileM + r] = make_key(top.dist[i], top.row[i]);
                 a.out_count[o] = cnt;
-                a.out_thr[o] = cnt == kItemKeep ? top.dist[kItemKeep - 1] : inf;
+                a.out_thr[o] = cnt == K ? top.dist[K - 1] : inf;
             }
         }
     }
@@ -714,11 +722,11 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
         total += a.counts[o];
     }
     for (int i = tid; i < a.sort_size; i += kMergeThreads) {
-        const int s = i / kItemKeep, slot = i % kItemKeep;
+        const int s = i / kFlatKeep, slot = i % kFlatKeep;
         unsigned long long key = kEmptyKey;
         if (s < a.segments) {
             const size_t item = static_cast<size_t>(s) * a.n_qtiles + qtile;
-            if (slot < a.counts[item * kTileM + r]) key = a.keys[(item * kItemKeep + slot) * kTileM + r];
+            if (slot < a.counts[item * kTileM + r]) key = a.keys[(item * kFlatKeep + slot) * kTileM + r];
         }
         keys[i] = key;
     }
@@ -731,12 +739,20 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
     // exact re-rank in the reference order; flat scan position == row
     Top8 top;
     top.init();
-    for (int c0 = 0; c0 < m; c0 += 32) {
-        const int c = c0 + octet;
-        const bool valid = c < m;
-        const uint32_t row = key_pos(sel_keys[valid ? c : 0]);
-        const float dist = octet_l2(q, a.vectors + static_cast<size_t>(row) * d, d, j, lane & ~7, kFullMask);
-        if (valid && dist < inf) top.insert(make_key(dist, row));
+    for (int c0 = 0; c0 < m; c0 += 64) {
+        uint32_t rows[2];
+        const float *xs[2];
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 32 * kk;
+            rows[kk] = key_pos(sel_keys[c < m ? c : 0]);
+            xs[kk] = a.vectors + static_cast<size_t>(rows[kk]) * d;
+        }
+        float dist[2];
+        octet_l2n<2>(q, xs, d, j, lane & ~7, kFullMask, dist);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk)
+            if (c0 + octet + 32 * kk < m && dist[kk] < inf) top.insert(make_key(dist[kk], rows[kk]));
     }
     if (j == 0)
 #pragma unroll
@@ -939,7 +955,7 @@ WsLayout ws_layout(size_t frames, int d_pad, int sms) {
     l.qstats = off;
     off = align256(off + fr * sizeof(float4));
     l.keys = off;
-    off = align256(off + items * kItemKeep * kTileM * sizeof(unsigned long long));
+    off = align256(off + items * kFlatKeep * kTileM * sizeof(unsigned long long));
     l.counts = off;
     off = align256(off + items * kTileM * sizeof(int));
     l.thr = off;
@@ -1038,12 +1054,22 @@ __global__ void __launch_bounds__(kMergeThreads) coarse_select_kernel(CoarseArgs
     const float bound = fminf(tmin, cut);
     // exact centroid distances; every centroid takes part, as in the
     // reference's sort (no +inf filter here)
-    for (int c0 = 0; c0 < m; c0 += 32) {
-        const int c = c0 + octet;
-        const bool valid = c < m;
-        const uint32_t list = key_pos(sel_keys[valid ? c : 0]);
-        const float dist = octet_l2(q, a.centroids + static_cast<size_t>(list) * d, d, j, lane & ~7, kFullMask);
-        if (valid && j == 0) exact_keys[c] = make_key(dist, list);
+    for (int c0 = 0; c0 < m; c0 += 64) {
+        uint32_t lists[2];
+        const float *xs[2];
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 32 * kk;
+            lists[kk] = key_pos(sel_keys[c < m ? c : 0]);
+            xs[kk] = a.centroids + static_cast<size_t>(lists[kk]) * d;
+        }
+        float dist[2];
+        octet_l2n<2>(q, xs, d, j, lane & ~7, kFullMask, dist);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 32 * kk;
+            if (c < m && j == 0) exact_keys[c] = make_key(dist[kk], lists[kk]);
+        }
     }
     __syncthreads();
     // rank selection of the first P keys (keys are distinct: list ids are)
@@ -1251,15 +1277,26 @@ __global__ void __launch_bounds__(kMergeThreads) ivf_merge_kernel(IvfMergeArgs a
     // exact re-rank; the key's position is the reference's scan position
     Top8 top;
     top.init();
-    for (int c0 = 0; c0 < m; c0 += 32) {
-        const int c = c0 + octet;
-        const bool valid = c < m;
-        const uint32_t row = key_pos(sel_keys[valid ? c : 0]);
-        const float dist = octet_l2(iq, a.vectors + static_cast<size_t>(row) * d, d, j, lane & ~7, kFullMask);
-        if (valid && dist < inf) {
-            int p = 0;
-            while (p + 1 < P && !(static_cast<int32_t>(row) >= pstart[p] && static_cast<int32_t>(row) < pend[p])) ++p;
-            top.insert(make_key(dist, pbase[p] + (row - static_cast<uint32_t>(pstart[p]))));
+    for (int c0 = 0; c0 < m; c0 += 64) {
+        uint32_t rows[2];
+        const float *xs[2];
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 32 * kk;
+            rows[kk] = key_pos(sel_keys[c < m ? c : 0]);
+            xs[kk] = a.vectors + static_cast<size_t>(rows[kk]) * d;
+        }
+        float dist[2];
+        octet_l2n<2>(iq, xs, d, j, lane & ~7, kFullMask, dist);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const uint32_t row = rows[kk];
+            if (c0 + octet + 32 * kk < m && dist[kk] < inf) {
+                int p = 0;
+                while (p + 1 < P && !(static_cast<int32_t>(row) >= pstart[p] && static_cast<int32_t>(row) < pend[p]))
+                    ++p;
+                top.insert(make_key(dist[kk], pbase[p] + (row - static_cast<uint32_t>(pstart[p]))));
+            }
         }
     }
     if (j == 0)
@@ -1471,9 +1508,11 @@ void build_tc(VfrIndex *ix) {
     }
     encode_rows(&ix->tmap_vectors, ix->vectors_h, ix->d_pad, ix->n_pad, kTileN);
     if (ivf) encode_rows(&ix->tmap_centroids, ix->centroids_h, ix->d_pad, ix->nlist_pad, kTileN);
-    cuda_check(cudaFuncSetAttribute(cand_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kFlatKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kSmemTC)));
-    cuda_check(cudaFuncSetAttribute(cand_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kSmemTC)));
+    cuda_check(cudaFuncSetAttribute(cand_kernel<true, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kSmemTC)));
     cuda_check(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
     cuda_check(cudaFuncSetAttribute(coarse_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
@@ -1583,7 +1622,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     ca.out_thr = cthr;
     ca.counters = ix->counters;
     ix->prof.begin(kProfCand, stream);
-    cand_kernel<false><<<std::min(pc.segments * pc.n_qtiles, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(
+    cand_kernel<false, kIvfKeep><<<std::min(pc.segments * pc.n_qtiles, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(
         tmap_q, ix->tmap_centroids, ca);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
@@ -1650,7 +1689,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     cf.list_start = list_start;
     cf.pair_stride = static_cast<int>(pair_cap);
     ix->prof.begin(kProfCand, stream);
-    cand_kernel<true><<<ix->sm_count, kThreadsTC, kSmemTC, stream>>>(tmap_qp, ix->tmap_vectors, cf);
+    cand_kernel<true, kIvfKeep><<<ix->sm_count, kThreadsTC, kSmemTC, stream>>>(tmap_qp, ix->tmap_vectors, cf);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
 
@@ -1770,7 +1809,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     const int items = p.segments * p.n_qtiles;
     const int grid = std::min(items, ix->sm_count);
     ix->prof.begin(kProfCand, stream);
-    cand_kernel<false><<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    cand_kernel<false, kFlatKeep><<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
 
@@ -1778,7 +1817,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ma.d = ix->d;
     ma.n_qtiles = p.n_qtiles;
     ma.segments = p.segments * kHalves;  // candidate lists per frame tile
-    const int sort = (ma.segments * kItemKeep + 31) / 32 * 32;  // key slots per frame
+    const int sort = (ma.segments * kFlatKeep + 31) / 32 * 32;  // key slots per frame
     ma.sort_size = sort;
     ma.keys = keys;
     ma.counts = counts;
@@ -1842,7 +1881,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
 // synchronise the device and take driver locks (an unbounded stall inside a
 // hard deadline), or a host whose device memory budget is fixed up front.
 // Its working memory is the file-scope array below, sized for at most
-// kNoAllocMaxFrames frames of width <= kNoAllocMaxWidth (5.4 MiB, held by
+// kNoAllocMaxFrames frames of width <= kNoAllocMaxWidth (3.1 MiB, held by
 // every GPU that loads the library until the process exits).  The array's
 // device address is looked up once per device (cudaGetSymbolAddress) on the
 // first call made on that device, so that first call should come before any
@@ -1860,7 +1899,7 @@ constexpr size_t kNoAllocQ16 = 0;
 constexpr size_t kNoAllocQStats = kNoAllocQ16 + kNoAllocMaxFrames * kNoAllocMaxWidth * sizeof(__half);
 constexpr size_t kNoAllocKeys = kNoAllocQStats + kNoAllocMaxFrames * sizeof(float4);
 constexpr size_t kNoAllocLists = static_cast<size_t>(kNoAllocMaxItems) * kHalves;
-constexpr size_t kNoAllocCounts = kNoAllocKeys + kNoAllocLists * kItemKeep * kTileM * sizeof(unsigned long long);
+constexpr size_t kNoAllocCounts = kNoAllocKeys + kNoAllocLists * kFlatKeep * kTileM * sizeof(unsigned long long);
 constexpr size_t kNoAllocThr = kNoAllocCounts + kNoAllocLists * kTileM * sizeof(int);
 constexpr size_t kNoAllocList = kNoAllocThr + kNoAllocLists * kTileM * sizeof(float);
 constexpr size_t kNoAllocCount = kNoAllocList + kNoAllocMaxFrames * sizeof(int32_t);
@@ -1942,14 +1981,14 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ca.out_thr = thr;
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
-    cand_kernel<false><<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    cand_kernel<false, kFlatKeep><<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
     cuda_check(cudaGetLastError());
 
     MergeArgs ma{};
     ma.d = ix->d;
     ma.n_qtiles = p.n_qtiles;
     ma.segments = p.segments * kHalves;  // candidate lists per frame tile
-    const int sort = (ma.segments * kItemKeep + 31) / 32 * 32;  // key slots per frame
+    const int sort = (ma.segments * kFlatKeep + 31) / 32 * 32;  // key slots per frame
     ma.sort_size = sort;
     ma.keys = keys;
     ma.counts = counts;
