@@ -17,7 +17,8 @@ kernel (cand_kernel) timed with CUDA events on its stream during the timed
 steps; cpu_baseline = the CPU oracle (restatement of the reference's CPU
 retrieval) on a bounded sample of frames against the same database, all host
 cores; streaming = the c4 realtime config (Q=32 frames per block, N=100,000)
-replayed as a CUDA graph, p50/p95 per-block latency over 1,000 blocks.
+replayed as a CUDA graph, p50/p95 per-block latency over 1,000 blocks; ivf =
+the c3 IVF-Flat config (200k rows, nlist 256, 30k frames) at nprobe 1 and 8.
 
 `--impl reference` times the reference's CPU retrieval (the oracle port; the
 Rust original cannot be built here) on the same workload instead.
@@ -250,6 +251,41 @@ def streaming(device):
             "fallback_frames": diag["fallback_frames"]}
 
 
+def ivf(device):
+    """c3: IVF-Flat 200k x 768, nlist 256 (20 seeded k-means iterations), 30k
+    frames, nprobe 1 and 8; frames/s of the blend (CUDA events)."""
+    import torch
+
+    from vfr import GpuRetrievalIndex, synth
+
+    w = synth.CONFIGS["c3"]
+    arrays, queries = synth.make_torch("c3", device)
+    out = {"workload": "c3 rvc-v2-ivf-200k: IVF-Flat N=200000 x 768, nlist=256, Q=30000 frames, k=8, "
+                       "index_rate=0.75, 5 timed blends after 1 warm-up"}
+    rate = torch.tensor([w.ratio], device=device)
+    dst = torch.empty_like(queries)
+    s = torch.cuda.Stream()
+    for nprobe in w.nprobe:
+        idx = GpuRetrievalIndex.from_arrays(arrays["centroids"], arrays["offsets"], arrays["vectors"], arrays["ids"],
+                                            nprobe, max_frames=queries.shape[0])
+        torch.cuda.synchronize()
+        with torch.cuda.stream(s):
+            idx.blend_from(queries, dst, rate, stream=s)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(5):
+                idx.blend_from(queries, dst, rate, stream=s)
+            e1.record(s)
+        s.synchronize()
+        ms = e0.elapsed_time(e1) / 5
+        diag = idx.diagnostics()
+        out[f"nprobe{nprobe}"] = {"ms_per_30k_frames": ms, "frames_per_s": queries.shape[0] / (ms / 1000.0),
+                                  "exact_rerun_frames": diag["fallback_frames"] // 6,
+                                  "certified_frames": diag["candidate_frames"] // 6}
+        idx.close()
+    return out
+
+
 def main():
     a = args_parse()
     world, rank, local = dist_setup(a.gpus)
@@ -392,6 +428,7 @@ def main():
     extra = {}
     if rank == 0 and world == 1 and not a.no_streaming:
         extra["streaming"] = streaming(device)
+        extra["ivf"] = ivf(device)
     cpu = None
     if rank == 0 and world == 1 and full_host is not None:
         cpu = cpu_baseline(full_host, queries.cpu().numpy(), w.ratio, n)

@@ -37,13 +37,17 @@ constexpr int kTileM = 128;  // frames per tile: TMEM lanes
 constexpr int kTileN = 256;  // rows per MMA / accumulator
 constexpr int kTileK = 64;   // fp16 elements per 128-byte swizzled row
 constexpr int kStages = 4;
-// Candidates kept per frame per candidate list (in registers).  Flat work
-// items are random slices of the database, so a frame's neighbours spread
-// over many lists and 8 suffice; IVF lists (and the coarse centroid lists)
-// hold a frame's neighbours together and keep 16.
-constexpr int kFlatKeep = 8;
+// Candidates kept per frame per candidate list (in registers).  A list whose
+// K-th best lies close to the frame's 8th-best distance leaves the frame
+// uncertified (and re-run exactly), so the size follows how many of a
+// frame's neighbours one list can hold: short flat work items (at most
+// kShortItemTiles tiles) keep 8, long flat items and IVF lists (and the coarse
+// centroid lists) keep 16.  Fewer kept keys mean fewer insertions in the
+// epilogue.
+constexpr int kShortKeep = 8;
 constexpr int kIvfKeep = 16;
-constexpr int kItemKeep = kIvfKeep;  // largest list size (shared-memory sizing)
+constexpr int kItemKeep = kIvfKeep;  // largest list size (workspace sizing)
+constexpr int kShortItemTiles = 8;
 constexpr int kRerank = 64;     // candidates re-ranked exactly per frame (more on distance ties)
 constexpr int kRerankMax = 128;
 constexpr int kMaxSegments = 256;
@@ -513,6 +517,7 @@ __global__ void prep_queries_kernel(const float *__restrict__ q, __half *__restr
 
 // ---------------------------------------------------------------- merge
 struct MergeArgs {
+    int keep;  // keys per candidate list (kShortKeep or kIvfKeep)
     int d;
     int n_qtiles;
     int segments;
@@ -722,11 +727,11 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
         total += a.counts[o];
     }
     for (int i = tid; i < a.sort_size; i += kMergeThreads) {
-        const int s = i / kFlatKeep, slot = i % kFlatKeep;
+        const int s = i / a.keep, slot = i % a.keep;
         unsigned long long key = kEmptyKey;
         if (s < a.segments) {
             const size_t item = static_cast<size_t>(s) * a.n_qtiles + qtile;
-            if (slot < a.counts[item * kTileM + r]) key = a.keys[(item * kFlatKeep + slot) * kTileM + r];
+            if (slot < a.counts[item * kTileM + r]) key = a.keys[(item * a.keep + slot) * kTileM + r];
         }
         keys[i] = key;
     }
@@ -955,7 +960,7 @@ WsLayout ws_layout(size_t frames, int d_pad, int sms) {
     l.qstats = off;
     off = align256(off + fr * sizeof(float4));
     l.keys = off;
-    off = align256(off + items * kFlatKeep * kTileM * sizeof(unsigned long long));
+    off = align256(off + items * kItemKeep * kTileM * sizeof(unsigned long long));
     l.counts = off;
     off = align256(off + items * kTileM * sizeof(int));
     l.thr = off;
@@ -1508,7 +1513,7 @@ void build_tc(VfrIndex *ix) {
     }
     encode_rows(&ix->tmap_vectors, ix->vectors_h, ix->d_pad, ix->n_pad, kTileN);
     if (ivf) encode_rows(&ix->tmap_centroids, ix->centroids_h, ix->d_pad, ix->nlist_pad, kTileN);
-    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kFlatKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kShortKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kSmemTC)));
     cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kSmemTC)));
@@ -1809,7 +1814,10 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     const int items = p.segments * p.n_qtiles;
     const int grid = std::min(items, ix->sm_count);
     ix->prof.begin(kProfCand, stream);
-    cand_kernel<false, kFlatKeep><<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    if (p.tiles_per_seg <= kShortItemTiles)
+        cand_kernel<false, kShortKeep><<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    else
+        cand_kernel<false, kIvfKeep><<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
 
@@ -1817,7 +1825,8 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ma.d = ix->d;
     ma.n_qtiles = p.n_qtiles;
     ma.segments = p.segments * kHalves;  // candidate lists per frame tile
-    const int sort = (ma.segments * kFlatKeep + 31) / 32 * 32;  // key slots per frame
+    ma.keep = p.tiles_per_seg <= kShortItemTiles ? kShortKeep : kIvfKeep;
+    const int sort = (ma.segments * ma.keep + 31) / 32 * 32;  // key slots per frame
     ma.sort_size = sort;
     ma.keys = keys;
     ma.counts = counts;
@@ -1881,7 +1890,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
 // synchronise the device and take driver locks (an unbounded stall inside a
 // hard deadline), or a host whose device memory budget is fixed up front.
 // Its working memory is the file-scope array below, sized for at most
-// kNoAllocMaxFrames frames of width <= kNoAllocMaxWidth (3.1 MiB, held by
+// kNoAllocMaxFrames frames of width <= kNoAllocMaxWidth (5.4 MiB, held by
 // every GPU that loads the library until the process exits).  The array's
 // device address is looked up once per device (cudaGetSymbolAddress) on the
 // first call made on that device, so that first call should come before any
@@ -1899,7 +1908,7 @@ constexpr size_t kNoAllocQ16 = 0;
 constexpr size_t kNoAllocQStats = kNoAllocQ16 + kNoAllocMaxFrames * kNoAllocMaxWidth * sizeof(__half);
 constexpr size_t kNoAllocKeys = kNoAllocQStats + kNoAllocMaxFrames * sizeof(float4);
 constexpr size_t kNoAllocLists = static_cast<size_t>(kNoAllocMaxItems) * kHalves;
-constexpr size_t kNoAllocCounts = kNoAllocKeys + kNoAllocLists * kFlatKeep * kTileM * sizeof(unsigned long long);
+constexpr size_t kNoAllocCounts = kNoAllocKeys + kNoAllocLists * kItemKeep * kTileM * sizeof(unsigned long long);
 constexpr size_t kNoAllocThr = kNoAllocCounts + kNoAllocLists * kTileM * sizeof(int);
 constexpr size_t kNoAllocList = kNoAllocThr + kNoAllocLists * kTileM * sizeof(float);
 constexpr size_t kNoAllocCount = kNoAllocList + kNoAllocMaxFrames * sizeof(int32_t);
@@ -1981,14 +1990,18 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ca.out_thr = thr;
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
-    cand_kernel<false, kFlatKeep><<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    if (p.tiles_per_seg <= kShortItemTiles)
+        cand_kernel<false, kShortKeep><<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
+    else
+        cand_kernel<false, kIvfKeep><<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
     cuda_check(cudaGetLastError());
 
     MergeArgs ma{};
     ma.d = ix->d;
     ma.n_qtiles = p.n_qtiles;
     ma.segments = p.segments * kHalves;  // candidate lists per frame tile
-    const int sort = (ma.segments * kFlatKeep + 31) / 32 * 32;  // key slots per frame
+    ma.keep = p.tiles_per_seg <= kShortItemTiles ? kShortKeep : kIvfKeep;
+    const int sort = (ma.segments * ma.keep + 31) / 32 * 32;  // key slots per frame
     ma.sort_size = sort;
     ma.keys = keys;
     ma.counts = counts;
