@@ -97,7 +97,12 @@ __device__ __forceinline__ void octet_l2n(const float *__restrict__ q, const flo
     float acc[N];
 #pragma unroll
     for (int k = 0; k < N; ++k) acc[k] = 0.0f;
-#pragma unroll 4
+    // Each unrolled body issues all its row loads before the dependent adds,
+    // so the number of serialised memory round trips is d/8 / unroll: deep
+    // for the few-row re-ranks (random rows, latency bound), shallower for
+    // the 4-row scans (register bound).
+    constexpr int kUnroll = N <= 2 ? 16 : 4;
+#pragma unroll kUnroll
     for (int i = j; i < d8; i += 8) {
         const float qi = q[i];
 #pragma unroll
