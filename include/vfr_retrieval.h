@@ -167,7 +167,7 @@ VFR_API size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t len
  * library.  Same arguments, checks and results as vocal_faiss_gpu_blend, for
  * an index with the tensor-core layout (flat, engine auto or tensor), at most
  * 256 frames per call and feature width up to 1024.  Its working memory is a
- * 5.4 MiB static device array that every GPU loading the library holds until
+ * 5.3 MiB static device array that every GPU loading the library holds until
  * exit; the first call on a device looks up that array's address, so make it
  * before any stream capture.  All calls share the array: calls whose kernels
  * overlap on the GPU race and must be serialised by the caller. */

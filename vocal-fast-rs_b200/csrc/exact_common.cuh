@@ -89,8 +89,10 @@ __device__ __forceinline__ float octet_l2(const float *__restrict__ q, const flo
 
 // octet_l2 for N rows at once: N independent accumulation chains per lane
 // (each in the reference order), so N times as many row loads are in flight.
-// out[k] is the distance to x[k]; all 8 threads get the same values.
-template <int N>
+// out[k] is the distance to x[k]; all 8 threads get the same values.  Rows
+// in global memory go through the read-only cache (kGlobal); kGlobal = false
+// reads rows staged in shared memory.
+template <int N, bool kGlobal = true>
 __device__ __forceinline__ void octet_l2n(const float *__restrict__ q, const float *const (&x)[N], int d, int j,
                                           int octet_base, unsigned mask, float (&out)[N]) {
     const int d8 = d & ~7;
@@ -107,7 +109,7 @@ __device__ __forceinline__ void octet_l2n(const float *__restrict__ q, const flo
         const float qi = q[i];
 #pragma unroll
         for (int k = 0; k < N; ++k) {
-            const float t = __fsub_rn(qi, __ldg(x[k] + i));
+            const float t = __fsub_rn(qi, kGlobal ? __ldg(x[k] + i) : x[k][i]);
             acc[k] = __fadd_rn(acc[k], __fmul_rn(t, t));
         }
     }
@@ -118,11 +120,18 @@ __device__ __forceinline__ void octet_l2n(const float *__restrict__ q, const flo
         for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(mask, acc[k], octet_base + l));
         float tail = -0.0f;
         for (int i = d8; i < d; ++i) {
-            const float t = __fsub_rn(q[i], __ldg(x[k] + i));
+            const float t = __fsub_rn(q[i], kGlobal ? __ldg(x[k] + i) : x[k][i]);
             tail = __fadd_rn(tail, __fmul_rn(t, t));
         }
         out[k] = __fadd_rn(s, tail);
     }
+}
+
+// The reference's f64 weight of one neighbour at squared distance `dist`.
+__device__ __forceinline__ double reference_weight(float dist) {
+    const float s = fmaxf(dist, 1e-12f);  // f32::max: NaN yields the other operand
+    const double sd = static_cast<double>(s);
+    return __ddiv_rn(1.0, __dmul_rn(sd, sd));
 }
 
 // The reference's f64 weights for `count` neighbours; returns S.
@@ -130,12 +139,7 @@ __device__ __forceinline__ double reference_weights(const float *dist, int count
     double sum = -0.0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        double wk = 0.0;
-        if (k < count) {
-            float s = fmaxf(dist[k], 1e-12f);  // f32::max: NaN yields the other operand
-            double sd = static_cast<double>(s);
-            wk = __ddiv_rn(1.0, __dmul_rn(sd, sd));
-        }
+        const double wk = k < count ? reference_weight(dist[k]) : 0.0;
         w[k] = wk;
         sum = __dadd_rn(sum, wk);
     }
@@ -147,9 +151,12 @@ __device__ __forceinline__ double reference_weights(const float *dist, int count
 __device__ __forceinline__ float reference_blend_element(float q, const float *v, const double *w, double sum,
                                                          int count, float ratio) {
     double acc = -0.0;
-    for (int k = 0; k < count; ++k) {
-        double t = __dmul_rn(static_cast<double>(v[k]), w[k]);
-        acc = __dadd_rn(acc, __ddiv_rn(t, sum));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        if (k < count) {
+            const double t = __dmul_rn(static_cast<double>(v[k]), w[k]);
+            acc = __dadd_rn(acc, __ddiv_rn(t, sum));
+        }
     }
     float retrieved = __double2float_rn(acc);
     return __fadd_rn(__fmul_rn(q, __fsub_rn(1.0f, ratio)), __fmul_rn(retrieved, ratio));

@@ -73,9 +73,14 @@ struct CandArgs {
     int64_t seg_rows;
     const float *row_norms;
     float coef;  // -2 / s^2
-    unsigned long long *out_keys;  // [list][kItemKeep][128], list = (seg * kHalves + half) * n_qtiles + qtile
-    int *out_count;                // [list][128]
-    float *out_thr;                // [list][128]
+    // flat: keys [frame][lists][K] and thresholds [frame][thr_stride], list =
+    // seg * kHalves + half, so a frame's candidates are one contiguous block;
+    // IVF fine stage: keys [half][K][pair], counts and thresholds [half][pair]
+    unsigned long long *out_keys;
+    int *out_count;  // IVF only
+    float *out_thr;
+    int lists;       // flat: candidate lists per frame (segments * kHalves)
+    int thr_stride;  // flat: lists rounded up to a multiple of 4 (16-byte rows)
     DeviceCounters *counters;
     // IVF fine stage only: work items (list, frame tile within the list's
     // pairs) from a device table; A rows are the (frame, probe) pairs of the
@@ -468,14 +473,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     a.out_count[half * stride + pos] = cnt;
                     a.out_thr[half * stride + pos] = cnt == K ? top.dist[K - 1] : inf;
                 }
-            } else {
-                const size_t list = (static_cast<size_t>(it.seg) * kHalves + half) * a.n_qtiles + item % a.n_qtiles;
-                const size_t o = list * kTileM + r;
+            } else if (r < it.a_rows) {
+                // every slot is written (kEmptyKey past cnt), so the merge
+                // copies a frame's block without reading counts
+                const size_t frame = static_cast<size_t>(it.a_row0) + r;
+                const int list = it.seg * kHalves + half;
+                ulonglong2 *dk = reinterpret_cast<ulonglong2 *>(a.out_keys + (frame * a.lists + list) * K);
 #pragma unroll
-                for (int i = 0; i < K; ++i)
-                    if (i < cnt) a.out_keys[(list * K + i) * kTileM + r] = make_key(top.dist[i], top.row[i]);
-                a.out_count[o] = cnt;
-                a.out_thr[o] = cnt == K ? top.dist[K - 1] : inf;
+                for (int i = 0; i < K; i += 2)
+                    dk[i / 2] = make_ulonglong2(i < cnt ? make_key(top.dist[i], top.row[i]) : kEmptyKey,
+                                                i + 1 < cnt ? make_key(top.dist[i + 1], top.row[i + 1]) : kEmptyKey);
+                a.out_thr[frame * a.thr_stride + list] = cnt == K ? top.dist[K - 1] : inf;
             }
         }
     }
@@ -495,6 +503,7 @@ __global__ void prep_queries_kernel(const float *__restrict__ q, __half *__restr
     if (f >= frames) return;
     const float inv = 1.0f / scale;  // exact: scale is a power of two
     float qn2 = 0.f, hat2 = 0.f, res2 = 0.f;
+#pragma unroll 8
     for (int k = lane; k < d_pad; k += 32) {
         float v = k < d ? q[f * d + k] : 0.f;
         float sv = fminf(fmaxf(v * scale, -65504.f), 65504.f);
@@ -519,12 +528,11 @@ __global__ void prep_queries_kernel(const float *__restrict__ q, __half *__restr
 struct MergeArgs {
     int keep;  // keys per candidate list (kShortKeep or kIvfKeep)
     int d;
-    int n_qtiles;
-    int segments;
-    int sort_size;  // key slots per frame: segments * kItemKeep rounded up to 32
-    const unsigned long long *keys;
-    const int *counts;
-    const float *thr;
+    int lists;       // candidate lists per frame
+    int thr_stride;  // thresholds per frame row (lists rounded up to 4)
+    int sort_size;   // key slots per frame: lists * keep rounded up to 32
+    const unsigned long long *keys;  // [frame][lists][keep]
+    const float *thr;                // [frame][thr_stride]
     const float4 *qstats;
     const float *queries;
     float *out;
@@ -543,6 +551,7 @@ struct MergeArgs {
     int32_t *fallback_list;
     int32_t *fallback_count;
     DeviceCounters *counters;
+    int stage_rows;  // re-rank rows staged in shared memory per chunk (0: read them from global memory)
 };
 
 constexpr int kMergeThreads = 256;
@@ -551,106 +560,174 @@ constexpr int kMergeThreads = 256;
 // Shared state of select_rerank (one per CTA, in shared memory).
 struct SelectState {
     unsigned int hist[256];
-    uint32_t prefix, rank;
+    uint32_t bin, below_bin, in_bin;
+    uint32_t dropped_min;
     int count;
     float red_f[kMergeThreads / 32];
     int red_i[kMergeThreads / 32];
+    uint32_t red_lo[kMergeThreads / 32], red_hi[kMergeThreads / 32];
 };
 
-// Block-wide min of `tmin` and sum of `total` (all threads get the result).
-__device__ __forceinline__ void block_min_sum(float &tmin, int &total, SelectState &st) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) {
-        tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, s));
-        total += __shfl_xor_sync(kFullMask, total, s);
-    }
-    if (lane == 0) {
-        st.red_f[warp] = tmin;
-        st.red_i[warp] = total;
-    }
-    __syncthreads();
-    tmin = __int_as_float(0x7f800000);
-    total = 0;
-    for (int w = 0; w < kMergeThreads / 32; ++w) {
-        tmin = fminf(tmin, st.red_f[w]);
-        total += st.red_i[w];
-    }
-}
+// The real keys among a CTA's key slots: how many, and the smallest and
+// largest distance bits; plus the block-wide min of each thread's `tmin`.
+struct KeyStats {
+    int total;
+    uint32_t lo, hi;
+    float tmin;
+};
 
-// Chooses the keys to re-rank among keys[0 .. slots) (total real keys, the
-// rest kEmptyKey) without sorting them: radix-select (4 passes of 8 bits over
-// the distance bits) the kRerank-th smallest distance V, then keep every key
-// whose distance bits are <= V.  Every dropped key has a larger approximate
-// distance, so V's distance bounds them for the certificate.  Ties at V can
-// push the set past kRerank; up to kRerankMax are kept and `too_many` reports
-// an overflow.  Returns the number of keys written to sel_keys; `bound` is the
-// distance every dropped key reaches or exceeds (+inf when none is dropped).
-// Called by every thread of the CTA.
-__device__ int select_rerank(const unsigned long long *keys, int slots, int total, unsigned long long *sel_keys,
-                             SelectState &st, float &bound, bool &too_many) {
+// Block-wide KeyStats over keys[0 .. slots) (in shared memory); every thread
+// of the CTA calls it and gets the result.  Its barrier also publishes the
+// shared-memory writes made before the call.
+__device__ KeyStats key_stats(const unsigned long long *keys, int slots, float tmin, SelectState &st) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) {
-        st.prefix = 0u;
-        st.rank = kRerank;
-        st.count = 0;
-    }
-    __syncthreads();
-    uint32_t vbits = 0xffffffffu;  // all keys when nothing needs dropping
-    if (total > kRerank) {
-        uint32_t mask_bits = 0;
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            st.hist[tid] = 0;
-            __syncthreads();
-            const uint32_t prefix = st.prefix;
-            for (int i = tid; i < slots; i += kMergeThreads) {
-                const unsigned long long key = keys[i];
-                const uint32_t bits = static_cast<uint32_t>(key >> 32);
-                if (key != kEmptyKey && (bits & mask_bits) == prefix) atomicAdd(&st.hist[(bits >> shift) & 255u], 1u);
-            }
-            __syncthreads();
-            if (warp == 0) {
-                uint32_t c[8], sum = 0;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    c[k] = st.hist[lane * 8 + k];
-                    sum += c[k];
-                }
-                uint32_t incl = sum;
-#pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                    const uint32_t up = __shfl_up_sync(kFullMask, incl, off);
-                    if (lane >= off) incl += up;
-                }
-                const uint32_t want = st.rank;
-                uint32_t acc = incl - sum;
-                if (acc < want && want <= incl) {
-                    for (int k = 0; k < 8; ++k) {
-                        if (acc + c[k] >= want) {
-                            st.rank = want - acc;
-                            st.prefix = prefix | (static_cast<uint32_t>(lane * 8 + k) << shift);
-                            break;
-                        }
-                        acc += c[k];
-                    }
-                }
-            }
-            mask_bits |= 0xffu << shift;
-            __syncthreads();
-        }
-        vbits = st.prefix;
-    }
+    KeyStats ks{0, 0xffffffffu, 0u, tmin};
     for (int i = tid; i < slots; i += kMergeThreads) {
         const unsigned long long key = keys[i];
-        if (key != kEmptyKey && static_cast<uint32_t>(key >> 32) <= vbits) {
-            const int pos = atomicAdd(&st.count, 1);
-            if (pos < kRerankMax) sel_keys[pos] = key;
+        if (key != kEmptyKey) {
+            const uint32_t b = static_cast<uint32_t>(key >> 32);
+            ks.lo = min(ks.lo, b);
+            ks.hi = max(ks.hi, b);
+            ++ks.total;
         }
     }
+    ks.total = __reduce_add_sync(kFullMask, ks.total);
+    ks.lo = __reduce_min_sync(kFullMask, ks.lo);
+    ks.hi = __reduce_max_sync(kFullMask, ks.hi);
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) ks.tmin = fminf(ks.tmin, __shfl_xor_sync(kFullMask, ks.tmin, s));
+    if (lane == 0) {
+        st.red_i[warp] = ks.total;
+        st.red_lo[warp] = ks.lo;
+        st.red_hi[warp] = ks.hi;
+        st.red_f[warp] = ks.tmin;
+    }
+    __syncthreads();
+    ks = KeyStats{0, 0xffffffffu, 0u, __int_as_float(0x7f800000)};
+    for (int w = 0; w < kMergeThreads / 32; ++w) {
+        ks.total += st.red_i[w];
+        ks.lo = min(ks.lo, st.red_lo[w]);
+        ks.hi = max(ks.hi, st.red_hi[w]);
+        ks.tmin = fminf(ks.tmin, st.red_f[w]);
+    }
+    return ks;
+}
+
+// Keys kept for the exact re-rank when a radix pass can stop early: the pass
+// stops once the keys at or below the bin holding the kRerank-th smallest
+// distance number at most this many.
+constexpr int kRerankStop = 80;
+
+// Chooses the keys to re-rank among keys[0 .. slots) (ks from key_stats; the
+// slots past the real keys hold kEmptyKey; slots a multiple of 32) without
+// sorting them.  A radix
+// select over the distance bits below the real keys' common prefix finds the
+// digit bin holding the kRerank-th smallest distance; it refines that bin with
+// further 8-bit digits only while the keys at or below it number more than
+// kRerankStop.  Every key at or below the final bin is kept (kRerank to
+// kRerankStop keys, or up to kRerankMax when distances tie in every bit, with
+// `too_many` reporting an overflow past kRerankMax).  Every dropped key has a
+// larger approximate distance than every kept one; `bound` is the smallest
+// dropped distance (+inf when nothing is dropped).  Histogram updates are
+// aggregated per warp (match_any), so a crowded digit costs one shared atomic
+// per warp.  Returns the number of keys written to sel_keys.  Called by every
+// thread of the CTA.
+__device__ int select_rerank(const unsigned long long *keys, int slots, const KeyStats &ks,
+                             unsigned long long *sel_keys, SelectState &st, float &bound, bool &too_many) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int total = ks.total;
+    const uint32_t lo = ks.lo, hi = ks.hi;
+    uint32_t limit = 0xffffffffu;  // keep every real key whose distance bits are <= limit
+    if (total > kRerank) {
+        if (lo == hi) {
+            limit = lo;  // every real key has the same distance
+        } else {
+            int top = 31 - __clz(lo ^ hi);               // highest bit in which the keys differ
+            uint32_t mask_bits = ~((2u << top) - 1u);    // the common prefix (0 when top == 31)
+            uint32_t prefix = lo & mask_bits;
+            uint32_t rank = kRerank, below = 0;          // 1-based rank inside the prefix group
+            while (true) {
+                const int shift = top > 7 ? top - 7 : 0;
+                const uint32_t digits = (2u << (top - shift)) - 1u;
+                st.hist[tid] = 0u;
+                __syncthreads();
+                for (int i = tid; i < slots; i += kMergeThreads) {
+                    const unsigned long long key = keys[i];
+                    const uint32_t b = static_cast<uint32_t>(key >> 32);
+                    const bool in = key != kEmptyKey && (b & mask_bits) == prefix;
+                    const uint32_t digit = in ? (b >> shift) & digits : 0xffffffffu;
+                    const unsigned peers = __match_any_sync(kFullMask, digit);
+                    if (in && lane == __ffs(peers) - 1) atomicAdd(&st.hist[digit], __popc(peers));
+                }
+                __syncthreads();
+                if (warp == 0) {
+                    uint32_t c[8], sum = 0;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        c[k] = st.hist[lane * 8 + k];
+                        sum += c[k];
+                    }
+                    uint32_t incl = sum;
+#pragma unroll
+                    for (int off = 1; off < 32; off <<= 1) {
+                        const uint32_t up = __shfl_up_sync(kFullMask, incl, off);
+                        if (lane >= off) incl += up;
+                    }
+                    uint32_t acc = incl - sum;
+                    if (lane == 31 && incl < rank) {  // cannot happen: `total` counts the real keys
+                        st.bin = digits;
+                        st.below_bin = 0u;
+                        st.in_bin = kRerankMax + 1u;
+                    }
+                    if (acc < rank && rank <= incl) {
+                        for (int k = 0; k < 8; ++k) {
+                            if (acc + c[k] >= rank) {
+                                st.bin = static_cast<uint32_t>(lane * 8 + k);
+                                st.below_bin = acc;
+                                st.in_bin = c[k];
+                                break;
+                            }
+                            acc += c[k];
+                        }
+                    }
+                }
+                __syncthreads();
+                const uint32_t bin = st.bin, acc = st.below_bin, cnt = st.in_bin;
+                if (below + acc + cnt <= static_cast<uint32_t>(kRerankStop) || shift == 0) {
+                    limit = prefix | (bin << shift) | ((1u << shift) - 1u);
+                    break;
+                }
+                below += acc;
+                rank -= acc;
+                prefix |= bin << shift;
+                mask_bits |= digits << shift;
+                top = shift - 1;
+            }
+        }
+    }
+    if (tid == 0) {
+        st.count = 0;
+        st.dropped_min = 0xffffffffu;
+    }
+    __syncthreads();
+    uint32_t dropped = 0xffffffffu;
+    for (int i = tid; i < slots; i += kMergeThreads) {
+        const unsigned long long key = keys[i];
+        if (key == kEmptyKey) continue;
+        const uint32_t b = static_cast<uint32_t>(key >> 32);
+        if (b <= limit) {
+            const int pos = atomicAdd(&st.count, 1);
+            if (pos < kRerankMax) sel_keys[pos] = key;
+        } else {
+            dropped = min(dropped, b);
+        }
+    }
+    dropped = __reduce_min_sync(kFullMask, dropped);
+    if (lane == 0 && dropped != 0xffffffffu) atomicMin(&st.dropped_min, dropped);
     __syncthreads();
     const int selected = st.count;
     too_many = selected > kRerankMax;
-    bound = selected < total ? from_total_order_bits(vbits) : __int_as_float(0x7f800000);
+    bound = st.dropped_min != 0xffffffffu ? from_total_order_bits(st.dropped_min) : __int_as_float(0x7f800000);
     return selected < kRerankMax ? selected : kRerankMax;
 }
 
@@ -688,100 +765,194 @@ __device__ __forceinline__ bool certify(float bound, float dk, float4 qs, float 
     return lower > dk * (1.f + 4.f * exact_rel) + 1e-30f;
 }
 
+// Shared-memory row stride of the staged re-rank rows, in floats: 8 floats
+// of padding put the 4 rows a warp reads at once on different banks.
+__host__ __device__ constexpr int stage_stride(int d) { return d + 8; }
+
+// Dynamic shared memory of merge_kernel: key slots, thresholds, the query
+// row and the re-rank stage, each 16-byte aligned.
+struct MergeSmem {
+    size_t keys, thr, q, stage, total;
+};
+__host__ __device__ inline MergeSmem merge_smem(int sort_size, int thr_stride, int d, int stage_rows) {
+    MergeSmem m{};
+    m.keys = 0;
+    m.thr = static_cast<size_t>(sort_size) * 8;
+    m.q = m.thr + static_cast<size_t>(thr_stride) * 4;
+    m.stage = m.q + static_cast<size_t>((d + 3) & ~3) * 4;
+    m.total = m.stage + static_cast<size_t>(stage_rows) * stage_stride(d) * 4;
+    return m;
+}
+
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
     extern __shared__ __align__(16) uint8_t msm[];
-    unsigned long long *keys = reinterpret_cast<unsigned long long *>(msm);
-    float *q = reinterpret_cast<float *>(msm + static_cast<size_t>(a.sort_size) * 8);
+    const MergeSmem lay = merge_smem(a.sort_size, a.thr_stride, a.d, a.stage_rows);
+    unsigned long long *keys = reinterpret_cast<unsigned long long *>(msm + lay.keys);
+    float *thr = reinterpret_cast<float *>(msm + lay.thr);
+    float *q = reinterpret_cast<float *>(msm + lay.q);
+    float *stage = reinterpret_cast<float *>(msm + lay.stage);
     __shared__ unsigned long long octet_best[32 * 8];
     __shared__ unsigned long long best[8];
     __shared__ int certified_s;
     __shared__ SelectState sel;
     __shared__ unsigned long long sel_keys[kRerankMax];
     __shared__ double weights[8];
-    __shared__ double weight_sum;
+    __shared__ int best_slot[8];
+    __shared__ __align__(8) uint64_t gather_bar;
+    __shared__ __align__(8) uint64_t stage_bar;
 
     const int tid = threadIdx.x, lane = tid & 31, octet = tid >> 3, j = tid & 7;
     const long long frame = blockIdx.x;
-    const int qtile = static_cast<int>(frame / kTileM), r = static_cast<int>(frame % kTileM);
     const int d = a.d;
     const float *src = a.queries + frame * d;
     float *dst = a.out + frame * d;
     const float inf = __int_as_float(0x7f800000);
+    const int real_slots = a.lists * a.keep;
 
-    float ratio = 1.f;
-    if (a.mode == kModeBlend) {
-        ratio = load_ratio(a.index_rate);
-        if (!(ratio > 0.f)) {
-            if (dst != src)
-                for (int i = tid; i < d; i += kMergeThreads) dst[i] = src[i];
-            return;
-        }
+    // the frame's candidate block (keys, then thresholds) arrives by two bulk
+    // copies while the threads load the query row and pad the key slots
+    if (tid == 0) {
+        tc::mbar_init(&gather_bar, 1);
+        tc::mbar_init(&stage_bar, 1);
+        tc::fence_mbarrier_init();
+        const uint32_t kbytes = static_cast<uint32_t>(real_slots) * 8;
+        const uint32_t tbytes = static_cast<uint32_t>(a.thr_stride) * 4;
+        tc::mbar_arrive_expect_tx(&gather_bar, kbytes + tbytes);
+        tc::bulk_load(keys, a.keys + static_cast<size_t>(frame) * real_slots, kbytes, &gather_bar);
+        tc::bulk_load(thr, a.thr + static_cast<size_t>(frame) * a.thr_stride, tbytes, &gather_bar);
     }
+    const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
+    for (int i = real_slots + tid; i < a.sort_size; i += kMergeThreads) keys[i] = kEmptyKey;
     for (int i = tid; i < d; i += kMergeThreads) q[i] = src[i];
-    // gather the items' candidate keys for this frame
-    float tmin = inf;
-    int total = 0;
-    for (int s = tid; s < a.segments; s += kMergeThreads) {
-        const size_t o = (static_cast<size_t>(s) * a.n_qtiles + qtile) * kTileM + r;
-        tmin = fminf(tmin, a.thr[o]);
-        total += a.counts[o];
-    }
-    for (int i = tid; i < a.sort_size; i += kMergeThreads) {
-        const int s = i / a.keep, slot = i % a.keep;
-        unsigned long long key = kEmptyKey;
-        if (s < a.segments) {
-            const size_t item = static_cast<size_t>(s) * a.n_qtiles + qtile;
-            if (slot < a.counts[item * kTileM + r]) key = a.keys[(item * a.keep + slot) * kTileM + r];
+    __syncthreads();  // barrier initialisation is visible before anyone waits on it
+    const bool landed = tc::mbar_wait(&gather_bar, 0, kWaitLimitNs);
+    if (__syncthreads_or(!landed)) {
+        // the copy never completed: give it one more bounded wait before the
+        // shared memory is released, and hand the frame to the exact re-run
+        tc::mbar_wait(&gather_bar, 0, kWaitLimitNs);
+        if (tid == 0) {
+            if (a.counters) atomicAdd(&a.counters->timeouts, 1ull);
+            const int pos = atomicAdd(a.fallback_count, 1);
+            a.fallback_list[pos] = static_cast<int32_t>(frame);
         }
-        keys[i] = key;
+        return;
     }
-    block_min_sum(tmin, total, sel);
+    if (a.mode == kModeBlend && !(ratio > 0.f)) {
+        if (dst != src)
+            for (int i = tid; i < d; i += kMergeThreads) dst[i] = q[i];
+        return;
+    }
+    float tmin = inf;
+    for (int s = tid; s < a.lists; s += kMergeThreads) tmin = fminf(tmin, thr[s]);
+    const KeyStats ks = key_stats(keys, a.sort_size, tmin, sel);
     float cut;
     bool too_many_ties;
-    const int m = select_rerank(keys, a.sort_size, total, sel_keys, sel, cut, too_many_ties);
-    const float t_final = fminf(tmin, cut);
+    const int m = select_rerank(keys, a.sort_size, ks, sel_keys, sel, cut, too_many_ties);
+    const float t_final = fminf(ks.tmin, cut);
 
     // exact re-rank in the reference order; flat scan position == row
     Top8 top;
     top.init();
-    for (int c0 = 0; c0 < m; c0 += 64) {
-        uint32_t rows[2];
-        const float *xs[2];
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-            const int c = c0 + octet + 32 * kk;
-            rows[kk] = key_pos(sel_keys[c < m ? c : 0]);
-            xs[kk] = a.vectors + static_cast<size_t>(rows[kk]) * d;
+    bool stage_timeout = false;
+    if (a.stage_rows > 0) {
+        // the chunk's rows arrive by bulk copies into shared memory, all in
+        // flight at once, then the octets read them from there
+        const int stride = stage_stride(d);
+        uint32_t phase = 0;
+        for (int c0 = 0; c0 < m; c0 += a.stage_rows) {
+            const int rows_n = min(a.stage_rows, m - c0);
+            if ((tid >> 5) == 0) {
+                if (lane == 0) tc::mbar_arrive_expect_tx(&stage_bar, static_cast<uint32_t>(rows_n * d * 4));
+                __syncwarp();
+                for (int i = lane; i < rows_n; i += 32)
+                    tc::bulk_load(stage + i * stride, a.vectors + static_cast<size_t>(key_pos(sel_keys[c0 + i])) * d,
+                                  static_cast<uint32_t>(d * 4), &stage_bar);
+            }
+            const bool arrived = tc::mbar_wait(&stage_bar, phase, kWaitLimitNs);
+            phase ^= 1u;
+            if (__syncthreads_or(!arrived)) {
+                stage_timeout = true;
+                break;
+            }
+            // warp-uniform trip count: every octet takes part in the shuffles
+            for (int cb = 0; cb < rows_n; cb += 64) {
+                const int c = cb + octet, c2 = c + 32;
+                const float *xs[2] = {stage + (c < rows_n ? c : 0) * stride, stage + (c2 < rows_n ? c2 : 0) * stride};
+                float dist[2];
+                octet_l2n<2, false>(q, xs, d, j, lane & ~7, kFullMask, dist);
+                if (c < rows_n && dist[0] < inf) top.insert(make_key(dist[0], key_pos(sel_keys[c0 + c])));
+                if (c2 < rows_n && dist[1] < inf) top.insert(make_key(dist[1], key_pos(sel_keys[c0 + c2])));
+            }
+            __syncthreads();  // the next chunk overwrites the stage
         }
-        float dist[2];
-        octet_l2n<2>(q, xs, d, j, lane & ~7, kFullMask, dist);
+        if (stage_timeout) {
+            // a copy that never completed: let the copies in flight land
+            // (bounded) before the CTA's shared memory is released, and hand
+            // the frame to the exact re-run
+            tc::mbar_wait(&stage_bar, phase ^ 1u, kWaitLimitNs);
+            if (tid == 0) {
+                if (a.counters) atomicAdd(&a.counters->timeouts, 1ull);
+                const int pos = atomicAdd(a.fallback_count, 1);
+                a.fallback_list[pos] = static_cast<int32_t>(frame);
+            }
+            return;
+        }
+    } else {
+        for (int c0 = 0; c0 < m; c0 += 64) {
+            uint32_t rows[2];
+            const float *xs[2];
 #pragma unroll
-        for (int kk = 0; kk < 2; ++kk)
-            if (c0 + octet + 32 * kk < m && dist[kk] < inf) top.insert(make_key(dist[kk], rows[kk]));
+            for (int kk = 0; kk < 2; ++kk) {
+                const int c = c0 + octet + 32 * kk;
+                rows[kk] = key_pos(sel_keys[c < m ? c : 0]);
+                xs[kk] = a.vectors + static_cast<size_t>(rows[kk]) * d;
+            }
+            float dist[2];
+            octet_l2n<2>(q, xs, d, j, lane & ~7, kFullMask, dist);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+                if (c0 + octet + 32 * kk < m && dist[kk] < inf) top.insert(make_key(dist[kk], rows[kk]));
+        }
     }
     if (j == 0)
 #pragma unroll
         for (int i = 0; i < 8; ++i) octet_best[octet * 8 + i] = top.k[i];
     __syncthreads();
     merge_octet_lists(octet_best, best);
-    if (tid == 0) {
-        int count = 0;
-        while (count < 8 && best[count] != kEmptyKey) ++count;
+    int count = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) count += best[i] != kEmptyKey;
+    // in parallel: the certificate (thread 32), the neighbour weights
+    // (threads 0-7, one each) and, when the whole re-rank set is still
+    // staged, where each neighbour's row sits in the stage (warp w finds
+    // neighbour w)
+    const bool staged_all = a.stage_rows > 0 && m <= a.stage_rows;
+    if (tid == 32) {
         const float d8 = count == 8 ? key_dist(best[7]) : inf;
         const bool ok = !too_many_ties && certify(t_final, d8, a.qstats[frame], a.max_norm, a.max_hat,
                                                   a.max_residual, a.acc_rel, a.norm_rel, a.exact_rel);
-        certified_s = ok ? count + 1 : 0;  // 0 = not certified, else count + 1
+        certified_s = ok ? 1 : 0;
+    }
+    if (tid < 8) weights[tid] = tid < count ? reference_weight(key_dist(best[tid])) : 0.0;
+    if (staged_all && a.mode == kModeBlend) {
+        const int w = tid >> 5;
+        if (w < count) {
+            const uint32_t row = key_pos(best[w]);
+            int found = -1;
+            for (int c = lane; c < m; c += 32)
+                if (key_pos(sel_keys[c]) == row) found = c;
+            found = __reduce_max_sync(kFullMask, found);
+            if (lane == 0) best_slot[w] = found;
+        }
     }
     __syncthreads();
-    const int cert = certified_s;
-    if (cert == 0) {
+    if (certified_s == 0) {
         if (tid == 0) {
             const int pos = atomicAdd(a.fallback_count, 1);
             a.fallback_list[pos] = static_cast<int32_t>(frame);
         }
         return;
     }
-    const int count = cert - 1;
     if (tid == 0 && a.counters) atomicAdd(&a.counters->candidate_frames, 1ull);
     if (a.mode == kModeSearch) {
         if (tid < a.k) {
@@ -798,30 +969,35 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
             for (int i = tid; i < d; i += kMergeThreads) dst[i] = q[i];
         return;
     }
-    if (tid == 0) {
-        float dist[8];
-        double w[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) dist[i] = key_dist(best[i]);
-        weight_sum = reference_weights(dist, count, w);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) weights[i] = w[i];
-    }
-    __syncthreads();
     double w[8];
-    uint32_t rows[8];
+    double sum = -0.0;  // the reference's order: S = w0 + w1 + ... (zeros past count)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         w[i] = weights[i];
-        rows[i] = key_pos(best[i]);
+        sum = __dadd_rn(sum, w[i]);
     }
-    const double sum = weight_sum;
-    for (int i = tid; i < d; i += kMergeThreads) {
-        float v[8];
+    if (staged_all) {
+        const float *vrow[8];
+        const int stride = stage_stride(d);
 #pragma unroll
-        for (int kq = 0; kq < 8; ++kq)
-            v[kq] = kq < count ? __ldg(a.vectors + static_cast<size_t>(rows[kq]) * d + i) : 0.f;
-        dst[i] = reference_blend_element(q[i], v, w, sum, count, ratio);
+        for (int kq = 0; kq < 8; ++kq) vrow[kq] = stage + (kq < count ? best_slot[kq] : 0) * stride;
+        for (int i = tid; i < d; i += kMergeThreads) {
+            float v[8];
+#pragma unroll
+            for (int kq = 0; kq < 8; ++kq) v[kq] = vrow[kq][i];
+            dst[i] = reference_blend_element(q[i], v, w, sum, count, ratio);
+        }
+    } else {
+        uint32_t rows[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rows[i] = key_pos(best[i]);
+        for (int i = tid; i < d; i += kMergeThreads) {
+            float v[8];
+#pragma unroll
+            for (int kq = 0; kq < 8; ++kq)
+                v[kq] = kq < count ? __ldg(a.vectors + static_cast<size_t>(rows[kq]) * d + i) : 0.f;
+            dst[i] = reference_blend_element(q[i], v, w, sum, count, ratio);
+        }
     }
 }
 
@@ -916,6 +1092,29 @@ struct Plan {
     int n_qtiles, segments, tiles_per_seg;
 };
 
+// Launches merge_kernel over `frames` frames.  When the launch has at most
+// two frames per SM, each CTA's latency sets the time, so the re-rank rows
+// are staged in shared memory by bulk copies (64 or 32 rows per chunk, as
+// the opt-in shared memory allows; rows of d % 4 == 0 floats, 16-byte
+// aligned); larger launches keep many CTAs per SM and read the rows from
+// global memory.
+void launch_merge(VfrIndex *ix, MergeArgs &ma, size_t frames, cudaStream_t stream) {
+    ma.stage_rows = 0;
+    if (ix->d % 4 == 0 && reinterpret_cast<uintptr_t>(ix->vectors) % 16 == 0 &&
+        frames <= static_cast<size_t>(ix->sm_count) * 2) {
+        for (int rows : {64, 32})
+            if (merge_smem(ma.sort_size, ma.thr_stride, ix->d, rows).total <=
+                static_cast<size_t>(ix->merge_smem_max)) {
+                ma.stage_rows = rows;
+                break;
+            }
+    }
+    const size_t smem = merge_smem(ma.sort_size, ma.thr_stride, ix->d, ma.stage_rows).total;
+    require(smem <= static_cast<size_t>(ix->merge_smem_max), "candidate lists exceed the merge's shared memory");
+    merge_kernel<<<static_cast<unsigned>(frames), kMergeThreads, smem, stream>>>(ma);
+    cuda_check(cudaGetLastError());
+}
+
 Plan make_plan(size_t frames, int64_t n, int sms) {
     Plan p{};
     p.n_qtiles = static_cast<int>((frames + kTileM - 1) / kTileM);
@@ -947,7 +1146,7 @@ int64_t items_cap(size_t frames, int sms) {
 }
 
 struct WsLayout {
-    size_t q16, qstats, keys, counts, thr, flist, fcount, total;
+    size_t q16, qstats, keys, thr, flist, fcount, total;
 };
 
 WsLayout ws_layout(size_t frames, int d_pad, int sms) {
@@ -959,12 +1158,12 @@ WsLayout ws_layout(size_t frames, int d_pad, int sms) {
     off = align256(off + fr * d_pad * sizeof(__half));
     l.qstats = off;
     off = align256(off + fr * sizeof(float4));
+    // frame-major candidate blocks: frames x lists <= items x 128 entries;
+    // each threshold row is padded to a multiple of 4
     l.keys = off;
     off = align256(off + items * kItemKeep * kTileM * sizeof(unsigned long long));
-    l.counts = off;
-    off = align256(off + items * kTileM * sizeof(int));
     l.thr = off;
-    off = align256(off + items * kTileM * sizeof(float));
+    off = align256(off + (items * kTileM + fr * 4) * sizeof(float));
     l.flist = off;
     off = align256(off + fr * sizeof(int32_t));
     l.fcount = off;
@@ -992,12 +1191,11 @@ struct CoarseArgs {
     int d;
     int nlist;
     int nprobe;
-    int n_qtiles;
-    int lists;  // coarse candidate lists per frame tile
-    int slots;  // lists * kItemKeep rounded up to 32
-    const unsigned long long *keys;
-    const int *counts;
-    const float *thr;
+    int lists;       // coarse candidate lists per frame
+    int thr_stride;  // thresholds per frame row
+    int slots;       // lists * kItemKeep rounded up to 32
+    const unsigned long long *keys;  // [frame][lists][kItemKeep]
+    const float *thr;                // [frame][thr_stride]
     const float4 *qstats;
     const float *queries;
     float *out;
@@ -1023,7 +1221,6 @@ __global__ void __launch_bounds__(kMergeThreads) coarse_select_kernel(CoarseArgs
     __shared__ int ok_s;
     const int tid = threadIdx.x, lane = tid & 31, octet = tid >> 3, j = tid & 7;
     const long long frame = blockIdx.x;
-    const int qtile = static_cast<int>(frame / kTileM), r = static_cast<int>(frame % kTileM);
     const int d = a.d, P = a.nprobe;
     const float *src = a.queries + frame * d;
     const float inf = __int_as_float(0x7f800000);
@@ -1036,27 +1233,18 @@ __global__ void __launch_bounds__(kMergeThreads) coarse_select_kernel(CoarseArgs
         return;
     }
     for (int i = tid; i < d; i += kMergeThreads) q[i] = src[i];
+    // the frame's contiguous candidate block (slots past a list's count hold kEmptyKey)
     float tmin = inf;
-    int total = 0;
-    for (int s = tid; s < a.lists; s += kMergeThreads) {
-        const size_t o = (static_cast<size_t>(s) * a.n_qtiles + qtile) * kTileM + r;
-        tmin = fminf(tmin, a.thr[o]);
-        total += a.counts[o];
-    }
-    for (int i = tid; i < a.slots; i += kMergeThreads) {
-        const int s = i / kItemKeep, slot = i % kItemKeep;
-        unsigned long long key = kEmptyKey;
-        if (s < a.lists) {
-            const size_t item = static_cast<size_t>(s) * a.n_qtiles + qtile;
-            if (slot < a.counts[item * kTileM + r]) key = a.keys[(item * kItemKeep + slot) * kTileM + r];
-        }
-        keys[i] = key;
-    }
-    block_min_sum(tmin, total, sel);
+    for (int s = tid; s < a.lists; s += kMergeThreads) tmin = fminf(tmin, a.thr[frame * a.thr_stride + s]);
+    const int real_slots = a.lists * kItemKeep;
+    const unsigned long long *fk = a.keys + static_cast<size_t>(frame) * real_slots;
+#pragma unroll 4
+    for (int i = tid; i < a.slots; i += kMergeThreads) keys[i] = i < real_slots ? fk[i] : kEmptyKey;
+    const KeyStats ks = key_stats(keys, a.slots, tmin, sel);
     float cut;
     bool too_many;
-    const int m = select_rerank(keys, a.slots, total, sel_keys, sel, cut, too_many);
-    const float bound = fminf(tmin, cut);
+    const int m = select_rerank(keys, a.slots, ks, sel_keys, sel, cut, too_many);
+    const float bound = fminf(ks.tmin, cut);
     // exact centroid distances; every centroid takes part, as in the
     // reference's sort (no +inf filter here)
     for (int c0 = 0; c0 < m; c0 += 64) {
@@ -1259,26 +1447,22 @@ __global__ void __launch_bounds__(kMergeThreads) ivf_merge_kernel(IvfMergeArgs a
         pbase[P] = acc;
     }
     float tmin = inf;
-    int total = 0;
     for (int i = tid; i < kSlots; i += kMergeThreads) {
         const int p = i / (kHalves * kItemKeep), h = (i / kItemKeep) % kHalves, slot = i % kItemKeep;
         unsigned long long key = kEmptyKey;
         if (p < P) {
             const size_t pos = static_cast<size_t>(a.pair_slot[frame * P + p]);
             const int cnt = a.counts[h * stride + pos];
-            if (slot == 0) {
-                tmin = fminf(tmin, a.thr[h * stride + pos]);
-                total += cnt;
-            }
+            if (slot == 0) tmin = fminf(tmin, a.thr[h * stride + pos]);
             if (slot < cnt) key = a.keys[(h * kItemKeep + slot) * stride + pos];
         }
         keys[i] = key;
     }
-    block_min_sum(tmin, total, sel);
+    const KeyStats ks = key_stats(keys, kSlots, tmin, sel);
     float cut;
     bool too_many;
-    const int m = select_rerank(keys, kSlots, total, sel_keys, sel, cut, too_many);
-    const float bound = fminf(tmin, cut);
+    const int m = select_rerank(keys, kSlots, ks, sel_keys, sel, cut, too_many);
+    const float bound = fminf(ks.tmin, cut);
     // exact re-rank; the key's position is the reference's scan position
     Top8 top;
     top.init();
@@ -1381,7 +1565,7 @@ __global__ void __launch_bounds__(kMergeThreads) ivf_merge_kernel(IvfMergeArgs a
 }
 
 struct IvfWs {
-    size_t q16, qstats, ckeys, ccounts, cthr, probes, probe_ok, list_count, list_cursor, list_start, items, item_count,
+    size_t q16, qstats, ckeys, cthr, probes, probe_ok, list_count, list_cursor, list_start, items, item_count,
         pair_frame, pair_slot, qp, fkeys, fcounts, fthr, flist, fcount, total;
 };
 
@@ -1399,8 +1583,7 @@ IvfWs ivf_ws_layout(size_t frames, int d_pad, int nlist, int nprobe, int sms) {
     take(l.q16, fr * d_pad * sizeof(__half));
     take(l.qstats, fr * sizeof(float4));
     take(l.ckeys, clists * kItemKeep * kTileM * sizeof(unsigned long long));
-    take(l.ccounts, clists * kTileM * sizeof(int));
-    take(l.cthr, clists * kTileM * sizeof(float));
+    take(l.cthr, (clists * kTileM + fr * 4) * sizeof(float));
     take(l.probes, pairs * sizeof(int32_t));
     take(l.probe_ok, fr * sizeof(int32_t));
     take(l.list_count, static_cast<size_t>(nlist) * sizeof(int32_t));
@@ -1519,7 +1702,15 @@ void build_tc(VfrIndex *ix) {
                                     static_cast<int>(kSmemTC)));
     cuda_check(cudaFuncSetAttribute(cand_kernel<true, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(kSmemTC)));
-    cuda_check(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    {
+        int optin = 0;
+        cuda_check(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ix->device));
+        cudaFuncAttributes fa{};
+        cuda_check(cudaFuncGetAttributes(&fa, merge_kernel));
+        ix->merge_smem_max = optin - static_cast<int>(fa.sharedSizeBytes);
+        cuda_check(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        ix->merge_smem_max));
+    }
     cuda_check(cudaFuncSetAttribute(coarse_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
     cuda_check(cudaDeviceSynchronize());
     ix->have_tc = true;
@@ -1575,7 +1766,6 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     __half *q16 = reinterpret_cast<__half *>(ws + l.q16);
     float4 *qstats = reinterpret_cast<float4 *>(ws + l.qstats);
     auto *ckeys = reinterpret_cast<unsigned long long *>(ws + l.ckeys);
-    int *ccounts = reinterpret_cast<int *>(ws + l.ccounts);
     float *cthr = reinterpret_cast<float *>(ws + l.cthr);
     int32_t *probes = reinterpret_cast<int32_t *>(ws + l.probes);
     int32_t *probe_ok = reinterpret_cast<int32_t *>(ws + l.probe_ok);
@@ -1623,8 +1813,9 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     ca.row_norms = ix->centroid_norms;
     ca.coef = coef;
     ca.out_keys = ckeys;
-    ca.out_count = ccounts;
     ca.out_thr = cthr;
+    ca.lists = pc.segments * kHalves;
+    ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
     ix->prof.begin(kProfCand, stream);
     cand_kernel<false, kIvfKeep><<<std::min(pc.segments * pc.n_qtiles, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(
@@ -1637,11 +1828,10 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     cs.d = ix->d;
     cs.nlist = ix->nlist;
     cs.nprobe = P;
-    cs.n_qtiles = pc.n_qtiles;
-    cs.lists = pc.segments * kHalves;
+    cs.lists = ca.lists;
+    cs.thr_stride = ca.thr_stride;
     cs.slots = (cs.lists * kItemKeep + 31) / 32 * 32;
     cs.keys = ckeys;
-    cs.counts = ccounts;
     cs.thr = cthr;
     cs.qstats = qstats;
     cs.queries = queries;
@@ -1781,7 +1971,6 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     __half *q16 = reinterpret_cast<__half *>(ws + l.q16);
     float4 *qstats = reinterpret_cast<float4 *>(ws + l.qstats);
     auto *keys = reinterpret_cast<unsigned long long *>(ws + l.keys);
-    int *counts = reinterpret_cast<int *>(ws + l.counts);
     float *thr = reinterpret_cast<float *>(ws + l.thr);
     int32_t *flist = reinterpret_cast<int32_t *>(ws + l.flist);
     int32_t *fcount = reinterpret_cast<int32_t *>(ws + l.fcount);
@@ -1808,8 +1997,9 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ca.row_norms = ix->row_norms;
     ca.coef = -2.0f / (ix->tc_scale * ix->tc_scale);
     ca.out_keys = keys;
-    ca.out_count = counts;
     ca.out_thr = thr;
+    ca.lists = p.segments * kHalves;
+    ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
     const int grid = std::min(items, ix->sm_count);
@@ -1823,13 +2013,11 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
 
     MergeArgs ma{};
     ma.d = ix->d;
-    ma.n_qtiles = p.n_qtiles;
-    ma.segments = p.segments * kHalves;  // candidate lists per frame tile
+    ma.lists = ca.lists;
+    ma.thr_stride = ca.thr_stride;
     ma.keep = p.tiles_per_seg <= kShortItemTiles ? kShortKeep : kIvfKeep;
-    const int sort = (ma.segments * ma.keep + 31) / 32 * 32;  // key slots per frame
-    ma.sort_size = sort;
+    ma.sort_size = (ma.lists * ma.keep + 31) / 32 * 32;  // key slots per frame
     ma.keys = keys;
-    ma.counts = counts;
     ma.thr = thr;
     ma.qstats = qstats;
     ma.queries = queries;
@@ -1851,10 +2039,8 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ma.fallback_list = flist;
     ma.fallback_count = fcount;
     ma.counters = ix->counters;
-    const size_t msmem = static_cast<size_t>(sort) * 8 + static_cast<size_t>(ix->d) * 4;
     ix->prof.begin(kProfMerge, stream);
-    merge_kernel<<<static_cast<unsigned>(frames), kMergeThreads, msmem, stream>>>(ma);
-    cuda_check(cudaGetLastError());
+    launch_merge(ix, ma, frames, stream);
     ix->prof.end(stream);
 
     // frames the certificate could not settle: exact re-run
@@ -1890,7 +2076,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
 // synchronise the device and take driver locks (an unbounded stall inside a
 // hard deadline), or a host whose device memory budget is fixed up front.
 // Its working memory is the file-scope array below, sized for at most
-// kNoAllocMaxFrames frames of width <= kNoAllocMaxWidth (5.4 MiB, held by
+// kNoAllocMaxFrames frames of width <= kNoAllocMaxWidth (5.3 MiB, held by
 // every GPU that loads the library until the process exits).  The array's
 // device address is looked up once per device (cudaGetSymbolAddress) on the
 // first call made on that device, so that first call should come before any
@@ -1908,9 +2094,8 @@ constexpr size_t kNoAllocQ16 = 0;
 constexpr size_t kNoAllocQStats = kNoAllocQ16 + kNoAllocMaxFrames * kNoAllocMaxWidth * sizeof(__half);
 constexpr size_t kNoAllocKeys = kNoAllocQStats + kNoAllocMaxFrames * sizeof(float4);
 constexpr size_t kNoAllocLists = static_cast<size_t>(kNoAllocMaxItems) * kHalves;
-constexpr size_t kNoAllocCounts = kNoAllocKeys + kNoAllocLists * kItemKeep * kTileM * sizeof(unsigned long long);
-constexpr size_t kNoAllocThr = kNoAllocCounts + kNoAllocLists * kTileM * sizeof(int);
-constexpr size_t kNoAllocList = kNoAllocThr + kNoAllocLists * kTileM * sizeof(float);
+constexpr size_t kNoAllocThr = kNoAllocKeys + kNoAllocLists * kItemKeep * kTileM * sizeof(unsigned long long);
+constexpr size_t kNoAllocList = kNoAllocThr + (kNoAllocLists * kTileM + kNoAllocMaxFrames * 4) * sizeof(float);
 constexpr size_t kNoAllocCount = kNoAllocList + kNoAllocMaxFrames * sizeof(int32_t);
 constexpr size_t kNoAllocBytes = kNoAllocCount + 256;
 
@@ -1960,7 +2145,6 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     __half *q16 = reinterpret_cast<__half *>(ws + kNoAllocQ16);
     float4 *qstats = reinterpret_cast<float4 *>(ws + kNoAllocQStats);
     auto *keys = reinterpret_cast<unsigned long long *>(ws + kNoAllocKeys);
-    int *counts = reinterpret_cast<int *>(ws + kNoAllocCounts);
     float *thr = reinterpret_cast<float *>(ws + kNoAllocThr);
     int32_t *flist = reinterpret_cast<int32_t *>(ws + kNoAllocList);
     int32_t *fcount = reinterpret_cast<int32_t *>(ws + kNoAllocCount);
@@ -1986,8 +2170,9 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ca.row_norms = ix->row_norms;
     ca.coef = -2.0f / (ix->tc_scale * ix->tc_scale);
     ca.out_keys = keys;
-    ca.out_count = counts;
     ca.out_thr = thr;
+    ca.lists = p.segments * kHalves;
+    ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
     if (p.tiles_per_seg <= kShortItemTiles)
@@ -1998,13 +2183,11 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
 
     MergeArgs ma{};
     ma.d = ix->d;
-    ma.n_qtiles = p.n_qtiles;
-    ma.segments = p.segments * kHalves;  // candidate lists per frame tile
+    ma.lists = ca.lists;
+    ma.thr_stride = ca.thr_stride;
     ma.keep = p.tiles_per_seg <= kShortItemTiles ? kShortKeep : kIvfKeep;
-    const int sort = (ma.segments * ma.keep + 31) / 32 * 32;  // key slots per frame
-    ma.sort_size = sort;
+    ma.sort_size = (ma.lists * ma.keep + 31) / 32 * 32;  // key slots per frame
     ma.keys = keys;
-    ma.counts = counts;
     ma.thr = thr;
     ma.qstats = qstats;
     ma.queries = features;
@@ -2024,9 +2207,7 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ma.fallback_list = flist;
     ma.fallback_count = fcount;
     ma.counters = ix->counters;
-    const size_t msmem = static_cast<size_t>(sort) * 8 + static_cast<size_t>(ix->d) * 4;
-    merge_kernel<<<static_cast<unsigned>(frames), kMergeThreads, msmem, stream>>>(ma);
-    cuda_check(cudaGetLastError());
+    launch_merge(ix, ma, frames, stream);
 
     ExactArgs ea{};
     ea.d = ix->d;

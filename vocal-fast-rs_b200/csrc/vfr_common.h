@@ -113,6 +113,7 @@ struct VfrIndex {
     float max_row_hat = 0.f;       // max ||fp16(s x) / s||
     float max_row_residual = 0.f;  // max ||x - fp16(s x) / s||
     int sm_count = 148;
+    int merge_smem_max = 96 * 1024;  // dynamic shared memory merge_kernel may use (set by build_tc)
     // IVF: the same layout for the coarse centroids (nlist_pad rows).
     __half *centroids_h = nullptr;
     float *centroid_norms = nullptr;
