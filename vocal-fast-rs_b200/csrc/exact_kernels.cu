@@ -15,8 +15,12 @@
 // Differences taken from the reference CUDA kernels (retrieval_block.cuh):
 // a frame with no candidate keeps its query, index_rate is clamped to [0,1]
 // and r <= 0 leaves the frame untouched.
+#include <stdexcept>
+#include <string>
+
 #include "exact_common.cuh"
 #include "kernels.h"
+#include "pdl.cuh"
 
 namespace vfr {
 namespace {
@@ -227,6 +231,7 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame) {
 // One CTA per frame, or, with a device frame list (the frames the
 // tensor-core engine could not certify), a fixed grid striding over it.
 __global__ void __launch_bounds__(kThreads) exact_kernel(ExactArgs a) {
+    grid_dependency_wait();  // the frame list and the outputs belong to the kernel before
     if (a.frame_list) {
         const int count = *a.frame_count;
         for (int i = blockIdx.x; i < count; i += gridDim.x) {
@@ -240,12 +245,17 @@ __global__ void __launch_bounds__(kThreads) exact_kernel(ExactArgs a) {
 
 }  // namespace
 
-void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream) {
+void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream, bool after_kernel) {
     if (frames <= 0) return;
     size_t smem = static_cast<size_t>(args.d) * sizeof(float);
     unsigned grid = static_cast<unsigned>(frames);
     if (args.frame_list) grid = static_cast<unsigned>(frames < 1184 ? frames : 1184);
-    exact_kernel<<<grid, kThreads, smem, stream>>>(args);
+    if (after_kernel) {
+        const cudaError_t rc = launch_pdl(exact_kernel, dim3(grid), dim3(kThreads), smem, stream, args);
+        if (rc != cudaSuccess) throw std::runtime_error(std::string("exact kernel launch: ") + cudaGetErrorString(rc));
+    } else {
+        exact_kernel<<<grid, kThreads, smem, stream>>>(args);
+    }
 }
 
 }  // namespace vfr

@@ -42,7 +42,9 @@ struct ExactArgs {
     const int32_t *frame_count;  // with frame_list: its length (device)
 };
 // frames: the frame count, or with a frame list the largest possible length.
-void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream);
+// after_kernel: launched behind another kernel of the same call, which it may
+// overlap until its own dependency wait (programmatic dependent launch).
+void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream, bool after_kernel = false);
 
 // Sharded helpers (shard_kernels.cu).
 void launch_merge_topk(const float *dist, const int64_t *labels, int shards, long long frames, float *out_dist,

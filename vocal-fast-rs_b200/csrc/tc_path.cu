@@ -27,6 +27,7 @@
 
 #include "exact_common.cuh"
 #include "kernels.h"
+#include "pdl.cuh"
 #include "tc_path.h"
 #include "tc_ptx.cuh"
 
@@ -238,6 +239,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    launch_dependents();
+    // the IVF work-item table comes from the kernels before this one; the
+    // flat producer waits for the query tiles only (below)
+    if constexpr (kIvf) grid_dependency_wait();
     const int items = item_total<kIvf>(a);
 
     if (threadIdx.x == 0) {
@@ -273,17 +278,43 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer
+            // Flat: the database tiles of the first stages do not depend on
+            // the query preparation, so they are requested before waiting
+            // for it; those stages then only add their query tile.
+            int early = 0;
+            if constexpr (!kIvf) {
+                if (static_cast<int>(blockIdx.x) < items) {
+                    const Item it0 = item_at<kIvf>(a, blockIdx.x);
+                    early = min(kStages, it0.tiles * a.ksteps);
+                    for (int s = 0; s < early; ++s) {
+                        const int t = s / a.ksteps, k = s % a.ksteps;
+                        tc::mbar_arrive_expect_tx(&full[s], kStageBytes);
+                        tc::tma_load_2d(smem + s * kStageBytes + kABytes, &tmap_x, &full[s], k * kTileK,
+                                        static_cast<int32_t>(it0.b_row0 + t * kTileN));
+                    }
+                }
+                grid_dependency_wait();
+            }
             int stage = 0;
             uint32_t phase = 0;
+            int issued = 0;
             for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
                 const Item it = item_at<kIvf>(a, item);
                 for (int t = 0; t < it.tiles && !*abort_flag; ++t) {
-                    for (int k = 0; k < a.ksteps; ++k) {
+                    for (int k = 0; k < a.ksteps; ++k, ++issued) {
                         if (!tc::mbar_wait(&empty[stage], phase ^ 1, kWaitLimitNs)) {
                             fail();
                             break;
                         }
                         uint8_t *sa = smem + stage * kStageBytes;
+                        if (issued < early) {  // database tile already requested
+                            tc::tma_load_2d(sa, &tmap_q, &full[stage], k * kTileK, it.a_row0);
+                            if (++stage == kStages) {
+                                stage = 0;
+                                phase ^= 1;
+                            }
+                            continue;
+                        }
                         tc::mbar_arrive_expect_tx(&full[stage], kStageBytes);
                         tc::tma_load_2d(sa, &tmap_q, &full[stage], k * kTileK, it.a_row0);
                         tc::tma_load_2d(sa + kABytes, &tmap_x, &full[stage], k * kTileK,
@@ -497,7 +528,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
 // ---------------------------------------------------------------- queries
 __global__ void prep_queries_kernel(const float *__restrict__ q, __half *__restrict__ qh, float4 *__restrict__ stats,
-                                    long long frames, int d, int d_pad, float scale) {
+                                    long long frames, int d, int d_pad, float scale, int32_t *zero) {
+    launch_dependents();  // the candidate kernel may start its prologue and database loads now
+    if (blockIdx.x == 0 && threadIdx.x == 0 && zero) *zero = 0;  // the call's fallback frame count
     const long long f = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (f >= frames) return;
@@ -809,21 +842,25 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
     const float inf = __int_as_float(0x7f800000);
     const int real_slots = a.lists * a.keep;
 
-    // the frame's candidate block (keys, then thresholds) arrives by two bulk
-    // copies while the threads load the query row and pad the key slots
+    launch_dependents();
     if (tid == 0) {
         tc::mbar_init(&gather_bar, 1);
         tc::mbar_init(&stage_bar, 1);
         tc::fence_mbarrier_init();
+    }
+    // the caller's inputs first, while the candidate kernel may still run
+    const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
+    for (int i = tid; i < d; i += kMergeThreads) q[i] = src[i];
+    for (int i = real_slots + tid; i < a.sort_size; i += kMergeThreads) keys[i] = kEmptyKey;
+    grid_dependency_wait();
+    // then the frame's candidate block (keys, thresholds): two bulk copies
+    if (tid == 0) {
         const uint32_t kbytes = static_cast<uint32_t>(real_slots) * 8;
         const uint32_t tbytes = static_cast<uint32_t>(a.thr_stride) * 4;
         tc::mbar_arrive_expect_tx(&gather_bar, kbytes + tbytes);
         tc::bulk_load(keys, a.keys + static_cast<size_t>(frame) * real_slots, kbytes, &gather_bar);
         tc::bulk_load(thr, a.thr + static_cast<size_t>(frame) * a.thr_stride, tbytes, &gather_bar);
     }
-    const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
-    for (int i = real_slots + tid; i < a.sort_size; i += kMergeThreads) keys[i] = kEmptyKey;
-    for (int i = tid; i < d; i += kMergeThreads) q[i] = src[i];
     __syncthreads();  // barrier initialisation is visible before anyone waits on it
     const bool landed = tc::mbar_wait(&gather_bar, 0, kWaitLimitNs);
     if (__syncthreads_or(!landed)) {
@@ -1111,8 +1148,16 @@ void launch_merge(VfrIndex *ix, MergeArgs &ma, size_t frames, cudaStream_t strea
     }
     const size_t smem = merge_smem(ma.sort_size, ma.thr_stride, ix->d, ma.stage_rows).total;
     require(smem <= static_cast<size_t>(ix->merge_smem_max), "candidate lists exceed the merge's shared memory");
-    merge_kernel<<<static_cast<unsigned>(frames), kMergeThreads, smem, stream>>>(ma);
-    cuda_check(cudaGetLastError());
+    cuda_check(launch_pdl(merge_kernel, dim3(static_cast<unsigned>(frames)), dim3(kMergeThreads), smem, stream, ma));
+}
+
+// Launches the flat candidate kernel behind prep_queries_kernel (it starts
+// loading database tiles before the query tiles exist); the candidate list
+// size follows the work-item length.
+void launch_cand_flat(const Plan &p, int grid, const CUtensorMap &tmap_q, const CUtensorMap &tmap_x,
+                      const CandArgs &ca, cudaStream_t stream) {
+    auto kernel = p.tiles_per_seg <= kShortItemTiles ? cand_kernel<false, kShortKeep> : cand_kernel<false, kIvfKeep>;
+    cuda_check(launch_pdl(kernel, dim3(grid), dim3(kThreadsTC), kSmemTC, stream, tmap_q, tmap_x, ca));
 }
 
 Plan make_plan(size_t frames, int64_t n, int sms) {
@@ -1792,10 +1837,9 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     const long long lanes = static_cast<long long>(frames) * 32;
     ix->prof.begin(kProfPrep, stream);
     prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
-        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale);
+        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
-    cuda_check(cudaMemsetAsync(fcount, 0, sizeof(int32_t), stream));
     cuda_check(cudaMemsetAsync(list_count, 0, static_cast<size_t>(ix->nlist) * sizeof(int32_t), stream));
 
     // 2. coarse candidates over the centroids
@@ -1979,10 +2023,9 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     const long long lanes = static_cast<long long>(frames) * 32;
     ix->prof.begin(kProfPrep, stream);
     prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
-        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale);
+        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
-    cuda_check(cudaMemsetAsync(fcount, 0, sizeof(int32_t), stream));
 
     CUtensorMap tmap_q;
     encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
@@ -2004,11 +2047,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     const int items = p.segments * p.n_qtiles;
     const int grid = std::min(items, ix->sm_count);
     ix->prof.begin(kProfCand, stream);
-    if (p.tiles_per_seg <= kShortItemTiles)
-        cand_kernel<false, kShortKeep><<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
-    else
-        cand_kernel<false, kIvfKeep><<<grid, kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
-    cuda_check(cudaGetLastError());
+    launch_cand_flat(p, grid, tmap_q, ix->tmap_vectors, ca, stream);
     ix->prof.end(stream);
 
     MergeArgs ma{};
@@ -2064,7 +2103,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ea.frame_list = flist;
     ea.frame_count = fcount;
     ix->prof.begin(kProfExact, stream);
-    launch_exact(ea, static_cast<long long>(frames), stream);
+    launch_exact(ea, static_cast<long long>(frames), stream, true);
     ix->prof.end(stream);
 }
 
@@ -2153,9 +2192,8 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     require(p.segments > 0, "no-allocation scratch cannot hold this plan");
     const long long lanes = static_cast<long long>(frames) * 32;
     prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
-        features, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale);
+        features, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount);
     cuda_check(cudaGetLastError());
-    cuda_check(cudaMemsetAsync(fcount, 0, sizeof(int32_t), stream));
 
     CUtensorMap tmap_q;
     encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
@@ -2175,11 +2213,7 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
-    if (p.tiles_per_seg <= kShortItemTiles)
-        cand_kernel<false, kShortKeep><<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
-    else
-        cand_kernel<false, kIvfKeep><<<std::min(items, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(tmap_q, ix->tmap_vectors, ca);
-    cuda_check(cudaGetLastError());
+    launch_cand_flat(p, std::min(items, ix->sm_count), tmap_q, ix->tmap_vectors, ca, stream);
 
     MergeArgs ma{};
     ma.d = ix->d;
@@ -2226,7 +2260,7 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ea.counters = ix->counters;
     ea.frame_list = flist;
     ea.frame_count = fcount;
-    launch_exact(ea, static_cast<long long>(frames), stream);
+    launch_exact(ea, static_cast<long long>(frames), stream, true);
     cuda_check(cudaGetLastError());
 }
 
