@@ -37,7 +37,6 @@ namespace {
 constexpr int kTileM = 128;  // frames per tile: TMEM lanes
 constexpr int kTileN = 256;  // rows per MMA / accumulator
 constexpr int kTileK = 64;   // fp16 elements per 128-byte swizzled row
-constexpr int kStages = 4;
 // Candidates kept per frame per candidate list (in registers).  A list whose
 // K-th best lies close to the frame's 8th-best distance leaves the frame
 // uncertified (and re-run exactly), so the size follows how many of a
@@ -55,11 +54,25 @@ constexpr int kMaxSegments = 256;
 constexpr int kEpiWarps = 8;     // two per TMEM lane quarter, each on half of a tile's columns
 constexpr int kHalves = 2;       // candidate lists per (work item, frame)
 constexpr int kThreadsTC = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr uint32_t kABytes = kTileM * kTileK * 2;
 constexpr uint32_t kBBytes = kTileN * kTileK * 2;
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kNormBytes = kEpiWarps * 2 * (kTileN / kHalves) * sizeof(float);  // per warp, double buffered
-constexpr size_t kSmemTC = 1024 + kStages * kStageBytes + kNormBytes + 256;
+constexpr int kSmallBlock = 32;  // frame blocks up to this size load a 32-row query box
+
+// Pipeline shape of cand_kernel for a query box of kARows rows.  The MMA is
+// always M = 128; with a 32-row box (a block of at most 32 frames) the stage
+// holds 4 KB of query rows instead of 16 KB, the MMA's rows 32-127 read
+// whatever follows in the stage (their TMEM lanes are never read), and the
+// shared memory saved buys two more stages: 192 KB of database tiles in
+// flight per SM instead of 128 KB.
+template <int kARows>
+struct Pipe {
+    static constexpr int kStages = kARows == kTileM ? 4 : 6;
+    static constexpr uint32_t kABytes = kARows * kTileK * 2;
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr size_t kSmem = 1024 + kStages * kStageBytes + kNormBytes + 256;
+};
+static_assert(Pipe<kTileM>::kSmem <= 232448 && Pipe<kSmallBlock>::kSmem <= 232448, "cand_kernel shared memory");
+static_assert(Pipe<kSmallBlock>::kStageBytes % 1024 == 0, "stage bases stay 1024-byte aligned");
 constexpr uint32_t kTmemCols = 512;  // two 128 x 256 fp32 accumulators
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kFormatF16 = 0;
@@ -223,9 +236,12 @@ __device__ __forceinline__ float4 load_norms4(const float *p) {
     else return __ldg(reinterpret_cast<const float4 *>(p));
 }
 
-template <bool kIvf, int K>
+template <bool kIvf, int K, int kARows = kTileM>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     cand_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, CandArgs a) {
+    constexpr int kStages = Pipe<kARows>::kStages;
+    constexpr uint32_t kABytes = Pipe<kARows>::kABytes;
+    constexpr uint32_t kStageBytes = Pipe<kARows>::kStageBytes;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float *norm_smem = reinterpret_cast<float *>(smem + kStages * kStageBytes);
@@ -335,6 +351,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 }
             }
         }
+        // Lanes 1-31 wait here for the producer lane, so the warp reaches
+        // the CTA barrier below converged: lanes left parked at that barrier
+        // for the whole kernel resumed microseconds after it released.
+        __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer (one thread)
@@ -379,6 +399,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 }
             }
         }
+        __syncwarp();  // converged at the CTA barrier, as the producer warp
     } else {
         // ---------------- epilogue: one thread per frame of the tile; the two
         // warps of a TMEM lane quarter split each tile's columns in halves
@@ -587,18 +608,19 @@ struct MergeArgs {
     int stage_rows;  // re-rank rows staged in shared memory per chunk (0: read them from global memory)
 };
 
-constexpr int kMergeThreads = 256;
+constexpr int kMergeThreads = 256;     // per frame, when many frames share the GPU
+constexpr int kMergeThreadsMax = 512;  // per frame, when a launch has few frames
 
 
 // Shared state of select_rerank (one per CTA, in shared memory).
 struct SelectState {
-    unsigned int hist[256];
+    unsigned int hist[2][256];  // radix passes alternate between the two
     uint32_t bin, below_bin, in_bin;
     uint32_t dropped_min;
     int count;
-    float red_f[kMergeThreads / 32];
-    int red_i[kMergeThreads / 32];
-    uint32_t red_lo[kMergeThreads / 32], red_hi[kMergeThreads / 32];
+    float red_f[kMergeThreadsMax / 32];
+    int red_i[kMergeThreadsMax / 32];
+    uint32_t red_lo[kMergeThreadsMax / 32], red_hi[kMergeThreadsMax / 32];
 };
 
 // The real keys among a CTA's key slots: how many, and the smallest and
@@ -612,10 +634,12 @@ struct KeyStats {
 // Block-wide KeyStats over keys[0 .. slots) (in shared memory); every thread
 // of the CTA calls it and gets the result.  Its barrier also publishes the
 // shared-memory writes made before the call.
+template <int kT>
 __device__ KeyStats key_stats(const unsigned long long *keys, int slots, float tmin, SelectState &st) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     KeyStats ks{0, 0xffffffffu, 0u, tmin};
-    for (int i = tid; i < slots; i += kMergeThreads) {
+    for (int i = tid; i < 256; i += kT) st.hist[0][i] = 0u;  // select_rerank's first pass
+    for (int i = tid; i < slots; i += kT) {
         const unsigned long long key = keys[i];
         if (key != kEmptyKey) {
             const uint32_t b = static_cast<uint32_t>(key >> 32);
@@ -637,7 +661,7 @@ __device__ KeyStats key_stats(const unsigned long long *keys, int slots, float t
     }
     __syncthreads();
     ks = KeyStats{0, 0xffffffffu, 0u, __int_as_float(0x7f800000)};
-    for (int w = 0; w < kMergeThreads / 32; ++w) {
+    for (int w = 0; w < kT / 32; ++w) {
         ks.total += st.red_i[w];
         ks.lo = min(ks.lo, st.red_lo[w]);
         ks.hi = max(ks.hi, st.red_hi[w]);
@@ -665,6 +689,7 @@ constexpr int kRerankStop = 80;
 // aggregated per warp (match_any), so a crowded digit costs one shared atomic
 // per warp.  Returns the number of keys written to sel_keys.  Called by every
 // thread of the CTA.
+template <int kT>
 __device__ int select_rerank(const unsigned long long *keys, int slots, const KeyStats &ks,
                              unsigned long long *sel_keys, SelectState &st, float &bound, bool &too_many) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -679,25 +704,25 @@ __device__ int select_rerank(const unsigned long long *keys, int slots, const Ke
             uint32_t mask_bits = ~((2u << top) - 1u);    // the common prefix (0 when top == 31)
             uint32_t prefix = lo & mask_bits;
             uint32_t rank = kRerank, below = 0;          // 1-based rank inside the prefix group
+            int pass = 0;
             while (true) {
                 const int shift = top > 7 ? top - 7 : 0;
                 const uint32_t digits = (2u << (top - shift)) - 1u;
-                st.hist[tid] = 0u;
-                __syncthreads();
-                for (int i = tid; i < slots; i += kMergeThreads) {
+                unsigned int *hist = st.hist[pass & 1];  // cleared before this pass
+                for (int i = tid; i < slots; i += kT) {
                     const unsigned long long key = keys[i];
                     const uint32_t b = static_cast<uint32_t>(key >> 32);
                     const bool in = key != kEmptyKey && (b & mask_bits) == prefix;
                     const uint32_t digit = in ? (b >> shift) & digits : 0xffffffffu;
                     const unsigned peers = __match_any_sync(kFullMask, digit);
-                    if (in && lane == __ffs(peers) - 1) atomicAdd(&st.hist[digit], __popc(peers));
+                    if (in && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], __popc(peers));
                 }
                 __syncthreads();
                 if (warp == 0) {
                     uint32_t c[8], sum = 0;
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
-                        c[k] = st.hist[lane * 8 + k];
+                        c[k] = hist[lane * 8 + k];
                         sum += c[k];
                     }
                     uint32_t incl = sum;
@@ -723,6 +748,9 @@ __device__ int select_rerank(const unsigned long long *keys, int slots, const Ke
                             acc += c[k];
                         }
                     }
+                } else {
+                    // meanwhile the other warps clear the next pass's histogram
+                    for (int i = tid - 32; i < 256; i += kT - 32) st.hist[(pass + 1) & 1][i] = 0u;
                 }
                 __syncthreads();
                 const uint32_t bin = st.bin, acc = st.below_bin, cnt = st.in_bin;
@@ -735,6 +763,7 @@ __device__ int select_rerank(const unsigned long long *keys, int slots, const Ke
                 prefix |= bin << shift;
                 mask_bits |= digits << shift;
                 top = shift - 1;
+                ++pass;
             }
         }
     }
@@ -744,7 +773,7 @@ __device__ int select_rerank(const unsigned long long *keys, int slots, const Ke
     }
     __syncthreads();
     uint32_t dropped = 0xffffffffu;
-    for (int i = tid; i < slots; i += kMergeThreads) {
+    for (int i = tid; i < slots; i += kT) {
         const unsigned long long key = keys[i];
         if (key == kEmptyKey) continue;
         const uint32_t b = static_cast<uint32_t>(key >> 32);
@@ -764,14 +793,36 @@ __device__ int select_rerank(const unsigned long long *keys, int slots, const Ke
     return selected < kRerankMax ? selected : kRerankMax;
 }
 
-// Reduces the octets' sorted top-8 lists (octet_best[32][8]) to the CTA's
-// top-8 keys in best[0..8); warp 0 does the work, then the CTA syncs.
+// Reduces the octets' sorted top-8 lists (octet_best[kOct][8], kOct 32 or
+// 64) to the CTA's top-8 keys in best[0..8); warp 0 does the work (with 64
+// lists, lane l first merges lists l and l + 32), then the CTA syncs.
+template <int kOct>
 __device__ __forceinline__ void merge_octet_lists(const unsigned long long *octet_best, unsigned long long *best) {
+    static_assert(kOct == 32 || kOct == 64, "octet lists per CTA");
     const int lane = threadIdx.x & 31;
     if ((threadIdx.x >> 5) == 0) {
+        unsigned long long own[8];
+        if constexpr (kOct == 32) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) own[i] = octet_best[lane * 8 + i];
+        } else {
+            // the 8 smallest of two sorted lists, in order
+            const unsigned long long *x = octet_best + lane * 8, *y = octet_best + (lane + 32) * 8;
+            int ix = 0, iy = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const unsigned long long vx = x[ix], vy = y[iy];
+                const bool take_x = vx <= vy;
+                own[i] = take_x ? vx : vy;
+                ix += take_x;
+                iy += !take_x;
+            }
+        }
         int head = 0;
         for (int i = 0; i < 8; ++i) {
-            unsigned long long mine = head < 8 ? octet_best[lane * 8 + head] : kEmptyKey;
+            unsigned long long mine = kEmptyKey;
+#pragma unroll
+            for (int h = 0; h < 8; ++h) mine = h == head ? own[h] : mine;
             unsigned long long mn = mine;
 #pragma unroll
             for (int s = 16; s > 0; s >>= 1) {
@@ -817,14 +868,17 @@ __host__ __device__ inline MergeSmem merge_smem(int sort_size, int thr_stride, i
     return m;
 }
 
-__global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
+template <int kT>
+__global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
+    constexpr int kOct = kT / 8;           // octets: 8 threads per exact distance
+    constexpr int kPerOctet = 64 / kOct;   // rows per octet per pass of 64 rows
     extern __shared__ __align__(16) uint8_t msm[];
     const MergeSmem lay = merge_smem(a.sort_size, a.thr_stride, a.d, a.stage_rows);
     unsigned long long *keys = reinterpret_cast<unsigned long long *>(msm + lay.keys);
     float *thr = reinterpret_cast<float *>(msm + lay.thr);
     float *q = reinterpret_cast<float *>(msm + lay.q);
     float *stage = reinterpret_cast<float *>(msm + lay.stage);
-    __shared__ unsigned long long octet_best[32 * 8];
+    __shared__ unsigned long long exact_keys[kRerankMax];  // (exact distance, row) per re-ranked key
     __shared__ unsigned long long best[8];
     __shared__ int certified_s;
     __shared__ SelectState sel;
@@ -834,7 +888,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
     __shared__ __align__(8) uint64_t gather_bar;
     __shared__ __align__(8) uint64_t stage_bar;
 
-    const int tid = threadIdx.x, lane = tid & 31, octet = tid >> 3, j = tid & 7;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
     const long long frame = blockIdx.x;
     const int d = a.d;
     const float *src = a.queries + frame * d;
@@ -848,25 +902,32 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
         tc::mbar_init(&stage_bar, 1);
         tc::fence_mbarrier_init();
     }
+    if (tid < 8) best[tid] = kEmptyKey;
     // the caller's inputs first, while the candidate kernel may still run
     const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
-    for (int i = tid; i < d; i += kMergeThreads) q[i] = src[i];
-    for (int i = real_slots + tid; i < a.sort_size; i += kMergeThreads) keys[i] = kEmptyKey;
+    for (int i = tid; i < d; i += kT) q[i] = src[i];
+    for (int i = real_slots + tid; i < a.sort_size; i += kT) keys[i] = kEmptyKey;
     grid_dependency_wait();
-    // then the frame's candidate block (keys, thresholds): two bulk copies
-    if (tid == 0) {
-        const uint32_t kbytes = static_cast<uint32_t>(real_slots) * 8;
-        const uint32_t tbytes = static_cast<uint32_t>(a.thr_stride) * 4;
-        tc::mbar_arrive_expect_tx(&gather_bar, kbytes + tbytes);
-        tc::bulk_load(keys, a.keys + static_cast<size_t>(frame) * real_slots, kbytes, &gather_bar);
-        tc::bulk_load(thr, a.thr + static_cast<size_t>(frame) * a.thr_stride, tbytes, &gather_bar);
+    // then the frame's candidate block (keys, thresholds): two bulk copies.
+    // Warp 0 alone polls the barriers (a thread parked in a barrier poll can
+    // resume microseconds after the phase completes); the CTA barrier that
+    // follows releases the rest at once.
+    bool landed = true;
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t kbytes = static_cast<uint32_t>(real_slots) * 8;
+            const uint32_t tbytes = static_cast<uint32_t>(a.thr_stride) * 4;
+            tc::mbar_arrive_expect_tx(&gather_bar, kbytes + tbytes);
+            tc::bulk_load(keys, a.keys + static_cast<size_t>(frame) * real_slots, kbytes, &gather_bar);
+            tc::bulk_load(thr, a.thr + static_cast<size_t>(frame) * a.thr_stride, tbytes, &gather_bar);
+        }
+        __syncwarp();
+        landed = tc::mbar_wait(&gather_bar, 0, kWaitLimitNs);
     }
-    __syncthreads();  // barrier initialisation is visible before anyone waits on it
-    const bool landed = tc::mbar_wait(&gather_bar, 0, kWaitLimitNs);
     if (__syncthreads_or(!landed)) {
         // the copy never completed: give it one more bounded wait before the
         // shared memory is released, and hand the frame to the exact re-run
-        tc::mbar_wait(&gather_bar, 0, kWaitLimitNs);
+        if (warp == 0) tc::mbar_wait(&gather_bar, 0, kWaitLimitNs);
         if (tid == 0) {
             if (a.counters) atomicAdd(&a.counters->timeouts, 1ull);
             const int pos = atomicAdd(a.fallback_count, 1);
@@ -876,21 +937,20 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
     }
     if (a.mode == kModeBlend && !(ratio > 0.f)) {
         if (dst != src)
-            for (int i = tid; i < d; i += kMergeThreads) dst[i] = q[i];
+            for (int i = tid; i < d; i += kT) dst[i] = q[i];
         return;
     }
     float tmin = inf;
-    for (int s = tid; s < a.lists; s += kMergeThreads) tmin = fminf(tmin, thr[s]);
-    const KeyStats ks = key_stats(keys, a.sort_size, tmin, sel);
+    for (int s = tid; s < a.lists; s += kT) tmin = fminf(tmin, thr[s]);
+    const KeyStats ks = key_stats<kT>(keys, a.sort_size, tmin, sel);
     float cut;
     bool too_many_ties;
-    const int m = select_rerank(keys, a.sort_size, ks, sel_keys, sel, cut, too_many_ties);
+    const int m = select_rerank<kT>(keys, a.sort_size, ks, sel_keys, sel, cut, too_many_ties);
     const float t_final = fminf(ks.tmin, cut);
 
-    // exact re-rank in the reference order; flat scan position == row
-    Top8 top;
-    top.init();
-    bool stage_timeout = false;
+    // exact re-rank in the reference order (flat scan position == row): one
+    // octet per distance, each written to exact_keys; +inf and NaN distances
+    // never enter a top-8 list in the reference, so they become kEmptyKey
     if (a.stage_rows > 0) {
         // the chunk's rows arrive by bulk copies into shared memory, all in
         // flight at once, then the octets read them from there
@@ -898,71 +958,85 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
         uint32_t phase = 0;
         for (int c0 = 0; c0 < m; c0 += a.stage_rows) {
             const int rows_n = min(a.stage_rows, m - c0);
-            if ((tid >> 5) == 0) {
+            bool arrived = true;
+            if (warp == 0) {
                 if (lane == 0) tc::mbar_arrive_expect_tx(&stage_bar, static_cast<uint32_t>(rows_n * d * 4));
                 __syncwarp();
                 for (int i = lane; i < rows_n; i += 32)
                     tc::bulk_load(stage + i * stride, a.vectors + static_cast<size_t>(key_pos(sel_keys[c0 + i])) * d,
                                   static_cast<uint32_t>(d * 4), &stage_bar);
+                arrived = tc::mbar_wait(&stage_bar, phase, kWaitLimitNs);
             }
-            const bool arrived = tc::mbar_wait(&stage_bar, phase, kWaitLimitNs);
             phase ^= 1u;
             if (__syncthreads_or(!arrived)) {
-                stage_timeout = true;
-                break;
+                // a copy that never completed: let the copies in flight land
+                // (bounded) before the CTA's shared memory is released, and
+                // hand the frame to the exact re-run
+                if (warp == 0) tc::mbar_wait(&stage_bar, phase ^ 1u, kWaitLimitNs);
+                if (tid == 0) {
+                    if (a.counters) atomicAdd(&a.counters->timeouts, 1ull);
+                    const int pos = atomicAdd(a.fallback_count, 1);
+                    a.fallback_list[pos] = static_cast<int32_t>(frame);
+                }
+                return;
             }
             // warp-uniform trip count: every octet takes part in the shuffles
             for (int cb = 0; cb < rows_n; cb += 64) {
-                const int c = cb + octet, c2 = c + 32;
-                const float *xs[2] = {stage + (c < rows_n ? c : 0) * stride, stage + (c2 < rows_n ? c2 : 0) * stride};
-                float dist[2];
-                octet_l2n<2, false>(q, xs, d, j, lane & ~7, kFullMask, dist);
-                if (c < rows_n && dist[0] < inf) top.insert(make_key(dist[0], key_pos(sel_keys[c0 + c])));
-                if (c2 < rows_n && dist[1] < inf) top.insert(make_key(dist[1], key_pos(sel_keys[c0 + c2])));
+                const float *xs[kPerOctet];
+#pragma unroll
+                for (int kk = 0; kk < kPerOctet; ++kk) {
+                    const int c = cb + octet + kOct * kk;
+                    xs[kk] = stage + (c < rows_n ? c : 0) * stride;
+                }
+                float dist[kPerOctet];
+                octet_l2n<kPerOctet, false>(q, xs, d, j, lane & ~7, kFullMask, dist);
+#pragma unroll
+                for (int kk = 0; kk < kPerOctet; ++kk) {
+                    const int c = cb + octet + kOct * kk;
+                    if (j == 0 && c < rows_n)
+                        exact_keys[c0 + c] = dist[kk] < inf ? make_key(dist[kk], key_pos(sel_keys[c0 + c])) : kEmptyKey;
+                }
             }
-            __syncthreads();  // the next chunk overwrites the stage
-        }
-        if (stage_timeout) {
-            // a copy that never completed: let the copies in flight land
-            // (bounded) before the CTA's shared memory is released, and hand
-            // the frame to the exact re-run
-            tc::mbar_wait(&stage_bar, phase ^ 1u, kWaitLimitNs);
-            if (tid == 0) {
-                if (a.counters) atomicAdd(&a.counters->timeouts, 1ull);
-                const int pos = atomicAdd(a.fallback_count, 1);
-                a.fallback_list[pos] = static_cast<int32_t>(frame);
-            }
-            return;
+            __syncthreads();  // the next chunk overwrites the stage; exact_keys are complete
         }
     } else {
         for (int c0 = 0; c0 < m; c0 += 64) {
-            uint32_t rows[2];
-            const float *xs[2];
+            uint32_t rows[kPerOctet];
+            const float *xs[kPerOctet];
 #pragma unroll
-            for (int kk = 0; kk < 2; ++kk) {
-                const int c = c0 + octet + 32 * kk;
+            for (int kk = 0; kk < kPerOctet; ++kk) {
+                const int c = c0 + octet + kOct * kk;
                 rows[kk] = key_pos(sel_keys[c < m ? c : 0]);
                 xs[kk] = a.vectors + static_cast<size_t>(rows[kk]) * d;
             }
-            float dist[2];
-            octet_l2n<2>(q, xs, d, j, lane & ~7, kFullMask, dist);
+            float dist[kPerOctet];
+            octet_l2n<kPerOctet>(q, xs, d, j, lane & ~7, kFullMask, dist);
 #pragma unroll
-            for (int kk = 0; kk < 2; ++kk)
-                if (c0 + octet + 32 * kk < m && dist[kk] < inf) top.insert(make_key(dist[kk], rows[kk]));
+            for (int kk = 0; kk < kPerOctet; ++kk) {
+                const int c = c0 + octet + kOct * kk;
+                if (j == 0 && c < m) exact_keys[c] = dist[kk] < inf ? make_key(dist[kk], rows[kk]) : kEmptyKey;
+            }
+        }
+        __syncthreads();
+    }
+    // the frame's top 8: each re-ranked key's rank is the number of smaller
+    // keys (keys are distinct: one row each)
+    for (int c = tid; c < m; c += kT) {
+        const unsigned long long key = exact_keys[c];
+        if (key == kEmptyKey) continue;
+        int rank = 0;
+        for (int i = 0; i < m; ++i) rank += exact_keys[i] < key;
+        if (rank < 8) {
+            best[rank] = key;
+            best_slot[rank] = c;
         }
     }
-    if (j == 0)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) octet_best[octet * 8 + i] = top.k[i];
     __syncthreads();
-    merge_octet_lists(octet_best, best);
     int count = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) count += best[i] != kEmptyKey;
-    // in parallel: the certificate (thread 32), the neighbour weights
-    // (threads 0-7, one each) and, when the whole re-rank set is still
-    // staged, where each neighbour's row sits in the stage (warp w finds
-    // neighbour w)
+    // in parallel: the certificate (thread 32) and the neighbour weights
+    // (threads 0-7, one each)
     const bool staged_all = a.stage_rows > 0 && m <= a.stage_rows;
     if (tid == 32) {
         const float d8 = count == 8 ? key_dist(best[7]) : inf;
@@ -971,17 +1045,6 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
         certified_s = ok ? 1 : 0;
     }
     if (tid < 8) weights[tid] = tid < count ? reference_weight(key_dist(best[tid])) : 0.0;
-    if (staged_all && a.mode == kModeBlend) {
-        const int w = tid >> 5;
-        if (w < count) {
-            const uint32_t row = key_pos(best[w]);
-            int found = -1;
-            for (int c = lane; c < m; c += 32)
-                if (key_pos(sel_keys[c]) == row) found = c;
-            found = __reduce_max_sync(kFullMask, found);
-            if (lane == 0) best_slot[w] = found;
-        }
-    }
     __syncthreads();
     if (certified_s == 0) {
         if (tid == 0) {
@@ -1003,7 +1066,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
     if (count == 0) {
         if (tid == 0 && a.counters) atomicAdd(&a.counters->empty_frames, 1ull);
         if (dst != src)
-            for (int i = tid; i < d; i += kMergeThreads) dst[i] = q[i];
+            for (int i = tid; i < d; i += kT) dst[i] = q[i];
         return;
     }
     double w[8];
@@ -1018,7 +1081,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
         const int stride = stage_stride(d);
 #pragma unroll
         for (int kq = 0; kq < 8; ++kq) vrow[kq] = stage + (kq < count ? best_slot[kq] : 0) * stride;
-        for (int i = tid; i < d; i += kMergeThreads) {
+        for (int i = tid; i < d; i += kT) {
             float v[8];
 #pragma unroll
             for (int kq = 0; kq < 8; ++kq) v[kq] = vrow[kq][i];
@@ -1028,7 +1091,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeArgs a) {
         uint32_t rows[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) rows[i] = key_pos(best[i]);
-        for (int i = tid; i < d; i += kMergeThreads) {
+        for (int i = tid; i < d; i += kT) {
             float v[8];
 #pragma unroll
             for (int kq = 0; kq < 8; ++kq)
@@ -1148,16 +1211,28 @@ void launch_merge(VfrIndex *ix, MergeArgs &ma, size_t frames, cudaStream_t strea
     }
     const size_t smem = merge_smem(ma.sort_size, ma.thr_stride, ix->d, ma.stage_rows).total;
     require(smem <= static_cast<size_t>(ix->merge_smem_max), "candidate lists exceed the merge's shared memory");
-    cuda_check(launch_pdl(merge_kernel, dim3(static_cast<unsigned>(frames)), dim3(kMergeThreads), smem, stream, ma));
+    if (ma.stage_rows > 0)
+        cuda_check(launch_pdl(merge_kernel<kMergeThreadsMax>, dim3(static_cast<unsigned>(frames)),
+                              dim3(kMergeThreadsMax), smem, stream, ma));
+    else
+        cuda_check(launch_pdl(merge_kernel<kMergeThreads>, dim3(static_cast<unsigned>(frames)), dim3(kMergeThreads),
+                              smem, stream, ma));
 }
 
 // Launches the flat candidate kernel behind prep_queries_kernel (it starts
 // loading database tiles before the query tiles exist); the candidate list
 // size follows the work-item length.
-void launch_cand_flat(const Plan &p, int grid, const CUtensorMap &tmap_q, const CUtensorMap &tmap_x,
+void launch_cand_flat(const Plan &p, int grid, const void *q16, int d_pad, const CUtensorMap &tmap_x,
                       const CandArgs &ca, cudaStream_t stream) {
-    auto kernel = p.tiles_per_seg <= kShortItemTiles ? cand_kernel<false, kShortKeep> : cand_kernel<false, kIvfKeep>;
-    cuda_check(launch_pdl(kernel, dim3(grid), dim3(kThreadsTC), kSmemTC, stream, tmap_q, tmap_x, ca));
+    const bool small = ca.frames <= kSmallBlock;
+    CUtensorMap tmap_q;
+    encode_rows(&tmap_q, q16, d_pad, ca.frames, small ? kSmallBlock : kTileM);
+    const bool short_items = p.tiles_per_seg <= kShortItemTiles;
+    auto kernel = small ? (short_items ? cand_kernel<false, kShortKeep, kSmallBlock>
+                                       : cand_kernel<false, kIvfKeep, kSmallBlock>)
+                        : (short_items ? cand_kernel<false, kShortKeep> : cand_kernel<false, kIvfKeep>);
+    const size_t smem = small ? Pipe<kSmallBlock>::kSmem : Pipe<kTileM>::kSmem;
+    cuda_check(launch_pdl(kernel, dim3(grid), dim3(kThreadsTC), smem, stream, tmap_q, tmap_x, ca));
 }
 
 Plan make_plan(size_t frames, int64_t n, int sms) {
@@ -1285,10 +1360,10 @@ __global__ void __launch_bounds__(kMergeThreads) coarse_select_kernel(CoarseArgs
     const unsigned long long *fk = a.keys + static_cast<size_t>(frame) * real_slots;
 #pragma unroll 4
     for (int i = tid; i < a.slots; i += kMergeThreads) keys[i] = i < real_slots ? fk[i] : kEmptyKey;
-    const KeyStats ks = key_stats(keys, a.slots, tmin, sel);
+    const KeyStats ks = key_stats<kMergeThreads>(keys, a.slots, tmin, sel);
     float cut;
     bool too_many;
-    const int m = select_rerank(keys, a.slots, ks, sel_keys, sel, cut, too_many);
+    const int m = select_rerank<kMergeThreads>(keys, a.slots, ks, sel_keys, sel, cut, too_many);
     const float bound = fminf(ks.tmin, cut);
     // exact centroid distances; every centroid takes part, as in the
     // reference's sort (no +inf filter here)
@@ -1503,10 +1578,10 @@ __global__ void __launch_bounds__(kMergeThreads) ivf_merge_kernel(IvfMergeArgs a
         }
         keys[i] = key;
     }
-    const KeyStats ks = key_stats(keys, kSlots, tmin, sel);
+    const KeyStats ks = key_stats<kMergeThreads>(keys, kSlots, tmin, sel);
     float cut;
     bool too_many;
-    const int m = select_rerank(keys, kSlots, ks, sel_keys, sel, cut, too_many);
+    const int m = select_rerank<kMergeThreads>(keys, kSlots, ks, sel_keys, sel, cut, too_many);
     const float bound = fminf(ks.tmin, cut);
     // exact re-rank; the key's position is the reference's scan position
     Top8 top;
@@ -1537,7 +1612,7 @@ __global__ void __launch_bounds__(kMergeThreads) ivf_merge_kernel(IvfMergeArgs a
 #pragma unroll
         for (int i = 0; i < 8; ++i) octet_best[octet * 8 + i] = top.k[i];
     __syncthreads();
-    merge_octet_lists(octet_best, best);
+    merge_octet_lists<32>(octet_best, best);
     if (tid == 0) {
         int count = 0;
         while (count < 8 && best[count] != kEmptyKey) ++count;
@@ -1741,19 +1816,24 @@ void build_tc(VfrIndex *ix) {
     }
     encode_rows(&ix->tmap_vectors, ix->vectors_h, ix->d_pad, ix->n_pad, kTileN);
     if (ivf) encode_rows(&ix->tmap_centroids, ix->centroids_h, ix->d_pad, ix->nlist_pad, kTileN);
-    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kShortKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(kSmemTC)));
-    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(kSmemTC)));
-    cuda_check(cudaFuncSetAttribute(cand_kernel<true, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(kSmemTC)));
+    constexpr int kBig = static_cast<int>(Pipe<kTileM>::kSmem), kSmall = static_cast<int>(Pipe<kSmallBlock>::kSmem);
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kShortKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBig));
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBig));
+    cuda_check(cudaFuncSetAttribute(cand_kernel<true, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBig));
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kShortKeep, kSmallBlock>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmall));
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep, kSmallBlock>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmall));
     {
         int optin = 0;
         cuda_check(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ix->device));
-        cudaFuncAttributes fa{};
-        cuda_check(cudaFuncGetAttributes(&fa, merge_kernel));
-        ix->merge_smem_max = optin - static_cast<int>(fa.sharedSizeBytes);
-        cuda_check(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncAttributes fa{}, fb{};
+        cuda_check(cudaFuncGetAttributes(&fa, merge_kernel<kMergeThreads>));
+        cuda_check(cudaFuncGetAttributes(&fb, merge_kernel<kMergeThreadsMax>));
+        ix->merge_smem_max = optin - static_cast<int>(std::max(fa.sharedSizeBytes, fb.sharedSizeBytes));
+        cuda_check(cudaFuncSetAttribute(merge_kernel<kMergeThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        ix->merge_smem_max));
+        cuda_check(cudaFuncSetAttribute(merge_kernel<kMergeThreadsMax>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         ix->merge_smem_max));
     }
     cuda_check(cudaFuncSetAttribute(coarse_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
@@ -1862,7 +1942,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
     ix->prof.begin(kProfCand, stream);
-    cand_kernel<false, kIvfKeep><<<std::min(pc.segments * pc.n_qtiles, ix->sm_count), kThreadsTC, kSmemTC, stream>>>(
+    cand_kernel<false, kIvfKeep><<<std::min(pc.segments * pc.n_qtiles, ix->sm_count), kThreadsTC, Pipe<kTileM>::kSmem, stream>>>(
         tmap_q, ix->tmap_centroids, ca);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
@@ -1928,7 +2008,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     cf.list_start = list_start;
     cf.pair_stride = static_cast<int>(pair_cap);
     ix->prof.begin(kProfCand, stream);
-    cand_kernel<true, kIvfKeep><<<ix->sm_count, kThreadsTC, kSmemTC, stream>>>(tmap_qp, ix->tmap_vectors, cf);
+    cand_kernel<true, kIvfKeep><<<ix->sm_count, kThreadsTC, Pipe<kTileM>::kSmem, stream>>>(tmap_qp, ix->tmap_vectors, cf);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
 
@@ -2027,8 +2107,6 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
 
-    CUtensorMap tmap_q;
-    encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
     CandArgs ca{};
     ca.frames = static_cast<int>(frames);
     ca.n_qtiles = p.n_qtiles;
@@ -2047,7 +2125,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     const int items = p.segments * p.n_qtiles;
     const int grid = std::min(items, ix->sm_count);
     ix->prof.begin(kProfCand, stream);
-    launch_cand_flat(p, grid, tmap_q, ix->tmap_vectors, ca, stream);
+    launch_cand_flat(p, grid, q16, ix->d_pad, ix->tmap_vectors, ca, stream);
     ix->prof.end(stream);
 
     MergeArgs ma{};
@@ -2195,8 +2273,6 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
         features, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount);
     cuda_check(cudaGetLastError());
 
-    CUtensorMap tmap_q;
-    encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
     CandArgs ca{};
     ca.frames = static_cast<int>(frames);
     ca.n_qtiles = p.n_qtiles;
@@ -2213,7 +2289,7 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
-    launch_cand_flat(p, std::min(items, ix->sm_count), tmap_q, ix->tmap_vectors, ca, stream);
+    launch_cand_flat(p, std::min(items, ix->sm_count), q16, ix->d_pad, ix->tmap_vectors, ca, stream);
 
     MergeArgs ma{};
     ma.d = ix->d;
