@@ -102,8 +102,8 @@ __device__ __forceinline__ void octet_l2n(const float *__restrict__ q, const flo
     // Each unrolled body issues all its row loads before the dependent adds,
     // so the number of serialised memory round trips is d/8 / unroll: deep
     // for the few-row re-ranks (random rows, latency bound), shallower for
-    // the 4-row scans (register bound).
-    constexpr int kUnroll = N <= 2 ? 16 : 4;
+    // the 4-row scans (register bound) and for rows in shared memory.
+    constexpr int kUnroll = !kGlobal ? 8 : N <= 2 ? 16 : 4;
 #pragma unroll kUnroll
     for (int i = j; i < d8; i += 8) {
         const float qi = q[i];
@@ -146,16 +146,75 @@ __device__ __forceinline__ double reference_weights(const float *dist, int count
     return sum;
 }
 
+// Division by one frame's weight sum S, correctly rounded like the
+// reference's f64 `/`, for the frame's 8 x d quotients t / S.  With
+// y = RN(1/S) computed once, Markstein's FMA refinement (P. W. Markstein,
+// IBM J. Res. Develop. 34(1), 1990, the correction step of IA-64 division):
+// q0 = RN(t y); q1 = RN(q0 + RN(t - S q0) y) is within one ulp of t/S; then
+// r = t - S q1 is exact and RN(q1 + r y) = RN(t/S), y being within half an
+// ulp of 1/S.  The argument needs no overflow or underflow on the way, which
+// S in [2^-500, 2^500] and |t| in [2^-400, 2^400] guarantee; t == +-0 gives
+// t * y (exact, sign kept), other operands the divide instruction sequence.
+// tests/division_check.c checks the same operations against t / S.
+struct WeightDivisor {
+    double s, y;
+    bool fast;
+};
+__device__ __forceinline__ WeightDivisor weight_divisor(double s) {
+    WeightDivisor d;
+    d.s = s;
+    d.fast = s >= 0x1p-500 && s <= 0x1p500;
+    d.y = d.fast ? __drcp_rn(s) : 0.0;
+    return d;
+}
+// Markstein's quotient, valid for the operands `markstein_ok` admits.
+__device__ __forceinline__ double markstein_quotient(double t, const WeightDivisor &d) {
+    const double q0 = __dmul_rn(t, d.y);
+    const double r0 = __fma_rn(-d.s, q0, t);
+    const double q1 = __fma_rn(r0, d.y, q0);
+    const double r1 = __fma_rn(-d.s, q1, t);
+    const double q = __fma_rn(r1, d.y, q1);
+    return t == 0.0 ? q0 : q;
+}
+__device__ __forceinline__ bool markstein_ok(double t, const WeightDivisor &d) {
+    const double at = fabs(t);
+    return d.fast && (at == 0.0 || (at >= 0x1p-400 && at <= 0x1p400));
+}
+
 // One output element of the blend: retrieved from the gathered neighbour
-// values v[k] (k < count), then q*(1-r) + retrieved*r.
-__device__ __forceinline__ float reference_blend_element(float q, const float *v, const double *w, double sum,
-                                                         int count, float ratio) {
+// values v[k] (k < count), then q*(1-r) + retrieved*r; the quotients are
+// summed in the reference's order.  kSideBySide computes the 8 quotients as
+// independent chains (latency-bound callers with registers to spare; a
+// quotient outside Markstein's domain sends the element through the divide
+// instruction sequence); otherwise one quotient at a time.
+template <bool kSideBySide = false>
+__device__ __forceinline__ float reference_blend_element(float q, const float *v, const double *w,
+                                                         const WeightDivisor &sum, int count, float ratio) {
     double acc = -0.0;
+    if constexpr (kSideBySide) {
+        double t[8], quo[8];
+        bool ok = true;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        if (k < count) {
-            const double t = __dmul_rn(static_cast<double>(v[k]), w[k]);
-            acc = __dadd_rn(acc, __ddiv_rn(t, sum));
+        for (int k = 0; k < 8; ++k) {
+            t[k] = __dmul_rn(static_cast<double>(v[k]), w[k]);
+            quo[k] = markstein_quotient(t[k], sum);
+            ok = ok && (k >= count || markstein_ok(t[k], sum));
+        }
+        if (!ok) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (k < count) quo[k] = __ddiv_rn(t[k], sum.s);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (k < count) acc = __dadd_rn(acc, quo[k]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if (k < count) {
+                const double t = __dmul_rn(static_cast<double>(v[k]), w[k]);
+                acc = __dadd_rn(acc, markstein_ok(t, sum) ? markstein_quotient(t, sum) : __ddiv_rn(t, sum.s));
+            }
         }
     }
     float retrieved = __double2float_rn(acc);

@@ -219,7 +219,7 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame) {
         w[i] = weights[i];
         rows[i] = best_row[i];
     }
-    const double sum = weight_sum;
+    const WeightDivisor sum = weight_divisor(weight_sum);
     for (int i = tid; i < d; i += kThreads) {
         float v[8];
 #pragma unroll

@@ -90,7 +90,7 @@ __global__ void blend_gathered_kernel(const float *__restrict__ queries, float *
     }
     double w[8];
     for (int k = 0; k < 8; ++k) w[k] = weights[k];
-    const double sum = weight_sum;
+    const WeightDivisor sum = weight_divisor(weight_sum);
     const float *nb = neighbours + f * 8 * static_cast<long long>(d);
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
         float v[8];

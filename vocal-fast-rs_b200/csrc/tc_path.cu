@@ -621,6 +621,9 @@ struct SelectState {
     float red_f[kMergeThreadsMax / 32];
     int red_i[kMergeThreadsMax / 32];
     uint32_t red_lo[kMergeThreadsMax / 32], red_hi[kMergeThreadsMax / 32];
+    float all_f;
+    int all_i;
+    uint32_t all_lo, all_hi;
 };
 
 // The real keys among a CTA's key slots: how many, and the smallest and
@@ -660,41 +663,59 @@ __device__ KeyStats key_stats(const unsigned long long *keys, int slots, float t
         st.red_f[warp] = ks.tmin;
     }
     __syncthreads();
-    ks = KeyStats{0, 0xffffffffu, 0u, __int_as_float(0x7f800000)};
-    for (int w = 0; w < kT / 32; ++w) {
-        ks.total += st.red_i[w];
-        ks.lo = min(ks.lo, st.red_lo[w]);
-        ks.hi = max(ks.hi, st.red_hi[w]);
-        ks.tmin = fminf(ks.tmin, st.red_f[w]);
+    if (warp == 0) {  // combines the warps' partials, then every thread reads the result
+        const bool have = lane < kT / 32;
+        int t = have ? st.red_i[lane] : 0;
+        uint32_t l = have ? st.red_lo[lane] : 0xffffffffu, h = have ? st.red_hi[lane] : 0u;
+        float f = have ? st.red_f[lane] : __int_as_float(0x7f800000);
+        t = __reduce_add_sync(kFullMask, t);
+        l = __reduce_min_sync(kFullMask, l);
+        h = __reduce_max_sync(kFullMask, h);
+#pragma unroll
+        for (int s = 16; s > 0; s >>= 1) f = fminf(f, __shfl_xor_sync(kFullMask, f, s));
+        if (lane == 0) {
+            st.all_i = t;
+            st.all_lo = l;
+            st.all_hi = h;
+            st.all_f = f;
+        }
     }
-    return ks;
+    __syncthreads();
+    return KeyStats{st.all_i, st.all_lo, st.all_hi, st.all_f};
 }
 
 // Keys kept for the exact re-rank when a radix pass can stop early: the pass
 // stops once the keys at or below the bin holding the kRerank-th smallest
-// distance number at most this many.
+// distance number at most this many (or fewer, as the caller asks: the rows
+// its shared memory can stage at once).
 constexpr int kRerankStop = 80;
+
+constexpr int kWideBins = 4096;  // bins of the optional 12-bit first pass
 
 // Chooses the keys to re-rank among keys[0 .. slots) (ks from key_stats; the
 // slots past the real keys hold kEmptyKey; slots a multiple of 32) without
-// sorting them.  A radix
-// select over the distance bits below the real keys' common prefix finds the
-// digit bin holding the kRerank-th smallest distance; it refines that bin with
-// further 8-bit digits only while the keys at or below it number more than
-// kRerankStop.  Every key at or below the final bin is kept (kRerank to
-// kRerankStop keys, or up to kRerankMax when distances tie in every bit, with
-// `too_many` reporting an overflow past kRerankMax).  Every dropped key has a
-// larger approximate distance than every kept one; `bound` is the smallest
-// dropped distance (+inf when nothing is dropped).  Histogram updates are
-// aggregated per warp (match_any), so a crowded digit costs one shared atomic
-// per warp.  Returns the number of keys written to sel_keys.  Called by every
-// thread of the CTA.
+// sorting them.  A radix select over the distance bits below the real keys'
+// common prefix finds the digit bin holding the kRerank-th smallest distance
+// (a first 12-bit digit when the caller lends a `wide` histogram of
+// kWideBins cleared bins, then 8-bit digits); it refines that bin only while
+// the keys at or below it number more than rerank_stop.  Every key at or
+// below the final bin is kept (kRerank to rerank_stop keys, or up to
+// kRerankMax when distances tie in every bit, with `too_many` reporting an
+// overflow past kRerankMax).  Every dropped key has a larger approximate
+// distance than every kept one; `bound` is the smallest dropped distance
+// (+inf when nothing is dropped).  Histogram updates are aggregated per warp
+// (match_any), so a crowded digit costs one shared atomic per warp.
+// Returns the number of keys written to sel_keys.  Called by every thread of
+// the CTA.
+
 template <int kT>
 __device__ int select_rerank(const unsigned long long *keys, int slots, const KeyStats &ks,
-                             unsigned long long *sel_keys, SelectState &st, float &bound, bool &too_many) {
+                             unsigned long long *sel_keys, SelectState &st, float &bound, bool &too_many,
+                             unsigned int *wide = nullptr, int rerank_stop = kRerankStop) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int total = ks.total;
     const uint32_t lo = ks.lo, hi = ks.hi;
+    const uint32_t stop = static_cast<uint32_t>(rerank_stop);
     uint32_t limit = 0xffffffffu;  // keep every real key whose distance bits are <= limit
     if (total > kRerank) {
         if (lo == hi) {
@@ -704,8 +725,70 @@ __device__ int select_rerank(const unsigned long long *keys, int slots, const Ke
             uint32_t mask_bits = ~((2u << top) - 1u);    // the common prefix (0 when top == 31)
             uint32_t prefix = lo & mask_bits;
             uint32_t rank = kRerank, below = 0;          // 1-based rank inside the prefix group
+            bool done = false;
+            if (wide != nullptr) {
+                // One 12-bit pass (kWideBins bins, cleared by the caller;
+                // every real key shares the prefix here), usually enough on
+                // its own.  Thread t owns bins [t * kPerLane, +kPerLane).
+                constexpr int kPerLane = kWideBins / kT;
+                const int shift = top > 11 ? top - 11 : 0;
+                const uint32_t digits = (2u << (top - shift)) - 1u;
+                for (int i = tid; i < slots; i += kT) {
+                    const unsigned long long key = keys[i];
+                    const bool in = key != kEmptyKey;
+                    const uint32_t digit = in ? (static_cast<uint32_t>(key >> 32) >> shift) & digits : 0xffffffffu;
+                    const unsigned peers = __match_any_sync(kFullMask, digit);
+                    if (in && lane == __ffs(peers) - 1) atomicAdd(&wide[digit], __popc(peers));
+                }
+                __syncthreads();
+                uint32_t c[kPerLane], sum = 0;
+#pragma unroll
+                for (int k = 0; k < kPerLane; ++k) {
+                    c[k] = wide[tid * kPerLane + k];
+                    sum += c[k];
+                }
+                uint32_t incl = sum;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const uint32_t up = __shfl_up_sync(kFullMask, incl, off);
+                    if (lane >= off) incl += up;
+                }
+                if (lane == 31) st.red_i[warp] = static_cast<int>(incl);
+                __syncthreads();
+                uint32_t before = 0;
+                for (int w = 0; w < warp; ++w) before += static_cast<uint32_t>(st.red_i[w]);
+                if (tid == kT - 1 && before + incl < rank) {  // cannot happen: `total` counts the real keys
+                    st.bin = digits;
+                    st.below_bin = 0u;
+                    st.in_bin = kRerankMax + 1u;
+                }
+                uint32_t acc = before + incl - sum;
+                if (acc < rank && rank <= before + incl) {
+                    for (int k = 0; k < kPerLane; ++k) {
+                        if (acc + c[k] >= rank) {
+                            st.bin = static_cast<uint32_t>(tid * kPerLane + k);
+                            st.below_bin = acc;
+                            st.in_bin = c[k];
+                            break;
+                        }
+                        acc += c[k];
+                    }
+                }
+                __syncthreads();
+                const uint32_t bin = st.bin, acc_b = st.below_bin, cnt = st.in_bin;
+                if (below + acc_b + cnt <= stop || shift == 0) {
+                    limit = prefix | (bin << shift) | ((1u << shift) - 1u);
+                    done = true;
+                } else {
+                    below += acc_b;
+                    rank -= acc_b;
+                    prefix |= bin << shift;
+                    mask_bits |= digits << shift;
+                    top = shift - 1;
+                }
+            }
             int pass = 0;
-            while (true) {
+            while (!done) {
                 const int shift = top > 7 ? top - 7 : 0;
                 const uint32_t digits = (2u << (top - shift)) - 1u;
                 unsigned int *hist = st.hist[pass & 1];  // cleared before this pass
@@ -754,7 +837,7 @@ __device__ int select_rerank(const unsigned long long *keys, int slots, const Ke
                 }
                 __syncthreads();
                 const uint32_t bin = st.bin, acc = st.below_bin, cnt = st.in_bin;
-                if (below + acc + cnt <= static_cast<uint32_t>(kRerankStop) || shift == 0) {
+                if (below + acc + cnt <= stop || shift == 0) {
                     limit = prefix | (bin << shift) | ((1u << shift) - 1u);
                     break;
                 }
@@ -849,27 +932,56 @@ __device__ __forceinline__ bool certify(float bound, float dk, float4 qs, float 
     return lower > dk * (1.f + 4.f * exact_rel) + 1e-30f;
 }
 
+// Exact distances of staged rows [0, rows) (stage rows of `stride` floats;
+// sel_keys / exact_keys indexed from c0): octet o takes rows o, o + kOct, ...
+// up to N rows.  Called by every thread; +inf and NaN distances become
+// kEmptyKey (they never enter a top-8 list in the reference).
+template <int N, int kOct>
+__device__ __forceinline__ void stage_distances(const float *q, const float *stage, int stride, int rows, int c0,
+                                                int d, int octet, int j, int lane, const unsigned long long *sel_keys,
+                                                unsigned long long *exact_keys) {
+    const float *xs[N];
+#pragma unroll
+    for (int kk = 0; kk < N; ++kk) {
+        const int c = octet + kOct * kk;
+        xs[kk] = stage + (c < rows ? c : 0) * stride;
+    }
+    float dist[N];
+    octet_l2n<N, false>(q, xs, d, j, lane & ~7, kFullMask, dist);
+#pragma unroll
+    for (int kk = 0; kk < N; ++kk) {
+        const int c = octet + kOct * kk;
+        if (j == 0 && c < rows)
+            exact_keys[c0 + c] = dist[kk] < __int_as_float(0x7f800000) ? make_key(dist[kk], key_pos(sel_keys[c0 + c]))
+                                                                       : kEmptyKey;
+    }
+}
+
 // Shared-memory row stride of the staged re-rank rows, in floats: 8 floats
 // of padding put the 4 rows a warp reads at once on different banks.
 __host__ __device__ constexpr int stage_stride(int d) { return d + 8; }
 
-// Dynamic shared memory of merge_kernel: key slots, thresholds, the query
-// row and the re-rank stage, each 16-byte aligned.
+// Dynamic shared memory of merge_kernel: thresholds, the query row, then one
+// region that holds the key slots and (with a stage) the 12-bit radix
+// histogram while the re-rank set is chosen, and the staged rows after.
 struct MergeSmem {
-    size_t keys, thr, q, stage, total;
+    size_t thr, q, keys, wide, stage, total;
 };
 __host__ __device__ inline MergeSmem merge_smem(int sort_size, int thr_stride, int d, int stage_rows) {
     MergeSmem m{};
-    m.keys = 0;
-    m.thr = static_cast<size_t>(sort_size) * 8;
-    m.q = m.thr + static_cast<size_t>(thr_stride) * 4;
-    m.stage = m.q + static_cast<size_t>((d + 3) & ~3) * 4;
-    m.total = m.stage + static_cast<size_t>(stage_rows) * stage_stride(d) * 4;
+    m.thr = 0;
+    m.q = static_cast<size_t>(thr_stride) * 4;  // thr_stride is a multiple of 4
+    m.keys = m.q + static_cast<size_t>((d + 3) & ~3) * 4;
+    m.wide = m.keys + ((static_cast<size_t>(sort_size) * 8 + 255) & ~size_t(255));
+    m.stage = m.keys;
+    const size_t select_end = stage_rows > 0 ? m.wide + kWideBins * 4 : m.wide;
+    const size_t stage_end = m.stage + static_cast<size_t>(stage_rows) * stage_stride(d) * 4;
+    m.total = select_end > stage_end ? select_end : stage_end;
     return m;
 }
 
 template <int kT>
-__global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
+__global__ void __launch_bounds__(kT, kT == kMergeThreads ? 3 : 1) merge_kernel(MergeArgs a) {
     constexpr int kOct = kT / 8;           // octets: 8 threads per exact distance
     constexpr int kPerOctet = 64 / kOct;   // rows per octet per pass of 64 rows
     extern __shared__ __align__(16) uint8_t msm[];
@@ -878,6 +990,7 @@ __global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
     float *thr = reinterpret_cast<float *>(msm + lay.thr);
     float *q = reinterpret_cast<float *>(msm + lay.q);
     float *stage = reinterpret_cast<float *>(msm + lay.stage);
+    unsigned int *wide = a.stage_rows > 0 ? reinterpret_cast<unsigned int *>(msm + lay.wide) : nullptr;
     __shared__ unsigned long long exact_keys[kRerankMax];  // (exact distance, row) per re-ranked key
     __shared__ unsigned long long best[8];
     __shared__ int certified_s;
@@ -903,11 +1016,15 @@ __global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
         tc::fence_mbarrier_init();
     }
     if (tid < 8) best[tid] = kEmptyKey;
+    if (wide)
+        for (int i = tid; i < kWideBins; i += kT) wide[i] = 0u;
     // the caller's inputs first, while the candidate kernel may still run
     const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
     for (int i = tid; i < d; i += kT) q[i] = src[i];
     for (int i = real_slots + tid; i < a.sort_size; i += kT) keys[i] = kEmptyKey;
     grid_dependency_wait();
+    // the certifying thread's query stats, early (prepared two kernels back)
+    const float4 qstat = tid == 32 ? a.qstats[frame] : make_float4(0.f, 0.f, 0.f, 0.f);
     // then the frame's candidate block (keys, thresholds): two bulk copies.
     // Warp 0 alone polls the barriers (a thread parked in a barrier poll can
     // resume microseconds after the phase completes); the CTA barrier that
@@ -945,7 +1062,8 @@ __global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
     const KeyStats ks = key_stats<kT>(keys, a.sort_size, tmin, sel);
     float cut;
     bool too_many_ties;
-    const int m = select_rerank<kT>(keys, a.sort_size, ks, sel_keys, sel, cut, too_many_ties);
+    const int stop = a.stage_rows >= kRerank ? min(kRerankStop, a.stage_rows) : kRerankStop;
+    const int m = select_rerank<kT>(keys, a.sort_size, ks, sel_keys, sel, cut, too_many_ties, wide, stop);
     const float t_final = fminf(ks.tmin, cut);
 
     // exact re-rank in the reference order (flat scan position == row): one
@@ -960,6 +1078,9 @@ __global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
             const int rows_n = min(a.stage_rows, m - c0);
             bool arrived = true;
             if (warp == 0) {
+                // the stage reuses the key slots and histogram that the
+                // threads have just read and updated
+                tc::fence_proxy_async_smem();
                 if (lane == 0) tc::mbar_arrive_expect_tx(&stage_bar, static_cast<uint32_t>(rows_n * d * 4));
                 __syncwarp();
                 for (int i = lane; i < rows_n; i += 32)
@@ -980,23 +1101,15 @@ __global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
                 }
                 return;
             }
-            // warp-uniform trip count: every octet takes part in the shuffles
-            for (int cb = 0; cb < rows_n; cb += 64) {
-                const float *xs[kPerOctet];
-#pragma unroll
-                for (int kk = 0; kk < kPerOctet; ++kk) {
-                    const int c = cb + octet + kOct * kk;
-                    xs[kk] = stage + (c < rows_n ? c : 0) * stride;
-                }
-                float dist[kPerOctet];
-                octet_l2n<kPerOctet, false>(q, xs, d, j, lane & ~7, kFullMask, dist);
-#pragma unroll
-                for (int kk = 0; kk < kPerOctet; ++kk) {
-                    const int c = cb + octet + kOct * kk;
-                    if (j == 0 && c < rows_n)
-                        exact_keys[c0 + c] = dist[kk] < inf ? make_key(dist[kk], key_pos(sel_keys[c0 + c])) : kEmptyKey;
-                }
-            }
+            // warp-uniform trip counts: every octet takes part in the
+            // shuffles; an octet takes two rows when the chunk has more rows
+            // than octets (one pass, the query loads shared)
+            if (rows_n <= kOct)
+                stage_distances<1, kOct>(q, stage, stride, rows_n, c0, d, octet, j, lane, sel_keys, exact_keys);
+            else
+                for (int cb = 0; cb < rows_n; cb += 2 * kOct)
+                    stage_distances<2, kOct>(q, stage + cb * stride, stride, rows_n - cb, c0 + cb, d, octet, j, lane,
+                                             sel_keys, exact_keys);
             __syncthreads();  // the next chunk overwrites the stage; exact_keys are complete
         }
     } else {
@@ -1040,8 +1153,8 @@ __global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
     const bool staged_all = a.stage_rows > 0 && m <= a.stage_rows;
     if (tid == 32) {
         const float d8 = count == 8 ? key_dist(best[7]) : inf;
-        const bool ok = !too_many_ties && certify(t_final, d8, a.qstats[frame], a.max_norm, a.max_hat,
-                                                  a.max_residual, a.acc_rel, a.norm_rel, a.exact_rel);
+        const bool ok = !too_many_ties && certify(t_final, d8, qstat, a.max_norm, a.max_hat, a.max_residual,
+                                                  a.acc_rel, a.norm_rel, a.exact_rel);
         certified_s = ok ? 1 : 0;
     }
     if (tid < 8) weights[tid] = tid < count ? reference_weight(key_dist(best[tid])) : 0.0;
@@ -1070,12 +1183,13 @@ __global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
         return;
     }
     double w[8];
-    double sum = -0.0;  // the reference's order: S = w0 + w1 + ... (zeros past count)
+    double wsum = -0.0;  // the reference's order: S = w0 + w1 + ... (zeros past count)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         w[i] = weights[i];
-        sum = __dadd_rn(sum, w[i]);
+        wsum = __dadd_rn(wsum, w[i]);
     }
+    const WeightDivisor sum = weight_divisor(wsum);
     if (staged_all) {
         const float *vrow[8];
         const int stride = stage_stride(d);
@@ -1085,7 +1199,7 @@ __global__ void __launch_bounds__(kT) merge_kernel(MergeArgs a) {
             float v[8];
 #pragma unroll
             for (int kq = 0; kq < 8; ++kq) v[kq] = vrow[kq][i];
-            dst[i] = reference_blend_element(q[i], v, w, sum, count, ratio);
+            dst[i] = reference_blend_element<kT == kMergeThreadsMax>(q[i], v, w, sum, count, ratio);
         }
     } else {
         uint32_t rows[8];
@@ -1202,7 +1316,9 @@ void launch_merge(VfrIndex *ix, MergeArgs &ma, size_t frames, cudaStream_t strea
     ma.stage_rows = 0;
     if (ix->d % 4 == 0 && reinterpret_cast<uintptr_t>(ix->vectors) % 16 == 0 &&
         frames <= static_cast<size_t>(ix->sm_count) * 2) {
-        for (int rows : {64, 32})
+        // as many rows as fit, up to kRerankStop (the usual re-rank set); at
+        // least 32, else the rows stay in global memory
+        for (int rows = kRerankStop; rows >= 32; --rows)
             if (merge_smem(ma.sort_size, ma.thr_stride, ix->d, rows).total <=
                 static_cast<size_t>(ix->merge_smem_max)) {
                 ma.stage_rows = rows;
@@ -1531,7 +1647,7 @@ struct IvfMergeArgs {
     DeviceCounters *counters;
 };
 
-__global__ void __launch_bounds__(kMergeThreads) ivf_merge_kernel(IvfMergeArgs a) {
+__global__ void __launch_bounds__(kMergeThreads, 3) ivf_merge_kernel(IvfMergeArgs a) {
     constexpr int kSlots = kIvfMaxProbe * kHalves * kItemKeep;
     extern __shared__ __align__(16) float iq[];  // [d]
     __shared__ unsigned long long keys[kSlots];
@@ -1674,7 +1790,7 @@ __global__ void __launch_bounds__(kMergeThreads) ivf_merge_kernel(IvfMergeArgs a
         w[i] = weights[i];
         rows[i] = best_row[i];
     }
-    const double sum = weight_sum;
+    const WeightDivisor sum = weight_divisor(weight_sum);
     for (int i = tid; i < d; i += kMergeThreads) {
         float v[8];
 #pragma unroll
