@@ -56,23 +56,59 @@ constexpr int kHalves = 2;       // candidate lists per (work item, frame)
 constexpr int kThreadsTC = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr uint32_t kBBytes = kTileN * kTileK * 2;
 constexpr uint32_t kNormBytes = kEpiWarps * 2 * (kTileN / kHalves) * sizeof(float);  // per warp, double buffered
-constexpr int kSmallBlock = 32;  // frame blocks up to this size load a 32-row query box
+constexpr int kSmallBlock = 32;  // frame blocks up to this size use the spread layout
 
-// Pipeline shape of cand_kernel for a query box of kARows rows.  The MMA is
-// always M = 128; with a 32-row box (a block of at most 32 frames) the stage
-// holds 4 KB of query rows instead of 16 KB, the MMA's rows 32-127 read
-// whatever follows in the stage (their TMEM lanes are never read), and the
-// shared memory saved buys two more stages: 192 KB of database tiles in
-// flight per SM instead of 128 KB.
-template <int kARows>
-struct Pipe {
-    static constexpr int kStages = kARows == kTileM ? 4 : 6;
-    static constexpr uint32_t kABytes = kARows * kTileK * 2;
-    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-    static constexpr size_t kSmem = 1024 + kStages * kStageBytes + kNormBytes + 256;
+// Shared-memory layouts of cand_kernel.  The MMA is always M = 128: query
+// row m of the A tile feeds TMEM lane m, and an epilogue warp can read only
+// the 32 lanes of its quarter (warp % 4), all four of whose warps run on
+// one SM sub-partition.
+//
+// kFullLayout: 128 query rows per tile, 4 stages of (A 16 KB, B 32 KB).
+//
+// kSpreadLayout (blocks of at most 32 frames): the frames go to A rows
+// 0-7, 32-39, 64-71 and 96-103 (four TMA boxes of 8 rows), so all four lane
+// quarters, and all eight epilogue warps on four sub-partitions, share the
+// per-tile filtering that otherwise falls on two warps of one.  The 1 KB
+// A blocks of four stages interleave in one 16 KB pack (stage s at s KB,
+// quarter q at +4q KB); the MMA's other A rows read whatever lies there
+// (their TMEM lanes are never read).  Six stages: two packs (the second
+// pack's free 2 KB pieces hold the row-norm buffers) and six 32 KB B tiles,
+// 192 KB of database tiles in flight per SM.
+enum { kFullLayout = 0, kSpreadLayout = 1 };
+template <int kLayout>
+struct Pipe;
+template <>
+struct Pipe<kFullLayout> {
+    static constexpr int kStages = 4;
+    static constexpr int kBlocks = 1;            // A boxes per stage
+    static constexpr int kBlockRows = kTileM;    // rows per A box
+    static constexpr int kRowsPerQuarter = 32;   // real A rows per TMEM lane quarter
+    static constexpr uint32_t kTx = kTileM * kTileK * 2 + kBBytes;
+    __host__ __device__ static constexpr uint32_t a_off(int s) { return s * (16384u + kBBytes); }
+    __host__ __device__ static constexpr uint32_t a_block_off(int s, int) { return a_off(s); }
+    __host__ __device__ static constexpr uint32_t b_off(int s) { return a_off(s) + 16384u; }
+    __host__ __device__ static constexpr uint32_t norm_off(int ew) { return kStages * (16384u + kBBytes) + ew * 1024u; }
+    static constexpr uint32_t kBarOff = kStages * (16384u + kBBytes) + kNormBytes;
+    static constexpr size_t kSmem = 1024 + kBarOff + 256;
 };
-static_assert(Pipe<kTileM>::kSmem <= 232448 && Pipe<kSmallBlock>::kSmem <= 232448, "cand_kernel shared memory");
-static_assert(Pipe<kSmallBlock>::kStageBytes % 1024 == 0, "stage bases stay 1024-byte aligned");
+template <>
+struct Pipe<kSpreadLayout> {
+    static constexpr int kStages = 6;
+    static constexpr int kBlocks = 4;
+    static constexpr int kBlockRows = 8;
+    static constexpr int kRowsPerQuarter = 8;
+    static constexpr uint32_t kTx = 4 * 1024 + kBBytes;
+    __host__ __device__ static constexpr uint32_t a_off(int s) { return (s / 4) * 16384u + (s % 4) * 1024u; }
+    __host__ __device__ static constexpr uint32_t a_block_off(int s, int q) { return a_off(s) + q * 4096u; }
+    __host__ __device__ static constexpr uint32_t b_off(int s) { return 32768u + s * kBBytes; }
+    __host__ __device__ static constexpr uint32_t norm_off(int ew) {
+        return 16384u + (ew / 2) * 4096u + 2048u + (ew % 2) * 1024u;
+    }
+    static constexpr uint32_t kBarOff = 32768u + kStages * kBBytes;
+    static constexpr size_t kSmem = 1024 + kBarOff + 256;
+};
+static_assert(Pipe<kFullLayout>::kSmem <= 232448 && Pipe<kSpreadLayout>::kSmem <= 232448, "cand_kernel shared memory");
+static_assert(kNormBytes == kEpiWarps * 1024, "one 1 KB row-norm double buffer per epilogue warp");
 constexpr uint32_t kTmemCols = 512;  // two 128 x 256 fp32 accumulators
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kFormatF16 = 0;
@@ -236,16 +272,15 @@ __device__ __forceinline__ float4 load_norms4(const float *p) {
     else return __ldg(reinterpret_cast<const float4 *>(p));
 }
 
-template <bool kIvf, int K, int kARows = kTileM>
+template <bool kIvf, int K, int kLayout = kFullLayout>
 __global__ void __launch_bounds__(kThreadsTC, 1)
     cand_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, CandArgs a) {
-    constexpr int kStages = Pipe<kARows>::kStages;
-    constexpr uint32_t kABytes = Pipe<kARows>::kABytes;
-    constexpr uint32_t kStageBytes = Pipe<kARows>::kStageBytes;
+    using P = Pipe<kLayout>;
+    constexpr int kStages = P::kStages;
+    static_assert(!kIvf || kLayout == kFullLayout, "IVF work items use the full layout");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *norm_smem = reinterpret_cast<float *>(smem + kStages * kStageBytes);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes + kNormBytes);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P::kBarOff);
     uint64_t *full = bars;
     uint64_t *empty = bars + kStages;
     uint64_t *acc_full = bars + 2 * kStages;
@@ -304,8 +339,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     early = min(kStages, it0.tiles * a.ksteps);
                     for (int s = 0; s < early; ++s) {
                         const int t = s / a.ksteps, k = s % a.ksteps;
-                        tc::mbar_arrive_expect_tx(&full[s], kStageBytes);
-                        tc::tma_load_2d(smem + s * kStageBytes + kABytes, &tmap_x, &full[s], k * kTileK,
+                        tc::mbar_arrive_expect_tx(&full[s], P::kTx);
+                        tc::tma_load_2d(smem + P::b_off(s), &tmap_x, &full[s], k * kTileK,
                                         static_cast<int32_t>(it0.b_row0 + t * kTileN));
                     }
                 }
@@ -322,19 +357,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                             fail();
                             break;
                         }
-                        uint8_t *sa = smem + stage * kStageBytes;
-                        if (issued < early) {  // database tile already requested
-                            tc::tma_load_2d(sa, &tmap_q, &full[stage], k * kTileK, it.a_row0);
-                            if (++stage == kStages) {
-                                stage = 0;
-                                phase ^= 1;
-                            }
-                            continue;
+                        if (issued >= early) {  // else the database tile is already requested
+                            tc::mbar_arrive_expect_tx(&full[stage], P::kTx);
+                            tc::tma_load_2d(smem + P::b_off(stage), &tmap_x, &full[stage], k * kTileK,
+                                            static_cast<int32_t>(it.b_row0 + t * kTileN));
                         }
-                        tc::mbar_arrive_expect_tx(&full[stage], kStageBytes);
-                        tc::tma_load_2d(sa, &tmap_q, &full[stage], k * kTileK, it.a_row0);
-                        tc::tma_load_2d(sa + kABytes, &tmap_x, &full[stage], k * kTileK,
-                                        static_cast<int32_t>(it.b_row0 + t * kTileN));
+#pragma unroll
+                        for (int qb = 0; qb < P::kBlocks; ++qb)
+                            tc::tma_load_2d(smem + P::a_block_off(stage, qb), &tmap_q, &full[stage], k * kTileK,
+                                            it.a_row0 + qb * P::kBlockRows);
                         if (++stage == kStages) {
                             stage = 0;
                             phase ^= 1;
@@ -380,8 +411,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                             break;
                         }
                         tc::tc_fence_after();
-                        const uint32_t sa = tc::smem_u32(smem + stage * kStageBytes);
-                        const uint32_t sb = sa + kABytes;
+                        const uint32_t sa = tc::smem_u32(smem + P::a_off(stage));
+                        const uint32_t sb = tc::smem_u32(smem + P::b_off(stage));
 #pragma unroll
                         for (int kk = 0; kk < kTileK / 16; ++kk) {
                             tc::mma_f16(d_tmem, tc::smem_desc_sw128(sa + kk * 32), tc::smem_desc_sw128(sb + kk * 32),
@@ -407,7 +438,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const int quarter = warp & 3;  // TMEM lanes this warp may access
         const int half = ew >> 2;
         constexpr int kHalfCols = kTileN / kHalves;
-        const int r = quarter * 32 + lane;
+        // this lane's frame in the tile: lanes past the layout's rows per
+        // quarter hold no frame (spread layout)
+        const int r = quarter * P::kRowsPerQuarter + lane;
+        const bool lane_real = lane < P::kRowsPerQuarter;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         uint32_t acc_count = 0;
         const float inf = __int_as_float(0x7f800000);
@@ -419,9 +453,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             top.init();
             bool aborted = false;
             // This warp's copy of the row norms, one tile ahead: lane l holds
-            // norms [8l, 8l+8) of the next tile in registers until the current
-            // tile is done, then stores them into the other buffer.
-            float *nbuf = norm_smem + ew * 2 * kHalfCols;
+            // norms [4l, 4l+4) of the next tile's half in registers until the
+            // current tile is done, then stores them into the other buffer.
+            float *nbuf = reinterpret_cast<float *>(smem + P::norm_off(ew));
             {
                 reinterpret_cast<float4 *>(nbuf)[lane] = load_norms4<kIvf>(a.row_norms + row0 + half * kHalfCols + lane * 4);
                 __syncwarp();
@@ -440,7 +474,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     break;
                 }
                 tc::tc_fence_after();
-                if (quarter * 32 >= it.a_rows) {
+                if (quarter * P::kRowsPerQuarter >= it.a_rows) {
                     // every TMEM lane of this warp is a padding row of a partial
                     // frame tile: release the accumulator without reading it
                     tc::tc_fence_before();
@@ -482,6 +516,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                             mask |= (dd[e] < thr ? 1u : 0u) << e;
                         }
                     }
+                    if (!lane_real) mask = 0u;  // no frame in this lane: its values are not distances
                     // many survivors (the start of an item): one bulk merge for
                     // the warp; otherwise insert the few survivors one by one
                     // (re-checked, the threshold drops as they go in)
@@ -525,7 +560,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     a.out_count[half * stride + pos] = cnt;
                     a.out_thr[half * stride + pos] = cnt == K ? top.dist[K - 1] : inf;
                 }
-            } else if (r < it.a_rows) {
+            } else if (lane_real && r < it.a_rows) {
                 // every slot is written (kEmptyKey past cnt), so the merge
                 // copies a frame's block without reading counts
                 const size_t frame = static_cast<size_t>(it.a_row0) + r;
@@ -1342,12 +1377,13 @@ void launch_cand_flat(const Plan &p, int grid, const void *q16, int d_pad, const
                       const CandArgs &ca, cudaStream_t stream) {
     const bool small = ca.frames <= kSmallBlock;
     CUtensorMap tmap_q;
-    encode_rows(&tmap_q, q16, d_pad, ca.frames, small ? kSmallBlock : kTileM);
+    encode_rows(&tmap_q, q16, d_pad, ca.frames,
+                small ? Pipe<kSpreadLayout>::kBlockRows : Pipe<kFullLayout>::kBlockRows);
     const bool short_items = p.tiles_per_seg <= kShortItemTiles;
-    auto kernel = small ? (short_items ? cand_kernel<false, kShortKeep, kSmallBlock>
-                                       : cand_kernel<false, kIvfKeep, kSmallBlock>)
+    auto kernel = small ? (short_items ? cand_kernel<false, kShortKeep, kSpreadLayout>
+                                       : cand_kernel<false, kIvfKeep, kSpreadLayout>)
                         : (short_items ? cand_kernel<false, kShortKeep> : cand_kernel<false, kIvfKeep>);
-    const size_t smem = small ? Pipe<kSmallBlock>::kSmem : Pipe<kTileM>::kSmem;
+    const size_t smem = small ? Pipe<kSpreadLayout>::kSmem : Pipe<kFullLayout>::kSmem;
     cuda_check(launch_pdl(kernel, dim3(grid), dim3(kThreadsTC), smem, stream, tmap_q, tmap_x, ca));
 }
 
@@ -1932,13 +1968,13 @@ void build_tc(VfrIndex *ix) {
     }
     encode_rows(&ix->tmap_vectors, ix->vectors_h, ix->d_pad, ix->n_pad, kTileN);
     if (ivf) encode_rows(&ix->tmap_centroids, ix->centroids_h, ix->d_pad, ix->nlist_pad, kTileN);
-    constexpr int kBig = static_cast<int>(Pipe<kTileM>::kSmem), kSmall = static_cast<int>(Pipe<kSmallBlock>::kSmem);
+    constexpr int kBig = static_cast<int>(Pipe<kFullLayout>::kSmem), kSmall = static_cast<int>(Pipe<kSpreadLayout>::kSmem);
     cuda_check(cudaFuncSetAttribute(cand_kernel<false, kShortKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBig));
     cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBig));
     cuda_check(cudaFuncSetAttribute(cand_kernel<true, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBig));
-    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kShortKeep, kSmallBlock>,
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kShortKeep, kSpreadLayout>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kSmall));
-    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep, kSmallBlock>,
+    cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep, kSpreadLayout>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kSmall));
     {
         int optin = 0;
@@ -2058,7 +2094,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
     ix->prof.begin(kProfCand, stream);
-    cand_kernel<false, kIvfKeep><<<std::min(pc.segments * pc.n_qtiles, ix->sm_count), kThreadsTC, Pipe<kTileM>::kSmem, stream>>>(
+    cand_kernel<false, kIvfKeep><<<std::min(pc.segments * pc.n_qtiles, ix->sm_count), kThreadsTC, Pipe<kFullLayout>::kSmem, stream>>>(
         tmap_q, ix->tmap_centroids, ca);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
@@ -2124,7 +2160,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     cf.list_start = list_start;
     cf.pair_stride = static_cast<int>(pair_cap);
     ix->prof.begin(kProfCand, stream);
-    cand_kernel<true, kIvfKeep><<<ix->sm_count, kThreadsTC, Pipe<kTileM>::kSmem, stream>>>(tmap_qp, ix->tmap_vectors, cf);
+    cand_kernel<true, kIvfKeep><<<ix->sm_count, kThreadsTC, Pipe<kFullLayout>::kSmem, stream>>>(tmap_qp, ix->tmap_vectors, cf);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
 
