@@ -253,6 +253,67 @@ def streaming(device):
             "fallback_frames": diag["fallback_frames"]}
 
 
+def protection(device):
+    """The step after the blend on the realtime path: the raw copy fused into
+    the blend (vfr_retrieval_blend_save_raw) against the reference's separate
+    device copy + blend, and vocal_retrieval_protect on the interpolated block
+    (2 x 32 + 1 frames x 768, half of them unvoiced), each replayed from a
+    CUDA graph (p50 over 200 replays)."""
+    import torch
+
+    from vfr import GpuRetrievalIndex, synth
+    from vfr.protection import RetrievalProtection
+
+    w = synth.CONFIGS["c4"]
+    arrays, block = synth.make_torch("c4", device, q=w.q)
+    idx = GpuRetrievalIndex.from_arrays(arrays["centroids"], arrays["offsets"], arrays["vectors"], arrays["ids"], 1,
+                                        max_frames=w.q)
+    del arrays
+    rate = torch.tensor([w.ratio], device=device)
+    feats = block.clone()
+    prot = RetrievalProtection(w.q, w.d, device=device)
+    frames = 2 * w.q + 1
+    interp = torch.randn((frames, w.d), device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(5005)
+    pitch = torch.where(torch.rand(frames, generator=g, device=device) < 0.5, 0.0, 150.0)
+    s = torch.cuda.Stream()
+
+    def p50(fn):
+        torch.cuda.synchronize()
+        with torch.cuda.stream(s):
+            fn()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                fn()
+            for _ in range(20):
+                graph.replay()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(200)]
+            for a, b in ev:
+                a.record(s)
+                graph.replay()
+                b.record(s)
+        s.synchronize()
+        lat = sorted(a.elapsed_time(b) for a, b in ev)
+        del graph
+        return lat[len(lat) // 2] * 1000.0
+
+    def copy_then_blend():
+        prot.save_raw(feats, w.q, stream=s)
+        idx.blend(feats, w.q, rate, stream=s)
+
+    t_copy = p50(copy_then_blend)
+    t_fused = p50(lambda: idx.blend_save_raw(feats, prot.raw, w.q, rate, stream=s))
+    t_protect = p50(lambda: prot.apply(interp, pitch, rate, frames, w.q, stream=s))
+    idx.close()
+    unvoiced = int((pitch <= 0).sum().item())
+    bytes_protect = unvoiced * w.d * 4 * 3 + frames * 4
+    return {"workload": f"c4 block: {w.q} HuBERT frames, {frames} interpolated frames x {w.d}, {unvoiced} unvoiced",
+            "copy_then_blend_us_p50": t_copy, "blend_save_raw_us_p50": t_fused,
+            "protect_us_p50": t_protect, "protect_bytes": bytes_protect,
+            "protect_gbs_at_p50": bytes_protect / (t_protect * 1e-6) / 1e9}
+
+
 def ivf(device):
     """c3: IVF-Flat 200k x 768, nlist 256 (20 seeded k-means iterations), 30k
     frames, nprobe 1 and 8; frames/s of the blend (CUDA events)."""
@@ -444,6 +505,7 @@ def main():
     extra = {}
     if rank == 0 and world == 1 and not a.no_streaming:
         extra["streaming"] = streaming(device)
+        extra["protection"] = protection(device)
         extra["ivf"] = ivf(device)
     cpu = None
     if rank == 0 and world == 1 and full_host is not None:

@@ -84,6 +84,20 @@ VFR_API int vocal_faiss_gpu_blend(VfrIndex *index, float *features, size_t frame
 /* Frees an error string (bridge.h:23, vocal_trt_free_error). */
 VFR_API void vfr_free_error(char *message);
 
+/* Replaces vocal_retrieval_protect (crates/vocal-tensorrt/native/
+ * retrieval_protection.cu:18-33; Rust binding crates/vocal-tensorrt/src/
+ * ffi.rs:405-416): after the frontend's 2x interpolation, every frame f with
+ * pitchf[f] <= 0 (or NaN) becomes features * p + raw[min(f / 2,
+ * hubert_frames - 1)] * (1 - p), p = *protect; nothing changes when
+ * *ratio <= 0 or *protect >= 0.5.  features: device f32 [frames][width];
+ * raw: device f32 [hubert_frames][width] (the features saved before the
+ * blend); pitchf: device f32 [frames]; ratio, protect: device scalars.  Same
+ * checks and messages as the reference; stream->stream may be the default
+ * stream. */
+VFR_API int vocal_retrieval_protect(float *features, const float *raw, const float *pitchf, const float *ratio,
+                                    const float *protect, int32_t frames, int32_t hubert_frames, int32_t width,
+                                    VfrStream *stream, char **error);
+
 /* ------------------------------------------------------------------------ */
 /* Index loading (restates crates/vocal-model/src/retrieval.rs:45-268)      */
 /* ------------------------------------------------------------------------ */
@@ -153,6 +167,16 @@ VFR_API int vfr_retrieval_search(VfrIndex *index, const float *queries, size_t f
 /* Out-of-place blend: reads queries, writes out (may alias queries). */
 VFR_API int vfr_retrieval_blend_from(VfrIndex *index, const float *queries, float *out, size_t frames, int32_t width,
                              const float *index_rate, VfrStream *stream, char **error);
+
+/* vocal_faiss_gpu_blend with RetrievalProtection::save_raw fused in
+ * (crates/vocal-tensorrt/src/pipeline.rs:1842-1853,
+ * crates/vocal-tensorrt/src/retrieval/protection.rs:47-55): raw (device f32
+ * [frames][width], not overlapping features) receives the features as they
+ * are before the blend, then features are blended in place.  On the flat
+ * tensor-core path the merge kernel writes raw from its own load of each
+ * frame, so the separate device copy of the reference disappears. */
+VFR_API int vfr_retrieval_blend_save_raw(VfrIndex *index, float *features, float *raw, size_t frames,
+                                         int32_t width, const float *index_rate, VfrStream *stream, char **error);
 
 /* JSON diagnostics (engine, candidate width, empty-frame count, fallback
  * count, layout).  Returns the length needed (excluding NUL); writes at most

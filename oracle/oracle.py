@@ -64,6 +64,9 @@ def lib():
                                        ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_void_p]
         L.orc_search_batch.restype = ctypes.c_int
+        L.orc_protect.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_float,
+                                  ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]
+        L.orc_protect.restype = None
         L.orc_view.argtypes = [P(_Index), ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         _lib = L
@@ -186,3 +189,17 @@ def vfrm_find_faiss(image: bytes):
     if rc < 0:
         raise ValueError("malformed VFRM container")
     return (off.value, n.value) if rc == 1 else None
+
+
+def protect(features: np.ndarray, raw: np.ndarray, pitchf: np.ndarray, ratio: float, amount: float,
+            hubert_frames: int) -> np.ndarray:
+    """Restated protect_features (crates/vocal-tensorrt/native/retrieval_protection.cu:4-16)
+    on a copy of `features` [frames][width]; `raw` holds hubert_frames rows."""
+    out = np.ascontiguousarray(features, dtype=np.float32).copy()
+    raw = np.ascontiguousarray(raw, dtype=np.float32)
+    pitchf = np.ascontiguousarray(pitchf, dtype=np.float32)
+    frames, width = out.shape
+    assert pitchf.shape[0] >= frames and raw.shape[0] >= hubert_frames and raw.shape[1] == width
+    lib().orc_protect(_ptr(out), _ptr(raw), _ptr(pitchf), ctypes.c_float(ratio), ctypes.c_float(amount),
+                      frames, hubert_frames, width)
+    return out

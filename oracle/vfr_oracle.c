@@ -15,6 +15,8 @@
  *   - distances:      crates/vocal-cpu/src/retrieval.rs:5-26 (scalar_l2, avx2_l2)
  *   - search + blend: crates/vocal-cpu/src/retrieval.rs:27-83 (blend)
  *   - call site:      crates/vocal-cpu/src/pipeline.rs:292-301 (serial per-frame loop)
+ *   - protection:     crates/vocal-tensorrt/native/retrieval_protection.cu:4-16
+ *                     (protect_features; GPU-only in the reference)
  *
  * Arithmetic order is kept exactly: AVX2 8-lane direct-difference squared L2
  * with separate multiply and add, the eight lanes folded left to right, then
@@ -623,3 +625,23 @@ void orc_view(orc_index *ix, int64_t d, int64_t nlist, int64_t nprobe, int64_t n
 }
 
 size_t orc_index_size(void) { return sizeof(orc_index); }
+
+/* Unvoiced-frame protection, restating protect_features
+ * (crates/vocal-tensorrt/native/retrieval_protection.cu:4-16) element by
+ * element: nothing when ratio <= 0 or protect >= 0.5 (NaN passes both); frames
+ * with pitchf > 0 keep their features; the others become
+ * f * p + raw[min(frame / 2, hubert_frames - 1)] * (1 - p), each operation
+ * rounded on its own (this file builds with -ffp-contract=off). */
+void orc_protect(float *features, const float *raw, const float *pitchf, float ratio, float protect,
+                 int64_t frames, int64_t hubert_frames, int64_t width) {
+    if (ratio <= 0.0f || protect >= 0.5f) return;
+    for (int64_t f = 0; f < frames; ++f) {
+        if (pitchf[f] > 0.0f) continue;
+        const int64_t row = f / 2 < hubert_frames - 1 ? f / 2 : hubert_frames - 1;
+        for (int64_t c = 0; c < width; ++c) {
+            const float a = features[f * width + c] * protect;
+            const float b = raw[row * width + c] * (1.0f - protect);
+            features[f * width + c] = a + b;
+        }
+    }
+}

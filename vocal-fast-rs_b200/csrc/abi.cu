@@ -155,15 +155,23 @@ ExactArgs exact_args(VfrIndex *ix, const float *queries, float *out, const float
 }
 
 void blend_impl(VfrIndex *ix, const float *queries, float *out, size_t frames, int32_t width, const float *rate,
-                VfrStream *stream) {
+                VfrStream *stream, float *raw = nullptr) {
     require(ix && queries && out && frames > 0 && rate, "invalid FAISS GPU blend arguments");
     require(frames <= static_cast<size_t>(INT32_MAX), "FAISS frame count exceeds CUDA grid limit");
     require(width == ix->d, "FAISS feature width mismatch");
     cudaStream_t s = stream_of(stream);
     DeviceGuard guard(ix->device);
+    if (raw) {
+        const size_t bytes = frames * static_cast<size_t>(width) * sizeof(float);
+        const auto *r = reinterpret_cast<const uint8_t *>(raw), *q = reinterpret_cast<const uint8_t *>(queries);
+        require(r + bytes <= q || q + bytes <= r, "raw feature buffer overlaps the features");
+    }
     if (ix->have_tc && use_tc(ix, frames)) {
-        run_tc(ix, queries, out, rate, kModeBlend, 8, nullptr, nullptr, frames, s);
+        run_tc(ix, queries, out, rate, kModeBlend, 8, nullptr, nullptr, frames, s, raw);
     } else {
+        if (raw)
+            cuda_check(cudaMemcpyAsync(raw, queries, frames * static_cast<size_t>(width) * sizeof(float),
+                                       cudaMemcpyDeviceToDevice, s));
         ix->prof.begin(kProfExact, s);
         launch_exact(exact_args(ix, queries, out, rate, kModeBlend), static_cast<long long>(frames), s);
         ix->prof.end(s);
@@ -176,6 +184,7 @@ void blend_impl(VfrIndex *ix, const float *queries, float *out, size_t frames, i
 
 using vfr::guarded;
 using vfr::require;
+using vfr::cuda_check;
 
 extern "C" int vocal_faiss_gpu_create(int32_t dimensions, int32_t nlist, int32_t nprobe, size_t vector_count,
                                       const float *centroids, size_t centroid_count, const int32_t *offsets,
@@ -212,6 +221,32 @@ extern "C" int vocal_faiss_gpu_blend(VfrIndex *index, float *features, size_t fr
 extern "C" int vfr_retrieval_blend_from(VfrIndex *index, const float *queries, float *out, size_t frames,
                                         int32_t width, const float *index_rate, VfrStream *stream, char **error) {
     return guarded(error, [&] { vfr::blend_impl(index, queries, out, frames, width, index_rate, stream); });
+}
+
+extern "C" int vfr_retrieval_blend_save_raw(VfrIndex *index, float *features, float *raw, size_t frames,
+                                            int32_t width, const float *index_rate, VfrStream *stream,
+                                            char **error) {
+    return guarded(error, [&] {
+        require(raw != nullptr, "null raw feature buffer");
+        vfr::blend_impl(index, features, features, frames, width, index_rate, stream, raw);
+    });
+}
+
+extern "C" int vocal_retrieval_protect(float *features, const float *raw, const float *pitchf, const float *ratio,
+                                       const float *protect, int32_t frames, int32_t hubert_frames, int32_t width,
+                                       VfrStream *stream, char **error) {
+    return guarded(error, [&] {
+        require(features && raw && pitchf && ratio && protect && stream, "null retrieval protection binding");
+        require(frames > 0 && hubert_frames > 0 && width > 0 && frames <= INT32_MAX / width,
+                "invalid retrieval protection dimensions");
+        int device = 0;
+        cuda_check(cudaGetDevice(&device));
+        int sms = 0;
+        cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+        vfr::launch_protect(features, raw, pitchf, ratio, protect, frames, hubert_frames, width, sms,
+                            static_cast<cudaStream_t>(stream->stream));
+        cuda_check(cudaGetLastError());
+    });
 }
 
 extern "C" int vfr_retrieval_search(VfrIndex *index, const float *queries, size_t frames, int32_t width, int32_t k,

@@ -46,6 +46,10 @@ struct ExactArgs {
 // overlap until its own dependency wait (programmatic dependent launch).
 void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream, bool after_kernel = false);
 
+// Unvoiced-frame protection (protect_kernels.cu).
+void launch_protect(float *features, const float *raw, const float *pitchf, const float *ratio, const float *protect,
+                    int frames, int hubert_frames, int width, int sm_count, cudaStream_t stream);
+
 // Sharded helpers (shard_kernels.cu).
 void launch_merge_topk(const float *dist, const int64_t *labels, int shards, long long frames, float *out_dist,
                        int64_t *out_labels, cudaStream_t stream);

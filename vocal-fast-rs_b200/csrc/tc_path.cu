@@ -641,6 +641,7 @@ struct MergeArgs {
     int32_t *fallback_count;
     DeviceCounters *counters;
     int stage_rows;  // re-rank rows staged in shared memory per chunk (0: read them from global memory)
+    float *raw_out;  // optional: the frames before the blend (RetrievalProtection::save_raw)
 };
 
 constexpr int kMergeThreads = 256;     // per frame, when many frames share the GPU
@@ -1055,7 +1056,12 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreads ? 3 : 1) merge_kernel(
         for (int i = tid; i < kWideBins; i += kT) wide[i] = 0u;
     // the caller's inputs first, while the candidate kernel may still run
     const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
-    for (int i = tid; i < d; i += kT) q[i] = src[i];
+    float *raw_row = a.raw_out ? a.raw_out + frame * d : nullptr;
+    for (int i = tid; i < d; i += kT) {
+        const float v = src[i];
+        q[i] = v;
+        if (raw_row) raw_row[i] = v;
+    }
     for (int i = real_slots + tid; i < a.sort_size; i += kT) keys[i] = kEmptyKey;
     grid_dependency_wait();
     // the certifying thread's query stats, early (prepared two kernels back)
@@ -2229,7 +2235,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
 }  // namespace
 
 void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, int mode, int k, float *dist_out,
-            int64_t *label_out, size_t frames, cudaStream_t stream) {
+            int64_t *label_out, size_t frames, cudaStream_t stream, float *raw) {
     if (frames > ix->ws.frames) {
         cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
         cuda_check(cudaStreamIsCapturing(stream, &st));
@@ -2239,6 +2245,9 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
         reserve_tc(ix, frames);
     }
     if (ix->nlist > 1) {
+        if (raw)
+            cuda_check(cudaMemcpyAsync(raw, queries, frames * static_cast<size_t>(ix->d) * sizeof(float),
+                                       cudaMemcpyDeviceToDevice, stream));
         run_ivf(ix, queries, out, rate, mode, k, dist_out, label_out, frames, stream);
         return;
     }
@@ -2306,6 +2315,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ma.norm_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -23);
     ma.exact_rel = static_cast<float>(ix->d / 8 + 9) * std::ldexp(1.0f, -24);
     ma.fallback_list = flist;
+    ma.raw_out = raw;
     ma.fallback_count = fcount;
     ma.counters = ix->counters;
     ix->prof.begin(kProfMerge, stream);

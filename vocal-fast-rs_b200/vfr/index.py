@@ -171,6 +171,22 @@ class GpuRetrievalIndex:
         s = stream_struct(stream)
         call(L.vocal_faiss_gpu_blend, self._h, _ptr(features), frames, self.d, _ptr(index_rate), ctypes.byref(s))
 
+    def blend_save_raw(self, features, raw, frames: int, index_rate, stream=None) -> None:
+        """`blend` with RetrievalProtection::save_raw fused in
+        (crates/vocal-tensorrt/src/pipeline.rs:1842-1853): `raw` (a CUDA f32
+        tensor of at least frames*d values) receives the frames as they are
+        before the blend."""
+        if frames == 0:
+            return
+        validate_blend_buffers(frames, self.d, features.numel() * features.element_size(),
+                               index_rate.numel() * index_rate.element_size())
+        if raw.numel() < frames * self.d:
+            raise ValueError("raw feature buffer is smaller than frames x width")
+        L = load_library()
+        s = stream_struct(stream)
+        call(L.vfr_retrieval_blend_save_raw, self._h, _ptr(features), _ptr(raw), frames, self.d, _ptr(index_rate),
+             ctypes.byref(s))
+
     def blend_from(self, queries, out, index_rate, stream=None) -> None:
         frames = queries.shape[0]
         if frames == 0:

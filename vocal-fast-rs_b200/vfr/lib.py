@@ -65,6 +65,8 @@ def load_library(path: str | None = None):
         "vocal_faiss_gpu_create": ([i32, i32, i32, sz, vp, sz, vp, sz, vp, sz, vp, sz, P(vp), err], ctypes.c_int),
         "vocal_faiss_gpu_destroy": ([vp], None),
         "vocal_faiss_gpu_blend": ([vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
+        "vocal_retrieval_protect": ([vp, vp, vp, vp, vp, i32, i32, i32, P(Stream), err], ctypes.c_int),
+        "vfr_retrieval_blend_save_raw": ([vp, vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
         "vfr_free_error": ([vp], None),
         "vfr_index_parse_faiss": ([ctypes.c_char_p, sz, P(vp), err], ctypes.c_int),
         "vfr_index_from_vfrm": ([ctypes.c_char_p, sz, i32, P(vp), err], ctypes.c_int),
