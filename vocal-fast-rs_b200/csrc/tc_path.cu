@@ -1368,12 +1368,14 @@ void launch_merge(VfrIndex *ix, MergeArgs &ma, size_t frames, cudaStream_t strea
     }
     const size_t smem = merge_smem(ma.sort_size, ma.thr_stride, ix->d, ma.stage_rows).total;
     require(smem <= static_cast<size_t>(ix->merge_smem_max), "candidate lists exceed the merge's shared memory");
+    // A plain launch: with programmatic launch the merge CTAs, resident early
+    // and parked in their dependency wait through the candidate stream, ran
+    // their phases slower afterwards (a c4 block took 64 us instead of 58).
     if (ma.stage_rows > 0)
-        cuda_check(launch_pdl(merge_kernel<kMergeThreadsMax>, dim3(static_cast<unsigned>(frames)),
-                              dim3(kMergeThreadsMax), smem, stream, ma));
+        merge_kernel<kMergeThreadsMax><<<static_cast<unsigned>(frames), kMergeThreadsMax, smem, stream>>>(ma);
     else
-        cuda_check(launch_pdl(merge_kernel<kMergeThreads>, dim3(static_cast<unsigned>(frames)), dim3(kMergeThreads),
-                              smem, stream, ma));
+        merge_kernel<kMergeThreads><<<static_cast<unsigned>(frames), kMergeThreads, smem, stream>>>(ma);
+    cuda_check(cudaGetLastError());
 }
 
 // Launches the flat candidate kernel behind prep_queries_kernel (it starts
