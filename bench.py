@@ -257,12 +257,13 @@ def protection(device):
     """The step after the blend on the realtime path: the raw copy fused into
     the blend (vfr_retrieval_blend_save_raw) against the reference's separate
     device copy + blend, and vocal_retrieval_protect on the interpolated block
-    (2 x 32 + 1 frames x 768, half of them unvoiced), each replayed from a
-    CUDA graph (p50 over 200 replays)."""
+    (2 x 32 + 1 frames x 768, half of them unvoiced), and the frontend with
+    the protection fused (vfr_rvc_frontend) against frontend + protect, each
+    replayed from a CUDA graph (p50 over 200 replays)."""
     import torch
 
     from vfr import GpuRetrievalIndex, synth
-    from vfr.protection import RetrievalProtection
+    from vfr.protection import RetrievalProtection, rvc_frontend
 
     w = synth.CONFIGS["c4"]
     arrays, block = synth.make_torch("c4", device, q=w.q)
@@ -305,13 +306,25 @@ def protection(device):
     t_copy = p50(copy_then_blend)
     t_fused = p50(lambda: idx.blend_save_raw(feats, prot.raw, w.q, rate, stream=s))
     t_protect = p50(lambda: prot.apply(interp, pitch, rate, frames, w.q, stream=s))
+    # the frontend (append, 2x, crop, coarse pitch) on the same block, f0 of
+    # 2 (q + 1) frames: separate frontend + protect as in the reference's
+    # pipeline, then the fused kernel
+    f0 = torch.where(torch.rand(2 * (w.q + 1), generator=g, device=device) < 0.5, 0.0, 150.0)
+
+    def frontend_then_protect():
+        out, pf, _ = rvc_frontend(feats, f0, w.q, stream=s)
+        prot.apply(out, pf, rate, out.shape[0], w.q, stream=s)
+
+    t_front_sep = p50(frontend_then_protect)
+    t_front = p50(lambda: rvc_frontend(feats, f0, w.q, prot, rate, stream=s))
     idx.close()
     unvoiced = int((pitch <= 0).sum().item())
     bytes_protect = unvoiced * w.d * 4 * 3 + frames * 4
     return {"workload": f"c4 block: {w.q} HuBERT frames, {frames} interpolated frames x {w.d}, {unvoiced} unvoiced",
             "copy_then_blend_us_p50": t_copy, "blend_save_raw_us_p50": t_fused,
             "protect_us_p50": t_protect, "protect_bytes": bytes_protect,
-            "protect_gbs_at_p50": bytes_protect / (t_protect * 1e-6) / 1e9}
+            "protect_gbs_at_p50": bytes_protect / (t_protect * 1e-6) / 1e9,
+            "frontend_then_protect_us_p50": t_front_sep, "frontend_fused_us_p50": t_front}
 
 
 def ivf(device):

@@ -168,6 +168,25 @@ VFR_API int vfr_retrieval_search(VfrIndex *index, const float *queries, size_t f
 VFR_API int vfr_retrieval_blend_from(VfrIndex *index, const float *queries, float *out, size_t frames, int32_t width,
                              const float *index_rate, VfrStream *stream, char **error);
 
+/* The RVC frontend after the blend with the protection fused in, replacing
+ * the TensorRT frontend graph (crates/vocal-tensorrt/native/frontend.cpp:
+ * 36-75) and the vocal_retrieval_protect pass after it
+ * (crates/vocal-tensorrt/src/pipeline.rs:1826-1828): the last HuBERT frame
+ * is appended, the frames are interpolated 2x (nearest: output frame t reads
+ * frame t / 2) and cropped to target = min(2 (hubert_frames + 1), f0_frames)
+ * frames; pitchf = f0[0 .. target) and pitch = the coarse mel bin
+ * round(clamp((1127 ln(1 + f0/700) - mel_min) * 254 / (mel_max - mel_min)
+ * + 1, 1, 255)).  When raw is not null the unvoiced frames (f0 <= 0) are
+ * protected as vocal_retrieval_protect does, under the same ratio and
+ * protect device scalars.  hubert, raw: device f32 [hubert_frames][width];
+ * f0: device f32 [f0_frames]; feats: device f32 [target][width]; pitchf:
+ * device f32 [target]; pitch: device i32 [target]; *out_frames (host, may
+ * be null) receives target. */
+VFR_API int vfr_rvc_frontend(const float *hubert, const float *raw, const float *f0, const float *ratio,
+                             const float *protect, int32_t hubert_frames, int32_t f0_frames, int32_t width,
+                             float *feats, float *pitchf, int32_t *pitch, int32_t *out_frames, VfrStream *stream,
+                             char **error);
+
 /* vocal_faiss_gpu_blend with RetrievalProtection::save_raw fused in
  * (crates/vocal-tensorrt/src/pipeline.rs:1842-1853,
  * crates/vocal-tensorrt/src/retrieval/protection.rs:47-55): raw (device f32

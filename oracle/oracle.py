@@ -67,6 +67,10 @@ def lib():
         L.orc_protect.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_float,
                                   ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]
         L.orc_protect.restype = None
+        L.orc_rvc_frontend.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float,
+                                       ctypes.c_float, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        L.orc_rvc_frontend.restype = ctypes.c_int64
         L.orc_view.argtypes = [P(_Index), ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         _lib = L
@@ -203,3 +207,25 @@ def protect(features: np.ndarray, raw: np.ndarray, pitchf: np.ndarray, ratio: fl
     lib().orc_protect(_ptr(out), _ptr(raw), _ptr(pitchf), ctypes.c_float(ratio), ctypes.c_float(amount),
                       frames, hubert_frames, width)
     return out
+
+
+def rvc_frontend(hubert: np.ndarray, raw, f0: np.ndarray, ratio: float, amount: float):
+    """Restated frontend.cpp:36-75 plus the protection (raw=None skips it):
+    (feats [target][w], pitchf [target], pitch [target] i32, coarse [target]
+    unrounded and unclamped)."""
+    hubert = np.ascontiguousarray(hubert, dtype=np.float32)
+    f0 = np.ascontiguousarray(f0, dtype=np.float32)
+    h, w = hubert.shape
+    target = min(2 * (h + 1), f0.shape[0])
+    feats = np.empty((target, w), np.float32)
+    pitchf = np.empty(target, np.float32)
+    pitch = np.empty(target, np.int32)
+    coarse = np.empty(target, np.float32)
+    rawp = None
+    if raw is not None:
+        raw = np.ascontiguousarray(raw, dtype=np.float32)
+        rawp = _ptr(raw)
+    got = lib().orc_rvc_frontend(_ptr(hubert), rawp, _ptr(f0), ctypes.c_float(ratio), ctypes.c_float(amount), h,
+                                 f0.shape[0], w, _ptr(feats), _ptr(pitchf), _ptr(pitch), _ptr(coarse))
+    assert got == target
+    return feats, pitchf, pitch, coarse

@@ -17,6 +17,9 @@
  *   - call site:      crates/vocal-cpu/src/pipeline.rs:292-301 (serial per-frame loop)
  *   - protection:     crates/vocal-tensorrt/native/retrieval_protection.cu:4-16
  *                     (protect_features; GPU-only in the reference)
+ *   - RVC frontend:   crates/vocal-tensorrt/native/frontend.cpp:36-75 (append the
+ *                     last HuBERT frame, nearest 2x, crop, coarse pitch; a
+ *                     TensorRT graph in the reference)
  *
  * Arithmetic order is kept exactly: AVX2 8-lane direct-difference squared L2
  * with separate multiply and add, the eight lanes folded left to right, then
@@ -644,4 +647,44 @@ void orc_protect(float *features, const float *raw, const float *pitchf, float r
             features[f * width + c] = a + b;
         }
     }
+}
+
+/* The RVC frontend after the blend with the protection fused, restating
+ * frontend.cpp:36-75 (a TensorRT graph in the reference) then protect_features:
+ * target = min(2 (hubert_frames + 1), f0_frames); output frame t reads HuBERT
+ * row min(t / 2, hubert_frames - 1) (the appended last frame and the nearest,
+ * asymmetric 2x resize); pitchf = f0[t]; coarse[t] = the unrounded mel bin
+ * (before clamping) and pitch[t] its clamped, rounded (half to even) value.
+ * raw == NULL skips the protection.  Returns target. */
+int64_t orc_rvc_frontend(const float *hubert, const float *raw, const float *f0, float ratio, float protect,
+                         int64_t hubert_frames, int64_t f0_frames, int64_t width, float *feats, float *pitchf,
+                         int32_t *pitch, float *coarse) {
+    const int64_t interp = 2 * (hubert_frames + 1);
+    const int64_t target = interp < f0_frames ? interp : f0_frames;
+    const int protecting = raw != NULL && !(ratio <= 0.0f || protect >= 0.5f);
+    const float mel_min = 1127.0f * log1pf(50.0f / 700.0f);
+    const float mel_max = 1127.0f * log1pf(1100.0f / 700.0f);
+    const float mel_scale = 254.0f / (mel_max - mel_min);
+    for (int64_t t = 0; t < target; ++t) {
+        const int64_t row = t / 2 < hubert_frames - 1 ? t / 2 : hubert_frames - 1;
+        const float f = f0[t];
+        for (int64_t c = 0; c < width; ++c) {
+            float v = hubert[row * width + c];
+            if (protecting && !(f > 0.0f)) {
+                const float a = v * protect;
+                const float b = raw[row * width + c] * (1.0f - protect);
+                v = a + b;
+            }
+            feats[t * width + c] = v;
+        }
+        pitchf[t] = f;
+        const float scaled = f * (1.0f / 700.0f);
+        const float mel = logf(scaled + 1.0f) * 1127.0f;
+        float x = (mel - mel_min) * mel_scale + 1.0f;
+        if (coarse) coarse[t] = x;
+        x = x > 1.0f ? x : 1.0f;
+        x = x < 255.0f ? x : 255.0f;
+        pitch[t] = (int32_t)rintf(x);
+    }
+    return target;
 }

@@ -232,6 +232,24 @@ extern "C" int vfr_retrieval_blend_save_raw(VfrIndex *index, float *features, fl
     });
 }
 
+extern "C" int vfr_rvc_frontend(const float *hubert, const float *raw, const float *f0, const float *ratio,
+                                const float *protect, int32_t hubert_frames, int32_t f0_frames, int32_t width,
+                                float *feats, float *pitchf, int32_t *pitch, int32_t *out_frames, VfrStream *stream,
+                                char **error) {
+    return guarded(error, [&] {
+        require(hubert && f0 && feats && pitchf && pitch && stream, "null RVC frontend binding");
+        require(!raw || (ratio && protect), "null retrieval protection binding");
+        require(hubert_frames > 0 && f0_frames > 0 && width > 0 && hubert_frames < INT32_MAX / 2 - 1 &&
+                    f0_frames <= INT32_MAX / width,
+                "invalid RVC frontend dimensions");
+        const int target = vfr::frontend_frames(hubert_frames, f0_frames);
+        if (out_frames) *out_frames = target;
+        vfr::launch_frontend(hubert, raw, f0, ratio, protect, hubert_frames, f0_frames, width, feats, pitchf, pitch,
+                             static_cast<cudaStream_t>(stream->stream));
+        cuda_check(cudaGetLastError());
+    });
+}
+
 extern "C" int vocal_retrieval_protect(float *features, const float *raw, const float *pitchf, const float *ratio,
                                        const float *protect, int32_t frames, int32_t hubert_frames, int32_t width,
                                        VfrStream *stream, char **error) {
@@ -239,11 +257,7 @@ extern "C" int vocal_retrieval_protect(float *features, const float *raw, const 
         require(features && raw && pitchf && ratio && protect && stream, "null retrieval protection binding");
         require(frames > 0 && hubert_frames > 0 && width > 0 && frames <= INT32_MAX / width,
                 "invalid retrieval protection dimensions");
-        int device = 0;
-        cuda_check(cudaGetDevice(&device));
-        int sms = 0;
-        cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
-        vfr::launch_protect(features, raw, pitchf, ratio, protect, frames, hubert_frames, width, sms,
+        vfr::launch_protect(features, raw, pitchf, ratio, protect, frames, hubert_frames, width,
                             static_cast<cudaStream_t>(stream->stream));
         cuda_check(cudaGetLastError());
     });

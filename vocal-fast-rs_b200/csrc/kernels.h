@@ -48,7 +48,13 @@ void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream, 
 
 // Unvoiced-frame protection (protect_kernels.cu).
 void launch_protect(float *features, const float *raw, const float *pitchf, const float *ratio, const float *protect,
-                    int frames, int hubert_frames, int width, int sm_count, cudaStream_t stream);
+                    int frames, int hubert_frames, int width, cudaStream_t stream);
+
+// RVC frontend after the blend, with the protection fused (protect_kernels.cu).
+int frontend_frames(int hubert_frames, int f0_frames);
+void launch_frontend(const float *hubert, const float *raw, const float *f0, const float *ratio,
+                     const float *protect, int hubert_frames, int f0_frames, int width, float *feats, float *pitchf,
+                     int32_t *pitch, cudaStream_t stream);
 
 // Sharded helpers (shard_kernels.cu).
 void launch_merge_topk(const float *dist, const int64_t *labels, int shards, long long frames, float *out_dist,

@@ -11,7 +11,8 @@
 // fused multiply-adds), which the oracle restates.
 //
 // HBM-bound elementwise work: frames x width x 8 bytes of features plus the
-// raw rows; one float4 per thread when the width allows, grid-strided.
+// raw rows; one CTA per frame, float4 lanes when the width allows.
+#include <cmath>
 #include <stdexcept>
 #include <string>
 
@@ -24,57 +25,140 @@ __device__ __forceinline__ float protect_value(float f, float r, float p) {
     return __fadd_rn(__fmul_rn(f, p), __fmul_rn(r, __fsub_rn(1.0f, p)));
 }
 
-// width % 4 == 0: thread i handles features [4i, 4i + 4) of one frame.
-__global__ void protect_vec4_kernel(float4 *__restrict__ features, const float4 *__restrict__ raw,
+// One CTA per interpolated frame: a voiced frame's CTA returns at once, an
+// unvoiced one mixes its width features toward the raw row (float4 lanes when
+// kVec: width % 4 == 0 and both rows 16-byte aligned).
+template <bool kVec>
+__global__ void protect_rows_kernel(float *__restrict__ features, const float *__restrict__ raw,
                                     const float *__restrict__ pitchf, const float *__restrict__ ratio,
-                                    const float *__restrict__ protect, long long quads, int quads_per_frame,
-                                    int hubert_frames) {
+                                    const float *__restrict__ protect, int width, int hubert_frames) {
     const float r = *ratio, p = *protect;
-    if (r <= 0.0f || p >= 0.5f) return;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < quads;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const long long frame = i / quads_per_frame;
-        if (pitchf[frame] > 0.0f) continue;
-        const long long row = frame / 2 < hubert_frames - 1 ? frame / 2 : hubert_frames - 1;
-        const float4 f = features[i];
-        const float4 x = __ldg(raw + row * quads_per_frame + (i - frame * quads_per_frame));
-        features[i] = make_float4(protect_value(f.x, x.x, p), protect_value(f.y, x.y, p),
-                                  protect_value(f.z, x.z, p), protect_value(f.w, x.w, p));
+    const int frame = blockIdx.x;
+    if (r <= 0.0f || p >= 0.5f || pitchf[frame] > 0.0f) return;
+    const int row = frame / 2 < hubert_frames - 1 ? frame / 2 : hubert_frames - 1;
+    float *out = features + static_cast<long long>(frame) * width;
+    const float *src = raw + static_cast<long long>(row) * width;
+    if (kVec) {
+        float4 *o4 = reinterpret_cast<float4 *>(out);
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        for (int c = threadIdx.x; c < width / 4; c += blockDim.x) {
+            const float4 f = o4[c], x = __ldg(s4 + c);
+            o4[c] = make_float4(protect_value(f.x, x.x, p), protect_value(f.y, x.y, p), protect_value(f.z, x.z, p),
+                                protect_value(f.w, x.w, p));
+        }
+    } else {
+        for (int c = threadIdx.x; c < width; c += blockDim.x) out[c] = protect_value(out[c], __ldg(src + c), p);
     }
 }
 
-__global__ void protect_scalar_kernel(float *__restrict__ features, const float *__restrict__ raw,
-                                      const float *__restrict__ pitchf, const float *__restrict__ ratio,
-                                      const float *__restrict__ protect, long long elements, int width,
-                                      int hubert_frames) {
-    const float r = *ratio, p = *protect;
-    if (r <= 0.0f || p >= 0.5f) return;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < elements;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const long long frame = i / width;
-        if (pitchf[frame] > 0.0f) continue;
-        const long long row = frame / 2 < hubert_frames - 1 ? frame / 2 : hubert_frames - 1;
-        features[i] = protect_value(features[i], __ldg(raw + row * width + (i - frame * width)), p);
+// threads per frame CTA: the row's lanes rounded up to a warp, at most 256
+int row_threads(int lanes) {
+    const int t = (lanes + 31) / 32 * 32;
+    return t < 256 ? t : 256;
+}
+
+bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+}  // namespace
+
+void launch_protect(float *features, const float *raw, const float *pitchf, const float *ratio, const float *protect,
+                    int frames, int hubert_frames, int width, cudaStream_t stream) {
+    const bool vec = width % 4 == 0 && aligned16(features) && aligned16(raw);
+    if (vec)
+        protect_rows_kernel<true><<<frames, row_threads(width / 4), 0, stream>>>(features, raw, pitchf, ratio,
+                                                                                  protect, width, hubert_frames);
+    else
+        protect_rows_kernel<false><<<frames, row_threads(width), 0, stream>>>(features, raw, pitchf, ratio, protect,
+                                                                               width, hubert_frames);
+}
+
+}  // namespace vfr
+
+// ---------------------------------------------------------------- frontend
+// The RVC frontend after the blend (crates/vocal-tensorrt/native/
+// frontend.cpp:36-75, a TensorRT graph in the reference): the last HuBERT
+// frame is appended, the frames are interpolated 2x (nearest, asymmetric:
+// output frame t reads input frame t / 2) and cropped to
+// target = min(2 (hubert_frames + 1), f0_frames); pitchf is f0 cropped the
+// same way and pitch its coarse mel bin, round(clamp((1127 ln(1 + f0 / 700)
+// - mel_min) * 254 / (mel_max - mel_min) + 1, 1, 255)).  Output frame t thus
+// reads HuBERT row min(t / 2, hubert_frames - 1), the row the protection
+// (above) mixes back toward, so both run in one pass: when raw is given,
+// unvoiced frames get f * p + raw[row] * (1 - p) under the same ratio and
+// amount conditions.
+namespace vfr {
+namespace {
+
+// One CTA per output frame t: copies HuBERT row min(t / 2, hubert_frames - 1)
+// (mixed toward the raw row when protecting and the frame is unvoiced) and,
+// from thread 0, pitchf[t] and pitch[t].
+template <bool kVec>
+__global__ void frontend_kernel(const float *__restrict__ hubert, const float *__restrict__ raw,
+                                const float *__restrict__ f0, const float *__restrict__ ratio,
+                                const float *__restrict__ protect, int hubert_frames, int width, float mel_min,
+                                float mel_scale, float *__restrict__ feats, float *__restrict__ pitchf,
+                                int32_t *__restrict__ pitch) {
+    const int t = blockIdx.x;
+    const int row = t / 2 < hubert_frames - 1 ? t / 2 : hubert_frames - 1;
+    const float f = f0[t];
+    const bool protecting = raw != nullptr && !(*ratio <= 0.0f || *protect >= 0.5f) && !(f > 0.0f);
+    const float p = protecting ? *protect : 0.0f;
+    const float *src = hubert + static_cast<long long>(row) * width;
+    const float *rsrc = protecting ? raw + static_cast<long long>(row) * width : nullptr;
+    float *out = feats + static_cast<long long>(t) * width;
+    if (kVec) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        const float4 *r4 = reinterpret_cast<const float4 *>(rsrc);
+        float4 *o4 = reinterpret_cast<float4 *>(out);
+        for (int c = threadIdx.x; c < width / 4; c += blockDim.x) {
+            float4 v = __ldg(s4 + c);
+            if (protecting) {
+                const float4 x = __ldg(r4 + c);
+                v = make_float4(protect_value(v.x, x.x, p), protect_value(v.y, x.y, p), protect_value(v.z, x.z, p),
+                                protect_value(v.w, x.w, p));
+            }
+            o4[c] = v;
+        }
+    } else {
+        for (int c = threadIdx.x; c < width; c += blockDim.x) {
+            const float v = __ldg(src + c);
+            out[c] = protecting ? protect_value(v, __ldg(rsrc + c), p) : v;
+        }
+    }
+    if (threadIdx.x == 0) {
+        pitchf[t] = f;
+        // the graph's order: ((f * (1/700)) + 1) -> log -> * 1127, then
+        // (mel - mel_min) * mel_scale + 1 (constants from the host, as the
+        // graph's are); NaN and the clamp's low side both give 1
+        const float mel = __fmul_rn(logf(__fadd_rn(__fmul_rn(f, 1.0f / 700.0f), 1.0f)), 1127.0f);
+        float coarse = __fadd_rn(__fmul_rn(__fsub_rn(mel, mel_min), mel_scale), 1.0f);
+        coarse = fminf(fmaxf(coarse, 1.0f), 255.0f);
+        pitch[t] = static_cast<int32_t>(rintf(coarse));
     }
 }
 
 }  // namespace
 
-void launch_protect(float *features, const float *raw, const float *pitchf, const float *ratio, const float *protect,
-                    int frames, int hubert_frames, int width, int sm_count, cudaStream_t stream) {
-    const long long elements = static_cast<long long>(frames) * width;
-    const bool vec = width % 4 == 0 && reinterpret_cast<uintptr_t>(features) % 16 == 0 &&
-                     reinterpret_cast<uintptr_t>(raw) % 16 == 0;
-    const long long items = vec ? elements / 4 : elements;
-    const long long blocks_needed = (items + 255) / 256;
-    const int grid = static_cast<int>(blocks_needed < sm_count * 8LL ? blocks_needed : sm_count * 8LL);
+int frontend_frames(int hubert_frames, int f0_frames) {
+    const long long interp = 2LL * (hubert_frames + 1);
+    return static_cast<int>(interp < f0_frames ? interp : f0_frames);
+}
+
+void launch_frontend(const float *hubert, const float *raw, const float *f0, const float *ratio,
+                     const float *protect, int hubert_frames, int f0_frames, int width, float *feats, float *pitchf,
+                     int32_t *pitch, cudaStream_t stream) {
+    const int target = frontend_frames(hubert_frames, f0_frames);
+    // frontend.cpp:66-67, computed on the host in f32 like the graph's constants
+    const float mel_min = 1127.0f * std::log1p(50.0f / 700.0f);
+    const float mel_max = 1127.0f * std::log1p(1100.0f / 700.0f);
+    const float mel_scale = 254.0f / (mel_max - mel_min);
+    const bool vec = width % 4 == 0 && aligned16(hubert) && aligned16(feats) && (raw == nullptr || aligned16(raw));
     if (vec)
-        protect_vec4_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<float4 *>(features),
-                                                       reinterpret_cast<const float4 *>(raw), pitchf, ratio,
-                                                       protect, items, width / 4, hubert_frames);
+        frontend_kernel<true><<<target, row_threads(width / 4), 0, stream>>>(
+            hubert, raw, f0, ratio, protect, hubert_frames, width, mel_min, mel_scale, feats, pitchf, pitch);
     else
-        protect_scalar_kernel<<<grid, 256, 0, stream>>>(features, raw, pitchf, ratio, protect, elements, width,
-                                                         hubert_frames);
+        frontend_kernel<false><<<target, row_threads(width), 0, stream>>>(
+            hubert, raw, f0, ratio, protect, hubert_frames, width, mel_min, mel_scale, feats, pitchf, pitch);
 }
 
 }  // namespace vfr

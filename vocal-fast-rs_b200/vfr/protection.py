@@ -60,3 +60,30 @@ class RetrievalProtection:
         call(load_library().vocal_retrieval_protect, _ptr(features), _ptr(self.raw), _ptr(pitchf), _ptr(ratio),
              _ptr(self.amount), ctypes.c_int32(frames), ctypes.c_int32(hubert_frames), ctypes.c_int32(self.width),
              ctypes.byref(s))
+
+
+def rvc_frontend(hubert, f0, hubert_frames: int, protection: "RetrievalProtection | None" = None, ratio=None,
+                 stream=None):
+    """The RVC frontend after the blend (crates/vocal-tensorrt/native/
+    frontend.cpp:36-75) with the protection fused when `protection` is given
+    (its raw rows and amount, with the device `ratio`): returns CUDA tensors
+    (feats [target, width], pitchf [target], pitch [target] int32)."""
+    import torch
+
+    width = hubert.shape[-1]
+    f0_frames = f0.numel()
+    target = min(2 * (hubert_frames + 1), f0_frames)
+    feats = torch.empty((target, width), dtype=torch.float32, device=hubert.device)
+    pitchf = torch.empty(target, dtype=torch.float32, device=hubert.device)
+    pitch = torch.empty(target, dtype=torch.int32, device=hubert.device)
+    out = ctypes.c_int32(0)
+    L = load_library()
+    s = stream_struct(stream)
+    raw = amount = rate = None
+    if protection is not None:
+        raw, amount, rate = _ptr(protection.raw), _ptr(protection.amount), _ptr(ratio)
+    call(L.vfr_rvc_frontend, _ptr(hubert), raw, _ptr(f0), rate, amount, ctypes.c_int32(hubert_frames),
+         ctypes.c_int32(f0_frames), ctypes.c_int32(width), _ptr(feats), _ptr(pitchf), _ptr(pitch), ctypes.byref(out),
+         ctypes.byref(s))
+    assert out.value == target
+    return feats, pitchf, pitch
