@@ -263,7 +263,7 @@ def protection(device):
     import torch
 
     from vfr import GpuRetrievalIndex, synth
-    from vfr.protection import RetrievalProtection, rvc_frontend
+    from vfr.protection import RetrievalProtection, engine_frontend, rvc_frontend
 
     w = synth.CONFIGS["c4"]
     arrays, block = synth.make_torch("c4", device, q=w.q)
@@ -317,6 +317,9 @@ def protection(device):
 
     t_front_sep = p50(frontend_then_protect)
     t_front = p50(lambda: rvc_frontend(feats, f0, w.q, prot, rate, stream=s))
+    # the generic engine's linear frontend with its protection and coarse pitch
+    hz = torch.where(torch.rand(2 * w.q, generator=g, device=device) < 0.5, 0.0, 150.0)
+    t_engine = p50(lambda: engine_frontend(feats, w.q, prot.raw, hz, 0.33, stream=s))
     idx.close()
     unvoiced = int((pitch <= 0).sum().item())
     bytes_protect = unvoiced * w.d * 4 * 3 + frames * 4
@@ -324,7 +327,8 @@ def protection(device):
             "copy_then_blend_us_p50": t_copy, "blend_save_raw_us_p50": t_fused,
             "protect_us_p50": t_protect, "protect_bytes": bytes_protect,
             "protect_gbs_at_p50": bytes_protect / (t_protect * 1e-6) / 1e9,
-            "frontend_then_protect_us_p50": t_front_sep, "frontend_fused_us_p50": t_front}
+            "frontend_then_protect_us_p50": t_front_sep, "frontend_fused_us_p50": t_front,
+            "engine_frontend_us_p50": t_engine}
 
 
 def ivf(device):

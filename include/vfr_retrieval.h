@@ -187,6 +187,23 @@ VFR_API int vfr_rvc_frontend(const float *hubert, const float *raw, const float 
                              float *feats, float *pitchf, int32_t *pitch, int32_t *out_frames, VfrStream *stream,
                              char **error);
 
+/* The generic engine's frontend after its index blend, replacing
+ * FeatureMatrix::interpolate_2x and the protection loop of RvcPipeline::run
+ * (crates/vocal-engine/src/pipeline.rs:75-96 and 312-333): out[2 frames]
+ * is the linear 2x interpolation of blended (output frame t mixes frames
+ * floor(t/2) and min(floor(t/2) + 1, frames - 1) at weight 0 or 0.5); when
+ * hz and raw are given and protect < 0.5, each frame t < min(2 frames,
+ * hz_frames) becomes f v + before (1 - v), before the same interpolation of
+ * raw and v = 1 if hz[t] > 0 else protect; coarse[t] = f0_to_coarse(hz[t])
+ * (pipeline.rs:625-633) for the same frames when hz is given.  blended, raw:
+ * device f32 [frames][width]; hz: device f32 [hz_frames] or null; out:
+ * device f32 [2 frames][width]; coarse: device i32 [min(2 frames,
+ * hz_frames)] (required with hz and hz_frames > 0).  protect: finite, in [0, 1];
+ * 2 frames <= 2^24. */
+VFR_API int vfr_engine_frontend(const float *blended, const float *raw, const float *hz, float protect, int32_t frames,
+                                int32_t hz_frames, int32_t width, float *out, int32_t *coarse, VfrStream *stream,
+                                char **error);
+
 /* vocal_faiss_gpu_blend with RetrievalProtection::save_raw fused in
  * (crates/vocal-tensorrt/src/pipeline.rs:1842-1853,
  * crates/vocal-tensorrt/src/retrieval/protection.rs:47-55): raw (device f32

@@ -71,6 +71,10 @@ def lib():
                                        ctypes.c_float, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         L.orc_rvc_frontend.restype = ctypes.c_int64
+        L.orc_engine_frontend.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float,
+                                          ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+                                          ctypes.c_void_p]
+        L.orc_engine_frontend.restype = ctypes.c_int64
         L.orc_view.argtypes = [P(_Index), ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         _lib = L
@@ -229,3 +233,26 @@ def rvc_frontend(hubert: np.ndarray, raw, f0: np.ndarray, ratio: float, amount: 
                                  f0.shape[0], w, _ptr(feats), _ptr(pitchf), _ptr(pitch), _ptr(coarse))
     assert got == target
     return feats, pitchf, pitch, coarse
+
+
+def engine_frontend(blended: np.ndarray, raw, hz, protect: float):
+    """Restated generic-engine frontend (crates/vocal-engine/src/pipeline.rs:
+    75-96, 312-333, 625-633): (features [2 frames][w], coarse [min(2 frames,
+    len(hz))] i32 or None)."""
+    blended = np.ascontiguousarray(blended, dtype=np.float32)
+    frames, w = blended.shape
+    out = np.empty((2 * frames, w), np.float32)
+    rawp = hzp = None
+    hz_frames = 0
+    coarse = None
+    if raw is not None:
+        raw = np.ascontiguousarray(raw, dtype=np.float32)
+        rawp = _ptr(raw)
+    if hz is not None:
+        hz = np.ascontiguousarray(hz, dtype=np.float32)
+        hzp, hz_frames = _ptr(hz), hz.shape[0]
+        coarse = np.empty(min(2 * frames, hz_frames), np.int32)
+    got = lib().orc_engine_frontend(_ptr(blended), rawp, hzp, ctypes.c_float(protect), frames, hz_frames, w, _ptr(out),
+                                    None if coarse is None else _ptr(coarse))
+    assert got == (0 if coarse is None else coarse.shape[0])
+    return out, coarse

@@ -20,6 +20,8 @@
  *   - RVC frontend:   crates/vocal-tensorrt/native/frontend.cpp:36-75 (append the
  *                     last HuBERT frame, nearest 2x, crop, coarse pitch; a
  *                     TensorRT graph in the reference)
+ *   - engine frontend: crates/vocal-engine/src/pipeline.rs:75-96 (linear 2x),
+ *                     312-333 (protection), 625-633 (f0_to_coarse)
  *
  * Arithmetic order is kept exactly: AVX2 8-lane direct-difference squared L2
  * with separate multiply and add, the eight lanes folded left to right, then
@@ -687,4 +689,56 @@ int64_t orc_rvc_frontend(const float *hubert, const float *raw, const float *f0,
         pitch[t] = (int32_t)rintf(x);
     }
     return target;
+}
+
+/* The generic engine's frontend, restating crates/vocal-engine/src/
+ * pipeline.rs: interpolate_2x (75-96) of the blended features into
+ * out[2 frames][width]; when hz != NULL, raw != NULL and protect < 0.5
+ * (313), the protection (321-333) over t < min(2 frames, hz_frames) against
+ * interpolate_2x of raw; coarse[t] = f0_to_coarse(hz[t]) (625-633) for the
+ * same frames when hz != NULL.  Returns the number of coarse values. */
+static float orc_lerp_half(float a, float b, float w) {
+    const float x = a * (1.0f - w);
+    const float y = b * w;
+    return x + y;
+}
+
+static int32_t orc_f0_to_coarse(float f0, float mel_min, float mel_max) {
+    if (f0 <= 0.0f) return 1;
+    const float mel = 1127.0f * logf(1.0f + f0 / 700.0f);
+    const float scaled = (mel - mel_min) * 254.0f;
+    const float r = roundf(scaled / (mel_max - mel_min) + 1.0f);
+    if (r != r) return 0; /* Rust: clamp keeps NaN, `as i32` saturates NaN to 0 */
+    const float c = r < 1.0f ? 1.0f : (r > 255.0f ? 255.0f : r);
+    return (int32_t)c;
+}
+
+int64_t orc_engine_frontend(const float *blended, const float *raw, const float *hz, float protect, int64_t frames,
+                            int64_t hz_frames, int64_t width, float *out, int32_t *coarse) {
+    const int64_t out_frames = 2 * frames;
+    const int64_t pitch_frames = hz == NULL ? 0 : (hz_frames < out_frames ? hz_frames : out_frames);
+    const int mixing = hz != NULL && raw != NULL && protect < 0.5f;
+    const float p = protect < 0.0f ? 0.0f : (protect > 1.0f ? 1.0f : protect);
+    const float mel_min = 1127.0f * logf(1.0f + 50.0f / 700.0f);
+    const float mel_max = 1127.0f * logf(1.0f + 1100.0f / 700.0f);
+    for (int64_t t = 0; t < out_frames; ++t) {
+        const float source = (float)t / 2.0f;
+        const int64_t left = (int64_t)floorf(source);
+        const int64_t right = left + 1 < frames ? left + 1 : frames - 1;
+        const float w = source - (float)left;
+        const int mix = mixing && t < pitch_frames;
+        const float v = mix ? (hz[t] > 0.0f ? 1.0f : p) : 1.0f;
+        for (int64_t c = 0; c < width; ++c) {
+            float f = orc_lerp_half(blended[left * width + c], blended[right * width + c], w);
+            if (mix) {
+                const float before = orc_lerp_half(raw[left * width + c], raw[right * width + c], w);
+                const float a = f * v;
+                const float b = before * (1.0f - v);
+                f = a + b;
+            }
+            out[t * width + c] = f;
+        }
+        if (hz != NULL && t < pitch_frames) coarse[t] = orc_f0_to_coarse(hz[t], mel_min, mel_max);
+    }
+    return pitch_frames;
 }

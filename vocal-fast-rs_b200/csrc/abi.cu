@@ -5,6 +5,7 @@
 // limits and messages); the error convention follows
 // crates/vocal-tensorrt/native/bridge.h:24-32.
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -246,6 +247,22 @@ extern "C" int vfr_rvc_frontend(const float *hubert, const float *raw, const flo
         if (out_frames) *out_frames = target;
         vfr::launch_frontend(hubert, raw, f0, ratio, protect, hubert_frames, f0_frames, width, feats, pitchf, pitch,
                              static_cast<cudaStream_t>(stream->stream));
+        cuda_check(cudaGetLastError());
+    });
+}
+
+extern "C" int vfr_engine_frontend(const float *blended, const float *raw, const float *hz, float protect,
+                                   int32_t frames, int32_t hz_frames, int32_t width, float *out, int32_t *coarse,
+                                   VfrStream *stream, char **error) {
+    return guarded(error, [&] {
+        require(blended && out && stream && (!hz || hz_frames <= 0 || coarse), "null engine frontend binding");
+        require(std::isfinite(protect) && protect >= 0.0f && protect <= 1.0f, "protect must be finite and in [0,1]");
+        // 2 frames <= 2^24 keeps t / 2.0 exact in f32, as the Rust source computes it
+        require(frames > 0 && width > 0 && frames <= (1 << 23) && 2LL * frames * width <= INT32_MAX &&
+                    (!hz || hz_frames >= 0),
+                "invalid engine frontend dimensions");
+        vfr::launch_engine_frontend(blended, raw, hz, protect, frames, hz ? hz_frames : 0, width, out, coarse,
+                                    static_cast<cudaStream_t>(stream->stream));
         cuda_check(cudaGetLastError());
     });
 }

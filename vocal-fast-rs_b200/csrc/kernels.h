@@ -56,6 +56,11 @@ void launch_frontend(const float *hubert, const float *raw, const float *f0, con
                      const float *protect, int hubert_frames, int f0_frames, int width, float *feats, float *pitchf,
                      int32_t *pitch, cudaStream_t stream);
 
+// The generic engine's linear 2x frontend with its protection and coarse
+// pitch (protect_kernels.cu).
+void launch_engine_frontend(const float *blended, const float *raw, const float *hz, float protect, int frames,
+                            int hz_frames, int width, float *out, int32_t *coarse, cudaStream_t stream);
+
 // Sharded helpers (shard_kernels.cu).
 void launch_merge_topk(const float *dist, const int64_t *labels, int shards, long long frames, float *out_dist,
                        int64_t *out_labels, cudaStream_t stream);

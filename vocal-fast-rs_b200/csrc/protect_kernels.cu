@@ -162,3 +162,100 @@ void launch_frontend(const float *hubert, const float *raw, const float *f0, con
 }
 
 }  // namespace vfr
+
+// ------------------------------------------------------- engine frontend
+// The generic engine's frontend (crates/vocal-engine/src/pipeline.rs): the
+// blended features are interpolated 2x linearly (75-96: output frame t reads
+// source t / 2, left = floor, right = min(left + 1, frames - 1), weight 0 or
+// 0.5, a (1 - w) + b w), the features saved before the blend are
+// interpolated the same way and, when protect < 0.5, every frame below
+// min(2 frames, pitch frames) becomes f v + before (1 - v) with v = 1 for
+// pitch > 0 and protect otherwise (312-333); the coarse pitch of those frames
+// is f0_to_coarse (625-633: 1 at or below 0 Hz, Rust's f32 ln, division by
+// 700 and by the mel span, rounding half away from zero, 0 for NaN through
+// the saturating cast).  Every operation is rounded on its own, as in the
+// Rust source.
+namespace vfr {
+namespace {
+
+__device__ __forceinline__ float lerp_half(float a, float b, float w) {
+    return __fadd_rn(__fmul_rn(a, __fsub_rn(1.0f, w)), __fmul_rn(b, w));
+}
+
+__device__ __forceinline__ float engine_protect(float f, float before, float v) {
+    return __fadd_rn(__fmul_rn(f, v), __fmul_rn(before, __fsub_rn(1.0f, v)));
+}
+
+// One CTA per output frame (2 frames of them); four columns per lane when kVec.
+template <bool kVec>
+__global__ void engine_frontend_kernel(const float *__restrict__ blended, const float *__restrict__ raw,
+                                       const float *__restrict__ hz, float protect, int frames, int pitch_frames,
+                                       int width, float mel_min, float mel_span, float *__restrict__ out,
+                                       int32_t *__restrict__ coarse) {
+    const int t = blockIdx.x;
+    const int left = t >> 1;
+    const int right = left + 1 < frames ? left + 1 : frames - 1;
+    const float w = (t & 1) ? 0.5f : 0.0f;
+    const bool mixing = raw != nullptr && t < pitch_frames;
+    const float v = mixing ? (hz[t] > 0.0f ? 1.0f : protect) : 1.0f;
+    const long long lo = static_cast<long long>(left) * width, hi = static_cast<long long>(right) * width;
+    float *o = out + static_cast<long long>(t) * width;
+    if (kVec) {
+        for (int c = threadIdx.x; c < width / 4; c += blockDim.x) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(blended + lo) + c);
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(blended + hi) + c);
+            float4 f = make_float4(lerp_half(a.x, b.x, w), lerp_half(a.y, b.y, w), lerp_half(a.z, b.z, w),
+                                   lerp_half(a.w, b.w, w));
+            if (mixing) {
+                const float4 ra = __ldg(reinterpret_cast<const float4 *>(raw + lo) + c);
+                const float4 rb = __ldg(reinterpret_cast<const float4 *>(raw + hi) + c);
+                f = make_float4(engine_protect(f.x, lerp_half(ra.x, rb.x, w), v),
+                                engine_protect(f.y, lerp_half(ra.y, rb.y, w), v),
+                                engine_protect(f.z, lerp_half(ra.z, rb.z, w), v),
+                                engine_protect(f.w, lerp_half(ra.w, rb.w, w), v));
+            }
+            reinterpret_cast<float4 *>(o)[c] = f;
+        }
+    } else {
+        for (int c = threadIdx.x; c < width; c += blockDim.x) {
+            float f = lerp_half(__ldg(blended + lo + c), __ldg(blended + hi + c), w);
+            if (mixing) f = engine_protect(f, lerp_half(__ldg(raw + lo + c), __ldg(raw + hi + c), w), v);
+            o[c] = f;
+        }
+    }
+    if (threadIdx.x == 0 && coarse != nullptr && t < pitch_frames) {
+        const float f0 = hz[t];
+        int32_t bin = 1;
+        if (!(f0 <= 0.0f)) {
+            const float mel = __fmul_rn(1127.0f, logf(__fadd_rn(1.0f, __fdiv_rn(f0, 700.0f))));
+            const float x = __fadd_rn(__fdiv_rn(__fmul_rn(__fsub_rn(mel, mel_min), 254.0f), mel_span), 1.0f);
+            const float r = roundf(x);  // half away from zero, as Rust's f32::round
+            // Rust's clamp keeps NaN and `as i32` maps NaN to 0
+            bin = r != r ? 0 : static_cast<int32_t>(fminf(fmaxf(r, 1.0f), 255.0f));
+        }
+        coarse[t] = bin;
+    }
+}
+
+}  // namespace
+
+void launch_engine_frontend(const float *blended, const float *raw, const float *hz, float protect, int frames,
+                            int hz_frames, int width, float *out, int32_t *coarse, cudaStream_t stream) {
+    const int out_frames = 2 * frames;
+    const int pitch_frames = hz == nullptr ? 0 : (hz_frames < out_frames ? hz_frames : out_frames);
+    // pipeline.rs:313: the pre-blend features take part only when protect < 0.5
+    const float *mix = (hz != nullptr && protect < 0.5f) ? raw : nullptr;
+    // pipeline.rs:629-630, f32 on the host like the Rust constants
+    const float mel_min = 1127.0f * std::log(1.0f + 50.0f / 700.0f);
+    const float mel_max = 1127.0f * std::log(1.0f + 1100.0f / 700.0f);
+    const float mel_span = mel_max - mel_min;
+    const bool vec = width % 4 == 0 && aligned16(blended) && aligned16(out) && (mix == nullptr || aligned16(mix));
+    if (vec)
+        engine_frontend_kernel<true><<<out_frames, row_threads(width / 4), 0, stream>>>(
+            blended, mix, hz, protect, frames, pitch_frames, width, mel_min, mel_span, out, coarse);
+    else
+        engine_frontend_kernel<false><<<out_frames, row_threads(width), 0, stream>>>(
+            blended, mix, hz, protect, frames, pitch_frames, width, mel_min, mel_span, out, coarse);
+}
+
+}  // namespace vfr

@@ -67,6 +67,7 @@ def load_library(path: str | None = None):
         "vocal_faiss_gpu_blend": ([vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
         "vocal_retrieval_protect": ([vp, vp, vp, vp, vp, i32, i32, i32, P(Stream), err], ctypes.c_int),
         "vfr_rvc_frontend": ([vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp, P(i32), P(Stream), err], ctypes.c_int),
+        "vfr_engine_frontend": ([vp, vp, vp, ctypes.c_float, i32, i32, i32, vp, vp, P(Stream), err], ctypes.c_int),
         "vfr_retrieval_blend_save_raw": ([vp, vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
         "vfr_free_error": ([vp], None),
         "vfr_index_parse_faiss": ([ctypes.c_char_p, sz, P(vp), err], ctypes.c_int),

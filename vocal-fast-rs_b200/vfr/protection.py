@@ -87,3 +87,24 @@ def rvc_frontend(hubert, f0, hubert_frames: int, protection: "RetrievalProtectio
          ctypes.byref(s))
     assert out.value == target
     return feats, pitchf, pitch
+
+
+def engine_frontend(blended, frames: int, raw=None, hz=None, protect: float = 0.33, stream=None):
+    """The generic engine's frontend (crates/vocal-engine/src/pipeline.rs:
+    75-96, 312-333, 625-633) on the device: returns (features [2 frames,
+    width], coarse [min(2 frames, hz frames)] int32 or None)."""
+    import torch
+
+    width = blended.shape[-1]
+    out = torch.empty((2 * frames, width), dtype=torch.float32, device=blended.device)
+    coarse = None
+    hz_frames = 0
+    if hz is not None:
+        hz_frames = hz.numel()
+        coarse = torch.empty(min(2 * frames, hz_frames), dtype=torch.int32, device=blended.device)
+    s = stream_struct(stream)
+    call(load_library().vfr_engine_frontend, _ptr(blended), None if raw is None else _ptr(raw),
+         None if hz is None else _ptr(hz), ctypes.c_float(protect), ctypes.c_int32(frames), ctypes.c_int32(hz_frames),
+         ctypes.c_int32(width), _ptr(out), None if coarse is None or coarse.numel() == 0 else _ptr(coarse),
+         ctypes.byref(s))
+    return out, coarse
