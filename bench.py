@@ -30,6 +30,7 @@ import datetime
 import json
 import os
 import statistics
+import struct
 import subprocess
 import sys
 import threading
@@ -54,6 +55,7 @@ def args_parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-streaming", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-ingest", action="store_true", help="skip the c5 index-ingest timing")
     return ap.parse_args()
 
 
@@ -331,6 +333,59 @@ def protection(device):
             "engine_frontend_us_p50": t_engine}
 
 
+def ingest(device):
+    """Index ingest for c5 (flat 4,000,000 x 768, a 12.3 GB FAISS image in
+    host memory): the reference's route (host parse RetrievalIndex::from_faiss,
+    then create from the host arrays with pageable copies) against
+    vfr_index_load (rows straight from the image through pinned staging
+    buffers on several host threads, row check on the device), and a
+    shared-storage hit (content hash, no upload).  Wall-clock seconds of one
+    load each, device synchronised on both sides."""
+    import time
+
+    import numpy as np
+    import torch
+
+    from vfr import GpuRetrievalIndex, RetrievalIndex, faiss_io, synth
+
+    arrays, _ = synth.make_torch("c5", device, q=1)
+    v = arrays["vectors"]
+    n, d = v.shape
+    head = faiss_io._index_header(b"IxF2", d, n) + struct.pack("<Q", n * d)
+    raw = np.empty(len(head) + n * d * 4 + 64, np.uint8)
+    # rows 64-byte aligned in the buffer, as a page-aligned file mapping would leave them
+    start = (-(raw.ctypes.data + len(head))) % 64
+    image = raw[start:start + len(head) + n * d * 4]
+    image[:len(head)] = np.frombuffer(head, np.uint8)
+    torch.from_numpy(image[len(head):].view(np.float32).reshape(n, d)).copy_(v)
+    del arrays, v
+    torch.cuda.empty_cache()
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        r = fn()
+        torch.cuda.synchronize()
+        return r, time.perf_counter() - t
+
+    host, t_parse = timed(lambda: RetrievalIndex.from_faiss(image))
+    g, t_create = timed(lambda: GpuRetrievalIndex.upload(host))
+    g.close()
+    del host
+    g, t_load = timed(lambda: GpuRetrievalIndex.load(image))
+    g.close()
+    first, t_first = timed(lambda: GpuRetrievalIndex.load(image, share=True))
+    hit, t_hit = timed(lambda: GpuRetrievalIndex.load(image, share=True))
+    shared = hit.diagnostics()["shared_handles"]
+    hit.close()
+    first.close()
+    nbytes = int(image.size)
+    return {"workload": f"c5 image: flat {n} x {d} FAISS IxF2, {nbytes} bytes in host memory",
+            "reference_parse_s": t_parse, "create_from_host_arrays_s": t_create,
+            "reference_route_s": t_parse + t_create, "load_s": t_load, "load_gbs": nbytes / t_load / 1e9,
+            "load_shared_first_s": t_first, "load_shared_hit_s": t_hit, "shared_handles": shared}
+
+
 def ivf(device):
     """c3: IVF-Flat 200k x 768, nlist 256 (20 seeded k-means iterations), 30k
     frames, nprobe 1 and 8; frames/s of the blend (CUDA events)."""
@@ -524,6 +579,8 @@ def main():
         extra["streaming"] = streaming(device)
         extra["protection"] = protection(device)
         extra["ivf"] = ivf(device)
+        if not a.no_ingest:
+            extra["ingest"] = ingest(device)
     cpu = None
     if rank == 0 and world == 1 and full_host is not None:
         cpu = cpu_baseline(full_host, queries.cpu().numpy(), w.ratio, n)

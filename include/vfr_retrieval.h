@@ -138,11 +138,19 @@ enum {
     VFR_ENGINE_TENSOR = 2  /* tensor-core candidates + exact re-rank */
 };
 
+/* VfrOptions.flags */
+enum {
+    /* Loaders only: handles loaded from identical FAISS bytes on one device
+     * (same engine class) share one copy of the device arrays; each handle
+     * keeps its own workspace and counters. */
+    VFR_SHARE_STORAGE = 1
+};
+
 typedef struct VfrOptions {
     int32_t struct_size;   /* sizeof(VfrOptions) */
     int32_t engine;        /* VFR_ENGINE_* */
     int32_t candidates;    /* re-rank width per frame (16..128, multiple of 16); 0 = 64 */
-    int32_t reserved0;
+    int32_t flags;         /* VFR_SHARE_STORAGE, loaders only; 0 = none */
     int64_t label_base;    /* added to every returned label (row-sharded shards) */
     int64_t max_frames;    /* workspace pre-size; 0 = grow on demand (outside capture) */
 } VfrOptions;
@@ -153,6 +161,27 @@ VFR_API int vfr_retrieval_create(int32_t dimensions, int32_t nlist, int32_t npro
                          size_t offset_count, const float *vectors, size_t vector_value_count,
                          const int32_t *ids, size_t id_count, const VfrOptions *options, VfrIndex **out,
                          char **error);
+
+/* Device ingest: RetrievalIndex::from_faiss + GpuRetrievalIndex::new in one
+ * call (crates/vocal-model/src/retrieval.rs:45-193, crates/vocal-tensorrt/
+ * src/retrieval.rs:27-60) without the host copy of the rows: the FAISS
+ * structure is checked on the host with the parser's checks and messages,
+ * the rows go straight from `bytes` to device memory through pinned staging
+ * buffers on several host threads, and the finite check runs on the device;
+ * the error reported is the one the reference parser reports first.  options
+ * may be NULL; with VFR_SHARE_STORAGE, handles loaded from identical bytes
+ * on the same device share the device arrays. */
+VFR_API int vfr_index_load(const uint8_t *bytes, size_t length, const VfrOptions *options, VfrIndex **out,
+                           char **error);
+/* The same from a VFRM image's aux.retrieval.faiss tensor; *out stays NULL
+ * (rc 0) when the image has none; feature_dims > 0 must match the index
+ * width (retrieval.rs:45-57). */
+VFR_API int vfr_index_load_vfrm(const uint8_t *image, size_t length, int32_t feature_dims,
+                                const VfrOptions *options, VfrIndex **out, char **error);
+/* The same from a file (a FAISS .index, or a VFRM package recognised by its
+ * magic), mapped read-only: the page cache is the only host copy. */
+VFR_API int vfr_index_load_file(const char *path, int32_t feature_dims, const VfrOptions *options, VfrIndex **out,
+                                char **error);
 
 /* Sizes the per-index workspace for up to max_frames frames per call, so that
  * later calls allocate nothing (required before CUDA graph capture). */

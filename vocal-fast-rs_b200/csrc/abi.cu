@@ -7,9 +7,12 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <map>
+#include <memory>
 #include <mutex>
 #include <string>
 
+#include "ingest.h"
 #include "kernels.h"
 #include "tc_path.h"
 #include "vfr_common.h"
@@ -22,6 +25,19 @@ char *make_error(const char *message) noexcept {
     auto *result = static_cast<char *>(std::malloc(bytes));
     if (result) std::memcpy(result, message, bytes);
     return result;
+}
+
+SharedRows::~SharedRows() {
+    int previous = 0;
+    cudaGetDevice(&previous);
+    cudaSetDevice(proto.device);
+    for (void *p : {static_cast<void *>(proto.centroids), static_cast<void *>(proto.offsets),
+                    static_cast<void *>(proto.vectors), static_cast<void *>(proto.ids),
+                    static_cast<void *>(proto.row_of_id), static_cast<void *>(proto.vectors_h),
+                    static_cast<void *>(proto.row_norms), static_cast<void *>(proto.centroids_h),
+                    static_cast<void *>(proto.centroid_norms)})
+        if (p) cudaFree(p);
+    cudaSetDevice(previous);
 }
 
 namespace {
@@ -49,10 +65,13 @@ void free_index(VfrIndex *ix) noexcept {
     cudaGetDevice(&previous);
     cudaSetDevice(ix->device);
     release_tc(ix);
-    for (void *p : {static_cast<void *>(ix->centroids), static_cast<void *>(ix->offsets),
-                    static_cast<void *>(ix->vectors), static_cast<void *>(ix->ids),
-                    static_cast<void *>(ix->row_of_id), static_cast<void *>(ix->counters)})
-        if (p) cudaFree(p);
+    if (!ix->shared)
+        for (void *p : {static_cast<void *>(ix->centroids), static_cast<void *>(ix->offsets),
+                        static_cast<void *>(ix->vectors), static_cast<void *>(ix->ids),
+                        static_cast<void *>(ix->row_of_id)})
+            if (p) cudaFree(p);
+    if (ix->counters) cudaFree(ix->counters);
+    ix->shared.reset();
     cudaSetDevice(previous);
     delete ix;
 }
@@ -78,11 +97,7 @@ void validate_arrays(int32_t d, int32_t nlist, int32_t nprobe, size_t n, const f
     for (int32_t i = 0; i < nlist; ++i) require(offsets[i] <= offsets[i + 1], "FAISS list offsets are not monotonic");
 }
 
-VfrIndex *create_index(int32_t d, int32_t nlist, int32_t nprobe, size_t n, const float *centroids,
-                       size_t centroid_count, const int32_t *offsets, size_t offset_count, const float *vectors,
-                       size_t vector_value_count, const int32_t *ids, size_t id_count, const VfrOptions *opt) {
-    validate_arrays(d, nlist, nprobe, n, centroids, centroid_count, offsets, offset_count, vectors,
-                    vector_value_count, ids, id_count);
+VfrOptions resolve_options(const VfrOptions *opt) {
     VfrOptions o{};
     o.struct_size = sizeof(VfrOptions);
     if (opt) {
@@ -95,36 +110,199 @@ VfrIndex *create_index(int32_t d, int32_t nlist, int32_t nprobe, size_t n, const
     require(o.candidates >= 16 && o.candidates <= 128 && o.candidates % 16 == 0,
             "candidate width must be a multiple of 16 in 16..128");
     require(o.label_base >= 0 && o.max_frames >= 0, "invalid label base or frame reservation");
-    // The reference parser guarantees ids form a permutation of 0..n; the raw
-    // ABI (like retrieval.cu) accepts any ids, so the inverse map used by
-    // vfr_gather_owned is only built when they do.
-    std::vector<int32_t> inverse(n, -1);
-    bool permutation = true;
-    for (size_t r = 0; r < n && permutation; ++r) {
-        if (ids[r] < 0 || static_cast<size_t>(ids[r]) >= n || inverse[ids[r]] >= 0) permutation = false;
-        else inverse[ids[r]] = static_cast<int32_t>(r);
+    require((o.flags & ~VFR_SHARE_STORAGE) == 0, "unknown retrieval option flags");
+    return o;
+}
+
+// The inverse map used by vfr_gather_owned, when ids form a permutation of
+// 0..n-1 (the reference parser guarantees it; the raw ABI, like
+// retrieval.cu, accepts any ids).
+bool inverse_ids(const int32_t *ids, size_t n, std::vector<int32_t> &inverse) {
+    inverse.assign(n, -1);
+    for (size_t r = 0; r < n; ++r) {
+        if (ids[r] < 0 || static_cast<size_t>(ids[r]) >= n || inverse[ids[r]] >= 0) return false;
+        inverse[ids[r]] = static_cast<int32_t>(r);
     }
+    return true;
+}
+
+VfrIndex *new_handle(int32_t d, int32_t nlist, int32_t nprobe, size_t n, const int32_t *offsets,
+                     const VfrOptions &o) {
     auto *ix = new VfrIndex{};
+    ix->d = d;
+    ix->nlist = nlist;
+    ix->nprobe = nprobe;
+    ix->n = static_cast<int64_t>(n);
+    ix->label_base = o.label_base;
+    ix->engine = o.engine;
+    ix->candidates = o.candidates;
+    ix->host_offsets.assign(offsets, offsets + nlist + 1);
     try {
         cuda_check(cudaGetDevice(&ix->device));
-        ix->d = d;
-        ix->nlist = nlist;
-        ix->nprobe = nprobe;
-        ix->n = static_cast<int64_t>(n);
-        ix->label_base = o.label_base;
-        ix->engine = o.engine;
-        ix->candidates = o.candidates;
-        ix->host_offsets.assign(offsets, offsets + nlist + 1);
+    } catch (...) {
+        delete ix;
+        throw;
+    }
+    return ix;
+}
+
+// Counters, the tensor-core layout and the workspace reservation.
+void finish_index(VfrIndex *ix, const VfrOptions &o) {
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->counters), sizeof(DeviceCounters)));
+    cuda_check(cudaMemset(ix->counters, 0, sizeof(DeviceCounters)));
+    if (!ix->shared && ix->engine != VFR_ENGINE_EXACT) build_tc(ix);
+    if (o.max_frames > 0) reserve_tc(ix, static_cast<size_t>(o.max_frames));
+    cuda_check(cudaDeviceSynchronize());
+}
+
+VfrIndex *create_index(int32_t d, int32_t nlist, int32_t nprobe, size_t n, const float *centroids,
+                       size_t centroid_count, const int32_t *offsets, size_t offset_count, const float *vectors,
+                       size_t vector_value_count, const int32_t *ids, size_t id_count, const VfrOptions *opt) {
+    validate_arrays(d, nlist, nprobe, n, centroids, centroid_count, offsets, offset_count, vectors,
+                    vector_value_count, ids, id_count);
+    const VfrOptions o = resolve_options(opt);
+    std::vector<int32_t> inverse;
+    const bool permutation = inverse_ids(ids, n, inverse);
+    VfrIndex *ix = new_handle(d, nlist, nprobe, n, offsets, o);
+    try {
         alloc_copy(&ix->centroids, centroids, centroid_count);
         alloc_copy(&ix->offsets, offsets, offset_count);
         alloc_copy(&ix->vectors, vectors, vector_value_count);
         alloc_copy(&ix->ids, ids, id_count);
         if (permutation) alloc_copy(&ix->row_of_id, inverse.data(), n);
-        cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->counters), sizeof(DeviceCounters)));
-        cuda_check(cudaMemset(ix->counters, 0, sizeof(DeviceCounters)));
-        if (ix->engine != VFR_ENGINE_EXACT) build_tc(ix);
-        if (o.max_frames > 0) reserve_tc(ix, static_cast<size_t>(o.max_frames));
-        cuda_check(cudaDeviceSynchronize());
+        finish_index(ix, o);
+    } catch (...) {
+        free_index(ix);
+        throw;
+    }
+    return ix;
+}
+
+// ---- device ingest of FAISS bytes ---------------------------------------
+
+struct ShareKey {
+    ContentHash hash;
+    size_t length;
+    int device;
+    bool tensor;
+    bool operator<(const ShareKey &k) const {
+        if (!(hash == k.hash)) return hash < k.hash;
+        if (length != k.length) return length < k.length;
+        if (device != k.device) return device < k.device;
+        return tensor < k.tensor;
+    }
+};
+
+std::mutex share_lock;
+std::map<ShareKey, std::weak_ptr<SharedRows>> &share_table() {
+    static auto *table = new std::map<ShareKey, std::weak_ptr<SharedRows>>();
+    return *table;
+}
+
+VfrIndex *handle_from_shared(const std::shared_ptr<SharedRows> &rows, const VfrOptions &o) {
+    auto *ix = new VfrIndex(rows->proto);
+    ix->shared = rows;
+    ix->label_base = o.label_base;
+    ix->engine = o.engine;
+    ix->candidates = o.candidates;
+    try {
+        DeviceGuard guard(ix->device);
+        finish_index(ix, o);
+    } catch (...) {
+        free_index(ix);
+        throw;
+    }
+    return ix;
+}
+
+// Turns a freshly loaded handle into the first holder of shared rows.
+void publish_shared(VfrIndex *ix, const ShareKey &key) {
+    auto rows = std::make_shared<SharedRows>();
+    rows->proto = *ix;
+    rows->proto.counters = nullptr;
+    rows->proto.ws = Workspace{};
+    rows->proto.prof.pool.clear();
+    rows->proto.prof.marks.clear();
+    rows->proto.prof.used = 0;
+    ix->shared = rows;
+    std::lock_guard<std::mutex> g(share_lock);
+    share_table()[key] = rows;
+}
+
+// RetrievalIndex::from_faiss + GpuRetrievalIndex::new in one pass
+// (crates/vocal-model/src/retrieval.rs:62-193, crates/vocal-tensorrt/src/
+// retrieval.rs:27-60): the structure is walked on the host, the rows go from
+// the image to HBM through staged_upload without a host copy, the finite
+// check runs on the device, and the error raised is the one the reference
+// parser raises first.
+VfrIndex *load_index(const uint8_t *bytes, size_t length, int32_t feature_dims, const VfrOptions *opt) {
+    const VfrOptions o = resolve_options(opt);
+    const bool share = (o.flags & VFR_SHARE_STORAGE) != 0;
+    ShareKey key{};
+    if (share) {
+        require(bytes != nullptr || length == 0, "null FAISS byte buffer");
+        key.hash = content_hash(bytes, length);
+        key.length = length;
+        cuda_check(cudaGetDevice(&key.device));
+        key.tensor = o.engine != VFR_ENGINE_EXACT;
+        std::shared_ptr<SharedRows> rows;
+        {
+            std::lock_guard<std::mutex> g(share_lock);
+            auto it = share_table().find(key);
+            if (it != share_table().end() && !(rows = it->second.lock())) share_table().erase(it);
+        }
+        if (rows) {
+            if (feature_dims > 0 && rows->proto.d != feature_dims)
+                throw std::runtime_error("RVC retrieval index: index feature width does not match the voice model");
+            return handle_from_shared(rows, o);
+        }
+    }
+    FaissLayout L = faiss_layout(bytes, length);
+    std::vector<int32_t> ids;
+    const size_t bad_id = scan_ids(L, bytes, ids);
+    if (bad_id != FaissLayout::kNoFault) {
+        // error path: a non-finite row before the bad id wins, as in the reference
+        size_t nonfinite = FaissLayout::kNoFault;
+        for (const auto &list : L.lists) {
+            if (list.vec_pos > bad_id || nonfinite != FaissLayout::kNoFault) break;
+            for (uint64_t i = 0; i < list.size * static_cast<uint64_t>(L.d); ++i) {
+                float v;
+                std::memcpy(&v, bytes + list.vec_pos + 4 * i, 4);
+                if (!std::isfinite(v)) {
+                    nonfinite = list.vec_pos + 4 * i;
+                    break;
+                }
+            }
+        }
+        raise_first_fault(L, nonfinite, bad_id);
+    }
+    const size_t n = static_cast<size_t>(L.n);
+    const size_t values = n * static_cast<size_t>(L.d);
+    std::vector<int32_t> inverse;
+    const bool permutation = inverse_ids(ids.data(), n, inverse);
+    VfrIndex *ix = new_handle(L.d, L.nlist, L.nprobe, n, L.offsets.data(), o);
+    try {
+        alloc_copy(&ix->centroids, L.centroids.data(), L.centroids.size());
+        alloc_copy(&ix->offsets, L.offsets.data(), L.offsets.size());
+        alloc_copy(&ix->ids, ids.data(), n);
+        if (permutation) alloc_copy(&ix->row_of_id, inverse.data(), n);
+        cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->vectors), values * sizeof(float)), "cudaMalloc rows");
+        std::vector<UploadSpan> spans;
+        size_t at = 0;
+        for (const auto &list : L.lists) {
+            const size_t b = static_cast<size_t>(list.size) * L.d * sizeof(float);
+            if (b) spans.push_back({bytes + list.vec_pos, b, at});
+            at += b;
+        }
+        staged_upload(ix->vectors, spans, ix->device);
+        const unsigned long long first = first_nonfinite(ix->vectors, values, ix->sm_count);
+        raise_first_fault(L, first == ~0ull ? FaissLayout::kNoFault : L.row_position(first), FaissLayout::kNoFault);
+        if (feature_dims > 0 && L.d != feature_dims)
+            throw std::runtime_error("RVC retrieval index: index feature width does not match the voice model");
+        validate_arrays(L.d, L.nlist, L.nprobe, n, L.centroids.data(), L.centroids.size(), L.offsets.data(),
+                        L.offsets.size(), ix->vectors, values, ids.data(), n);
+        finish_index(ix, o);
+        if (share) publish_shared(ix, key);
     } catch (...) {
         free_index(ix);
         throw;
@@ -328,11 +506,12 @@ extern "C" size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t 
                           "\"nprobe\":%d,\"vectors\":%lld,\"label_base\":%lld,\"device\":%d,\"workspace_frames\":%zu,"
                           "\"workspace_bytes\":%zu,\"empty_frames\":%llu,\"fallback_frames\":%llu,"
                           "\"candidate_frames\":%llu,\"timeouts\":%llu,\"max_row_norm\":%.9g,"
-                          "\"max_row_residual\":%.9g}",
+                          "\"max_row_residual\":%.9g,\"shared_handles\":%ld}",
                           engine, index->have_tc ? "true" : "false", index->candidates, index->d, index->nlist,
                           index->nprobe, static_cast<long long>(index->n), static_cast<long long>(index->label_base),
                           index->device, index->ws.frames, index->ws.bytes, c.empty_frames, c.fallback_frames,
-                          c.candidate_frames, c.timeouts, index->max_row_norm, index->max_row_residual);
+                          c.candidate_frames, c.timeouts, index->max_row_norm, index->max_row_residual,
+                          static_cast<long>(index->shared ? index->shared.use_count() : 0));
     size_t need = m > 0 ? static_cast<size_t>(m) : 0;
     if (json && length) {
         size_t w = std::min(need, length - 1);
@@ -439,6 +618,43 @@ extern "C" int vfr_index_upload(const VfrHostIndex *index, VfrIndex **out, char 
         *out = vfr::create_index(h.d, h.nlist, h.nprobe, static_cast<size_t>(h.n), h.centroids.data(),
                                  h.centroids.size(), h.offsets.data(), h.offsets.size(), h.vectors.data(),
                                  h.vectors.size(), h.ids.data(), h.ids.size(), nullptr);
+    });
+}
+
+extern "C" int vfr_index_load(const uint8_t *bytes, size_t length, const VfrOptions *options, VfrIndex **out,
+                              char **error) {
+    return guarded(error, [&] {
+        require(out, "null FAISS GPU index output");
+        *out = nullptr;
+        *out = vfr::load_index(bytes, length, 0, options);
+    });
+}
+
+extern "C" int vfr_index_load_vfrm(const uint8_t *image, size_t length, int32_t feature_dims,
+                                   const VfrOptions *options, VfrIndex **out, char **error) {
+    return guarded(error, [&] {
+        require(out && image, "null VFRM input or output");
+        *out = nullptr;
+        size_t off = 0, size = 0;
+        if (!vfr::find_vfrm_faiss(image, length, &off, &size)) return;
+        *out = vfr::load_index(image + off, size, feature_dims, options);
+    });
+}
+
+extern "C" int vfr_index_load_file(const char *path, int32_t feature_dims, const VfrOptions *options, VfrIndex **out,
+                                   char **error) {
+    return guarded(error, [&] {
+        require(out && path, "null index path or output");
+        *out = nullptr;
+        vfr::MappedFile file(path);
+        static const uint8_t vfrm[4] = {'V', 'F', 'R', 'M'};
+        if (file.size >= 4 && std::memcmp(file.data, vfrm, 4) == 0) {
+            size_t off = 0, size = 0;
+            if (!vfr::find_vfrm_faiss(file.data, file.size, &off, &size)) return;
+            *out = vfr::load_index(file.data + off, size, feature_dims, options);
+        } else {
+            *out = vfr::load_index(file.data, file.size, feature_dims, options);
+        }
     });
 }
 

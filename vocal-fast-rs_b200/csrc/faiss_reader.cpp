@@ -8,6 +8,7 @@
 // IVF ids must be a permutation of 0..ntotal.  A Flat index becomes one list
 // with a zero centroid and nprobe 1.  Error messages keep the reference's
 // wording so callers see the same diagnostics.
+#include <algorithm>
 #include <cmath>
 #include <limits>
 
@@ -93,22 +94,30 @@ uint64_t le64(const uint8_t *p) {
 
 }  // namespace
 
-HostIndex parse_faiss(const uint8_t *bytes, size_t length) {
+// The structure walk: every check of RetrievalIndex::from_faiss that does
+// not depend on the row payload runs here, in the reference's order, and
+// throws at once.  The payload checks (finite rows, unique ids) are left to
+// the caller, which reports the fault that comes first in the file
+// (first_fault), so a host parse and a device ingest raise the same error.
+FaissLayout faiss_layout(const uint8_t *bytes, size_t length) {
     require(bytes != nullptr || length == 0, "null FAISS byte buffer");
     ByteReader r(bytes, length);
-    HostIndex ix;
+    FaissLayout L;
     uint32_t kind = r.tag();
     uint64_t d = 0, count = 0;
     r.header(d, count);
     if (kind == fourcc("IxF2")) {
         if (count > std::numeric_limits<uint64_t>::max() / d) bad("shape overflow");
-        r.floats(d * count, true, ix.vectors);
-        ix.centroids.assign(d, 0.f);
-        ix.offsets = {0, static_cast<int32_t>(count)};
-        ix.ids.resize(count);
-        for (uint64_t i = 0; i < count; ++i) ix.ids[i] = static_cast<int32_t>(i);
-        ix.nprobe = 1;
-        ix.nlist = 1;
+        if (r.u64() != d * count) bad("float vector length mismatch");
+        if (d * count > std::numeric_limits<size_t>::max() / 4) bad("float shape overflow");
+        const size_t pos = static_cast<size_t>(r.take(static_cast<size_t>(d * count * 4)) - bytes);
+        L.lists.push_back({pos, FaissLayout::kImplicitIds, count});
+        L.centroids.assign(d, 0.f);
+        L.offsets = {0, static_cast<int32_t>(count)};
+        L.nprobe = 1;
+        L.nlist = 1;
+        // checked after the rows, like the reference's final trailing check
+        L.trailing = r.remaining() != 0;
     } else if (kind == fourcc("IwFl")) {
         uint64_t nlist = r.u64();
         uint64_t nprobe = r.u64();
@@ -118,7 +127,7 @@ HostIndex parse_faiss(const uint8_t *bytes, size_t length) {
         r.header(cd, cc);
         if (cd != d || cc != nlist) bad("coarse quantizer shape mismatch");
         if (nlist > std::numeric_limits<uint64_t>::max() / d) bad("centroid shape overflow");
-        r.floats(nlist * d, true, ix.centroids);
+        r.floats(nlist * d, true, L.centroids);
         // Direct maps only accelerate id lookups; they carry no search data.
         uint8_t map_kind = r.take(1)[0];
         uint64_t map_len = r.u64();
@@ -151,29 +160,88 @@ HostIndex parse_faiss(const uint8_t *bytes, size_t length) {
         if (total != count) bad("list sizes disagree with ntotal");
         if (count > std::numeric_limits<uint64_t>::max() / (d * 4 + 8)) bad("payload overflow");
         if (count * (d * 4 + 8) != r.remaining()) bad("truncated or trailing IVF payload");
-        ix.vectors.reserve(count * d);
-        ix.ids.reserve(count);
-        ix.offsets.reserve(nlist + 1);
-        std::vector<uint8_t> seen(count, 0);
-        ix.offsets.push_back(0);
+        L.lists.reserve(nlist);
+        L.offsets.reserve(nlist + 1);
+        L.offsets.push_back(0);
         for (uint64_t s : sizes) {
-            r.floats(s * d, false, ix.vectors);
-            for (uint64_t i = 0; i < s; ++i) {
-                uint64_t id = r.u64();
-                if (id >= count || seen[id]) bad("RVC requires unique IDs in 0..ntotal");
-                seen[id] = 1;
-                ix.ids.push_back(static_cast<int32_t>(id));
-            }
-            ix.offsets.push_back(static_cast<int32_t>(ix.ids.size()));
+            const size_t vec_pos = static_cast<size_t>(r.take(static_cast<size_t>(s * d * 4)) - bytes);
+            const size_t id_pos = static_cast<size_t>(r.take(static_cast<size_t>(s * 8)) - bytes);
+            L.lists.push_back({vec_pos, id_pos, s});
+            L.offsets.push_back(L.offsets.back() + static_cast<int32_t>(s));
         }
-        ix.nprobe = static_cast<int32_t>(nprobe);
-        ix.nlist = static_cast<int32_t>(nlist);
+        L.nprobe = static_cast<int32_t>(nprobe);
+        L.nlist = static_cast<int32_t>(nlist);
     } else {
         bad("supported FAISS types are IxF2 and IwFl (L2 Flat/IVFFlat)");
     }
-    if (r.remaining() != 0) bad("unexpected trailing data");
-    ix.d = static_cast<int32_t>(d);
-    ix.n = static_cast<int64_t>(count);
+    L.d = static_cast<int32_t>(d);
+    L.n = static_cast<int64_t>(count);
+    return L;
+}
+
+size_t FaissLayout::row_position(uint64_t element) const {
+    const uint64_t row = element / static_cast<uint64_t>(d);
+    // the list holding `row`: offsets is non-decreasing, lists are in file order
+    const auto it = std::upper_bound(offsets.begin(), offsets.end(), static_cast<int32_t>(row));
+    const size_t list = static_cast<size_t>(it - offsets.begin()) - 1;
+    const uint64_t first = static_cast<uint64_t>(offsets[list]) * static_cast<uint64_t>(d);
+    return lists[list].vec_pos + static_cast<size_t>(element - first) * 4;
+}
+
+size_t scan_ids(const FaissLayout &L, const uint8_t *bytes, std::vector<int32_t> &ids) {
+    ids.resize(static_cast<size_t>(L.n));
+    if (L.lists.size() == 1 && L.lists[0].id_pos == FaissLayout::kImplicitIds) {
+        for (int64_t i = 0; i < L.n; ++i) ids[i] = static_cast<int32_t>(i);
+        return FaissLayout::kNoFault;
+    }
+    std::vector<uint8_t> seen(static_cast<size_t>(L.n), 0);
+    size_t row = 0;
+    for (const auto &list : L.lists) {
+        const uint8_t *p = bytes + list.id_pos;
+        for (uint64_t i = 0; i < list.size; ++i, ++row) {
+            const uint64_t id = le64(p + 8 * i);
+            if (id >= static_cast<uint64_t>(L.n) || seen[id]) return list.id_pos + 8 * i;
+            seen[id] = 1;
+            ids[row] = static_cast<int32_t>(id);
+        }
+    }
+    return FaissLayout::kNoFault;
+}
+
+void raise_first_fault(const FaissLayout &L, size_t nonfinite_pos, size_t bad_id_pos) {
+    if (nonfinite_pos != FaissLayout::kNoFault || bad_id_pos != FaissLayout::kNoFault) {
+        if (nonfinite_pos < bad_id_pos) bad("non-finite vector");
+        bad("RVC requires unique IDs in 0..ntotal");
+    }
+    if (L.trailing) bad("unexpected trailing data");
+}
+
+HostIndex parse_faiss(const uint8_t *bytes, size_t length) {
+    FaissLayout L = faiss_layout(bytes, length);
+    HostIndex ix;
+    ix.vectors.resize(static_cast<size_t>(L.n) * L.d);
+    size_t nonfinite = FaissLayout::kNoFault;
+    size_t at = 0;
+    for (const auto &list : L.lists) {
+        const size_t count = static_cast<size_t>(list.size) * L.d;
+        float *dst = ix.vectors.data() + at;
+        std::memcpy(dst, bytes + list.vec_pos, count * 4);
+        if (nonfinite == FaissLayout::kNoFault)
+            for (size_t i = 0; i < count; ++i)
+                if (!std::isfinite(dst[i])) {
+                    nonfinite = list.vec_pos + i * 4;
+                    break;
+                }
+        at += count;
+    }
+    const size_t bad_id = scan_ids(L, bytes, ix.ids);
+    raise_first_fault(L, nonfinite, bad_id);
+    ix.d = L.d;
+    ix.nlist = L.nlist;
+    ix.nprobe = L.nprobe;
+    ix.n = L.n;
+    ix.centroids = std::move(L.centroids);
+    ix.offsets = std::move(L.offsets);
     return ix;
 }
 

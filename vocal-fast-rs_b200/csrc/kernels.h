@@ -61,6 +61,10 @@ void launch_frontend(const float *hubert, const float *raw, const float *f0, con
 void launch_engine_frontend(const float *blended, const float *raw, const float *hz, float protect, int frames,
                             int hz_frames, int width, float *out, int32_t *coarse, cudaStream_t stream);
 
+// Index of the first non-finite value of x[0 .. count) (all ones when none);
+// synchronous, on the legacy stream of the current device (ingest_kernels.cu).
+unsigned long long first_nonfinite(const float *x, unsigned long long count, int sm_count);
+
 // Sharded helpers (shard_kernels.cu).
 void launch_merge_topk(const float *dist, const int64_t *labels, int shards, long long frames, float *out_dist,
                        int64_t *out_labels, cudaStream_t stream);

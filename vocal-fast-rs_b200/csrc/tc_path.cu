@@ -2002,10 +2002,12 @@ void build_tc(VfrIndex *ix) {
 }
 
 void release_tc(VfrIndex *ix) noexcept {
-    if (ix->vectors_h) cudaFree(ix->vectors_h);
-    if (ix->row_norms) cudaFree(ix->row_norms);
-    if (ix->centroids_h) cudaFree(ix->centroids_h);
-    if (ix->centroid_norms) cudaFree(ix->centroid_norms);
+    if (!ix->shared) {
+        if (ix->vectors_h) cudaFree(ix->vectors_h);
+        if (ix->row_norms) cudaFree(ix->row_norms);
+        if (ix->centroids_h) cudaFree(ix->centroids_h);
+        if (ix->centroid_norms) cudaFree(ix->centroid_norms);
+    }
     ix->centroids_h = nullptr;
     ix->centroid_norms = nullptr;
     if (ix->ws.base) cudaFree(ix->ws.base);

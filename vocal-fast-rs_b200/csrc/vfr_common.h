@@ -9,6 +9,7 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -57,6 +58,35 @@ struct HostIndex {
     std::vector<int32_t> ids;
 };
 
+// Where a FAISS image keeps each part of the index (byte positions in the
+// image); centroids are copied (and checked) during the walk.
+struct FaissLayout {
+    static constexpr size_t kImplicitIds = ~size_t(0);  // IxF2: ids are 0..n-1
+    static constexpr size_t kNoFault = ~size_t(0);
+    struct List {
+        size_t vec_pos;  // size * d little-endian f32
+        size_t id_pos;   // size little-endian u64 ids (kImplicitIds for IxF2)
+        uint64_t size;
+    };
+    int32_t d = 0;
+    int32_t nlist = 0;
+    int32_t nprobe = 0;
+    int64_t n = 0;
+    std::vector<float> centroids;
+    std::vector<int32_t> offsets;
+    std::vector<List> lists;  // file order = row order
+    bool trailing = false;    // IxF2 bytes after the rows
+    // byte position in the image of row element `element` (row-major, list order)
+    size_t row_position(uint64_t element) const;
+};
+
+FaissLayout faiss_layout(const uint8_t *bytes, size_t length);
+// ids in row order; returns the position of the first duplicate or
+// out-of-range id (kNoFault when they form a permutation of 0..n-1).
+size_t scan_ids(const FaissLayout &layout, const uint8_t *bytes, std::vector<int32_t> &ids);
+// Throws the payload error that comes first in the file, then the IxF2
+// trailing-data error; returns when there is none.
+void raise_first_fault(const FaissLayout &layout, size_t nonfinite_pos, size_t bad_id_pos);
 HostIndex parse_faiss(const uint8_t *bytes, size_t length);
 bool find_vfrm_faiss(const uint8_t *image, size_t length, size_t *offset, size_t *size);
 
@@ -81,6 +111,10 @@ struct Workspace {
 };
 
 }  // namespace vfr
+
+namespace vfr {
+struct SharedRows;
+}
 
 // Device-resident index.  Field order is private to this library.
 struct VfrIndex {
@@ -124,7 +158,20 @@ struct VfrIndex {
     bool have_tc = false;
     vfr::Workspace ws;
     vfr::Profiler prof;
+    // Set when the device arrays above (rows, ids, lists, shadow, norms) are
+    // shared with other handles loaded from the same content; they are then
+    // freed with the last handle, not by this one.
+    std::shared_ptr<vfr::SharedRows> shared;
 };
+
+namespace vfr {
+// Device arrays and derived layout of an index loaded with
+// VFR_SHARE_STORAGE; `proto` holds no workspace, counters or events.
+struct SharedRows {
+    VfrIndex proto;
+    ~SharedRows();
+};
+}  // namespace vfr
 
 struct VfrHostIndex {
     vfr::HostIndex h;

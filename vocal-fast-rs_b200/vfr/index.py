@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import ctypes
 import json
+import os
 
 import numpy as np
 
@@ -38,10 +39,17 @@ class RetrievalIndex:
         self._d, self._nlist, self._nprobe, self._n = d.value, nl.value, npb.value, n.value
 
     @classmethod
-    def from_faiss(cls, data: bytes) -> "RetrievalIndex":
+    def from_faiss(cls, data) -> "RetrievalIndex":
+        """bytes, or any contiguous buffer (numpy uint8, memoryview)."""
         L = load_library()
         out = ctypes.c_void_p()
-        call(L.vfr_index_parse_faiss, data, len(data), ctypes.byref(out))
+        if not isinstance(data, bytes):
+            view = np.ascontiguousarray(np.frombuffer(data, np.uint8) if not isinstance(data, np.ndarray)
+                                        else data.reshape(-1).view(np.uint8))
+            data = ctypes.cast(view.ctypes.data, ctypes.c_char_p) if view.size else b""
+            call(L.vfr_index_parse_faiss, data, view.size, ctypes.byref(out))
+        else:
+            call(L.vfr_index_parse_faiss, data, len(data), ctypes.byref(out))
         return cls(out.value)
 
     @classmethod
@@ -115,6 +123,37 @@ class GpuRetrievalIndex:
         out = ctypes.c_void_p()
         call(L.vfr_index_upload, index._h, ctypes.byref(out))
         return cls(out.value, index.dimensions(), index.nlist(), index.nprobe(), len(index))
+
+    @classmethod
+    def load(cls, source, feature_dims: int = 0, engine: int = _l.ENGINE_AUTO, candidates: int = 0,
+             label_base: int = 0, max_frames: int = 0, share: bool = False) -> "GpuRetrievalIndex | None":
+        """Device ingest of a FAISS index or a VFRM package (`vfr_index_load`,
+        `vfr_index_load_vfrm`, `vfr_index_load_file`): `source` is a path or
+        a bytes-like image (bytes, bytearray, memoryview, numpy uint8).  The
+        rows go from the image to the device without a host copy; errors are
+        the parser's (`RetrievalIndex.from_faiss`).  None when a VFRM package
+        has no retrieval index.  `share=True` shares the device arrays with
+        other handles loaded from the same bytes on this device."""
+        L = load_library()
+        out = ctypes.c_void_p()
+        opt = _l.Options(ctypes.sizeof(_l.Options), engine, candidates, _l.SHARE_STORAGE if share else 0,
+                         label_base, max_frames)
+        if isinstance(source, (str, os.PathLike)):
+            call(L.vfr_index_load_file, os.fsencode(source), int(feature_dims), ctypes.byref(opt), ctypes.byref(out))
+        else:
+            view = np.frombuffer(source, dtype=np.uint8) if not isinstance(source, np.ndarray) else source
+            view = np.ascontiguousarray(view.reshape(-1).view(np.uint8))
+            ptr = view.ctypes.data if view.size else None
+            if view.size >= 4 and bytes(view[:4]) == b"VFRM":
+                call(L.vfr_index_load_vfrm, ptr, view.size, int(feature_dims), ctypes.byref(opt), ctypes.byref(out))
+            else:
+                call(L.vfr_index_load, ptr, view.size, ctypes.byref(opt), ctypes.byref(out))
+        if not out.value:
+            return None
+        g = cls(out.value, 0, 0, 0, 0)
+        diag = g.diagnostics()
+        g.d, g.nlist, g.nprobe, g.n = diag["dimensions"], diag["nlist"], diag["nprobe"], diag["vectors"]
+        return g
 
     @classmethod
     def from_arrays(cls, centroids, offsets, vectors, ids, nprobe: int, engine: int = _l.ENGINE_AUTO,

@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(PKG, "libvfr_retrieval.so")
 HEADER = os.path.join(PKG, "..", "include", "vfr_retrieval.h")
 
 ENGINE_AUTO, ENGINE_EXACT, ENGINE_TENSOR = 0, 1, 2
+SHARE_STORAGE = 1  # VfrOptions.flags: VFR_SHARE_STORAGE
 
 _lib = None
 
@@ -34,7 +35,7 @@ class Options(ctypes.Structure):
         ("struct_size", ctypes.c_int32),
         ("engine", ctypes.c_int32),
         ("candidates", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
         ("label_base", ctypes.c_int64),
         ("max_frames", ctypes.c_int64),
     ]
@@ -79,6 +80,9 @@ def load_library(path: str | None = None):
         "vfr_index_vectors": ([vp], vp),
         "vfr_index_ids": ([vp], vp),
         "vfr_index_upload": ([vp, P(vp), err], ctypes.c_int),
+        "vfr_index_load": ([vp, sz, P(Options), P(vp), err], ctypes.c_int),
+        "vfr_index_load_vfrm": ([vp, sz, i32, P(Options), P(vp), err], ctypes.c_int),
+        "vfr_index_load_file": ([ctypes.c_char_p, i32, P(Options), P(vp), err], ctypes.c_int),
         "vfr_retrieval_create": ([i32, i32, i32, sz, vp, sz, vp, sz, vp, sz, vp, sz, P(Options), P(vp), err],
                                  ctypes.c_int),
         "vfr_retrieval_reserve": ([vp, sz, err], ctypes.c_int),
