@@ -56,6 +56,7 @@ def args_parse():
     ap.add_argument("--no-streaming", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ingest", action="store_true", help="skip the c5 index-ingest timing")
+    ap.add_argument("--no-training", action="store_true", help="skip the IVF training timing")
     return ap.parse_args()
 
 
@@ -386,6 +387,53 @@ def ingest(device):
             "load_shared_first_s": t_first, "load_shared_hit_s": t_hit, "shared_handles": shared}
 
 
+def training(device, cpu_threads: int):
+    """IVF training, the reference's offline FAISS step (IndexIVFFlat train +
+    add), on c5's rows: the first 200,000 into 256 lists and all 4,000,000
+    into 4,096 lists; vfr_kmeans (10 iterations on at most 256 sampled rows
+    per list) then vfr_ivf_build (every row assigned and gathered into its
+    list).  Wall-clock seconds with the device synchronised.  The CPU
+    restatement (oracle) runs one k-means iteration of the 256-list case on
+    the host threads for scale."""
+    import time
+
+    import torch
+
+    from vfr import synth
+    from vfr.training import build_ivf_index, kmeans
+
+    arrays, _ = synth.make_torch("c5", device, q=1)
+    x = arrays["vectors"]
+    del arrays
+    out = {"workload": "c5 rows (Gaussian mixture, 768-d): 200k rows -> 256 lists, 4M rows -> 4096 lists; "
+                       "10 k-means iterations, <= 256 sampled rows per list, then every row assigned"}
+    for name, rows, lists in (("lists256_rows200k", 200_000, 256), ("lists4096_rows4m", x.shape[0], 4096)):
+        xs = x[:rows].contiguous()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        c, obj = kmeans(xs, lists, niter=10, max_points_per_centroid=256, seed=1234)
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        g = build_ivf_index(xs, c, nprobe=8)
+        torch.cuda.synchronize()
+        t2 = time.perf_counter()
+        g.close()
+        out[name] = {"kmeans_s": t1 - t0, "build_s": t2 - t1, "total_s": t2 - t0,
+                     "objective_first": float(obj[0]), "objective_last": float(obj[-1])}
+        del xs, c
+    if cpu_threads > 0:
+        from oracle import oracle as orc
+
+        xs = x[:200_000].cpu().numpy()
+        t0 = time.perf_counter()
+        orc.kmeans(xs, 256, niter=1, max_points_per_centroid=256, seed=1234, threads=cpu_threads)
+        out["cpu_baseline_one_iteration_lists256_s"] = time.perf_counter() - t0
+        out["cpu_threads"] = cpu_threads
+    del x
+    torch.cuda.empty_cache()
+    return out
+
+
 def ivf(device):
     """c3: IVF-Flat 200k x 768, nlist 256 (20 seeded k-means iterations), 30k
     frames, nprobe 1 and 8; frames/s of the blend (CUDA events)."""
@@ -581,6 +629,8 @@ def main():
         extra["ivf"] = ivf(device)
         if not a.no_ingest:
             extra["ingest"] = ingest(device)
+        if not a.no_training:
+            extra["training"] = training(device, 0 if a.no_cpu_baseline else (os.cpu_count() or 1))
     cpu = None
     if rank == 0 and world == 1 and full_host is not None:
         cpu = cpu_baseline(full_host, queries.cpu().numpy(), w.ratio, n)

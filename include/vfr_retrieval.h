@@ -183,6 +183,33 @@ VFR_API int vfr_index_load_vfrm(const uint8_t *image, size_t length, int32_t fea
 VFR_API int vfr_index_load_file(const char *path, int32_t feature_dims, const VfrOptions *options, VfrIndex **out,
                                 char **error);
 
+/* IVF training (the offline FAISS step the reference runs with
+ * IndexIVFFlat::train/add; recipe in crates/vocal-directml/tests/fixtures/
+ * README.md and scripts/benchmark-retrieval.py:56-65), on the device.
+ * vfr_kmeans: k centroids [k][d] (device) from x [n][d] (device, finite):
+ * at most k * max_points_per_centroid rows sampled (0 = all), k of them as the
+ * first centroids, niter Lloyd iterations (exact nearest centroid; means in
+ * 64-bit fixed point) with empty clusters re-seeded by splitting; objective
+ * (host [niter], may be NULL) receives each iteration's sum of distances.
+ * Deterministic for a given seed.  Synchronous. */
+VFR_API int vfr_kmeans(const float *x, int64_t n, int32_t d, int32_t k, int32_t niter, int32_t max_points_per_centroid,
+                       uint64_t seed, float *centroids, double *objective, VfrStream *stream, char **error);
+/* lists[r] (device i32 [n]) = the nearest of the k centroids to row r, ties to
+ * the lower one; distances (device f32 [n], may be NULL) its squared L2. */
+VFR_API int vfr_ivf_assign(const float *centroids, int32_t k, const float *x, int64_t n, int32_t d, int32_t *lists,
+                           float *distances, VfrStream *stream, char **error);
+/* IndexIVFFlat::add into a device index directly: every row of x (device) in
+ * the list of its nearest centroid (device), lists in input order, labels the
+ * input row numbers. */
+VFR_API int vfr_ivf_build(const float *centroids, int32_t k, const float *x, int64_t n, int32_t d, int32_t nprobe,
+                          const VfrOptions *options, VfrIndex **out, char **error);
+/* FAISS IndexIVFFlat bytes (IwFl, Flat-L2 quantizer, ArrayInvertedLists) from
+ * host arrays: *size receives the byte count; out is written when capacity
+ * suffices (pass NULL to query the size). */
+VFR_API int vfr_ivf_write(const float *centroids, int32_t k, const float *x, int64_t n, int32_t d,
+                          const int32_t *lists, int32_t nprobe, uint8_t *out, size_t capacity, size_t *size,
+                          char **error);
+
 /* Sizes the per-index workspace for up to max_frames frames per call, so that
  * later calls allocate nothing (required before CUDA graph capture). */
 VFR_API int vfr_retrieval_reserve(VfrIndex *index, size_t max_frames, char **error);

@@ -75,6 +75,12 @@ def lib():
                                           ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
                                           ctypes.c_void_p]
         L.orc_engine_frontend.restype = ctypes.c_int64
+        L.orc_kmeans.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                 ctypes.c_int32, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        L.orc_kmeans.restype = ctypes.c_int
+        L.orc_ivf_assign.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int64,
+                                     ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        L.orc_ivf_assign.restype = None
         L.orc_view.argtypes = [P(_Index), ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         _lib = L
@@ -256,3 +262,28 @@ def engine_frontend(blended: np.ndarray, raw, hz, protect: float):
                                     None if coarse is None else _ptr(coarse))
     assert got == (0 if coarse is None else coarse.shape[0])
     return out, coarse
+
+
+def kmeans(x: np.ndarray, k: int, niter: int = 10, max_points_per_centroid: int = 256, seed: int = 1234,
+           threads: int = 1):
+    """Restated vfr_kmeans: (centroids [k][d] f32, objective [niter] f64)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, d = x.shape
+    c = np.empty((k, d), np.float32)
+    obj = np.empty(max(niter, 1), np.float64)
+    rc = lib().orc_kmeans(_ptr(x), n, d, k, niter, max_points_per_centroid, ctypes.c_uint64(seed), _ptr(c), _ptr(obj),
+                          threads)
+    if rc != 0:
+        raise ValueError("invalid k-means arguments")
+    return c, obj[:niter]
+
+
+def ivf_assign(centroids: np.ndarray, x: np.ndarray, threads: int = 1):
+    """Restated vfr_ivf_assign: (lists [n] i32, squared distances [n] f32)."""
+    c = np.ascontiguousarray(centroids, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, d = x.shape
+    lists = np.empty(n, np.int32)
+    dist = np.empty(n, np.float32)
+    lib().orc_ivf_assign(_ptr(c), c.shape[0], _ptr(x), n, d, _ptr(lists), _ptr(dist), threads)
+    return lists, dist

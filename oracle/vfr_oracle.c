@@ -22,6 +22,14 @@
  *                     TensorRT graph in the reference)
  *   - engine frontend: crates/vocal-engine/src/pipeline.rs:75-96 (linear 2x),
  *                     312-333 (protection), 625-633 (f0_to_coarse)
+ *   - IVF training:   the library's deterministic trainer (vfr_kmeans,
+ *                     vfr_ivf_assign).  The reference trains offline with
+ *                     FAISS IndexIVFFlat::train/add (recipe in
+ *                     crates/vocal-directml/tests/fixtures/README.md,
+ *                     scripts/benchmark-retrieval.py:56-65; FAISS is not
+ *                     vendored); the algorithm is FAISS's Clustering with a
+ *                     SplitMix64 generator, exact nearest-centroid assignment
+ *                     under avx2_l2's order and 64-bit fixed-point means.
  *
  * Arithmetic order is kept exactly: AVX2 8-lane direct-difference squared L2
  * with separate multiply and add, the eight lanes folded left to right, then
@@ -741,4 +749,183 @@ int64_t orc_engine_frontend(const float *blended, const float *raw, const float 
         if (hz != NULL && t < pitch_frames) coarse[t] = orc_f0_to_coarse(hz[t], mel_min, mel_max);
     }
     return pitch_frames;
+}
+
+/* ---------------------------------------------------------------- IVF trainer */
+
+static uint64_t orc_splitmix(uint64_t *state) {
+    uint64_t z = (*state += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static float orc_uniform(uint64_t *state) { return (float)(orc_splitmix(state) >> 40) * 0x1p-24f; }
+
+/* the first m entries of a Fisher-Yates shuffle of 0..n-1 */
+static int orc_shuffled_prefix(int64_t n, int64_t m, uint64_t seed, int64_t *out) {
+    int64_t *p = (int64_t *)malloc((size_t)n * sizeof(int64_t));
+    if (!p) return -1;
+    for (int64_t i = 0; i < n; ++i) p[i] = i;
+    uint64_t st = seed;
+    for (int64_t i = 0; i < m; ++i) {
+        const int64_t j = i + (int64_t)(orc_splitmix(&st) % (uint64_t)(n - i));
+        const int64_t t = p[i];
+        p[i] = p[j];
+        p[j] = t;
+    }
+    memcpy(out, p, (size_t)m * sizeof(int64_t));
+    free(p);
+    return 0;
+}
+
+/* nearest centroid under avx2_l2's order, ties to the lower centroid */
+static int32_t orc_nearest(const float *c, int32_t k, const float *row, int32_t d, float *dist) {
+    int32_t best = 0;
+    float bd = orc_l2_lanes(row, c, (size_t)d);
+    for (int32_t j = 1; j < k; ++j) {
+        const float v = orc_l2_lanes(row, c + (size_t)j * d, (size_t)d);
+        if (v < bd) {
+            bd = v;
+            best = j;
+        }
+    }
+    *dist = bd;
+    return best;
+}
+
+typedef struct {
+    const float *c, *x;
+    int32_t k, d;
+    int64_t lo, hi;
+    int32_t *lists;
+    float *dist;
+} assign_job;
+
+static void *run_assign(void *p) {
+    assign_job *j = (assign_job *)p;
+    for (int64_t r = j->lo; r < j->hi; ++r) j->lists[r] = orc_nearest(j->c, j->k, j->x + r * j->d, j->d, &j->dist[r]);
+    return NULL;
+}
+
+void orc_ivf_assign(const float *centroids, int32_t k, const float *x, int64_t n, int32_t d, int32_t *lists,
+                    float *dist, int threads) {
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    assign_job jobs[256];
+    pthread_t tid[256];
+    for (int t = 0; t < threads; ++t) {
+        jobs[t] = (assign_job){centroids, x, k, d, n * t / threads, n * (t + 1) / threads, lists, dist};
+        if (t > 0) pthread_create(&tid[t], NULL, run_assign, &jobs[t]);
+    }
+    run_assign(&jobs[0]);
+    for (int t = 1; t < threads; ++t) pthread_join(tid[t], NULL);
+}
+
+/* Restates vfr_kmeans (see the header comment); returns 0, or -1 on bad
+ * arguments / allocation failure. */
+int orc_kmeans(const float *x, int64_t n, int32_t d, int32_t k, int32_t niter, int32_t max_ppc, uint64_t seed,
+               float *centroids, double *objective, int threads) {
+    if (!x || !centroids || d <= 0 || k <= 0 || n < k || niter < 0 || max_ppc < 0) return -1;
+    int64_t m = n;
+    if (max_ppc > 0 && n > (int64_t)k * max_ppc) m = (int64_t)k * max_ppc;
+    float *train = (float *)x;
+    float *sample = NULL;
+    int64_t *rows = (int64_t *)malloc((size_t)(m > k ? m : k) * sizeof(int64_t));
+    int32_t *lists = (int32_t *)malloc((size_t)m * sizeof(int32_t));
+    float *dist = (float *)malloc((size_t)m * sizeof(float));
+    int64_t *sums = (int64_t *)malloc((size_t)k * d * sizeof(int64_t));
+    long long *counts = (long long *)malloc((size_t)k * sizeof(long long));
+    double *w = (double *)malloc((size_t)k * sizeof(double));
+    if (!rows || !lists || !dist || !sums || !counts || !w) goto fail;
+    if (m < n) {
+        sample = (float *)malloc((size_t)m * d * sizeof(float));
+        if (!sample || orc_shuffled_prefix(n, m, seed, rows)) goto fail;
+        for (int64_t i = 0; i < m; ++i) memcpy(sample + i * d, x + rows[i] * d, (size_t)d * sizeof(float));
+        train = sample;
+    }
+    if (orc_shuffled_prefix(m, k, seed + 1, rows)) goto fail;
+    for (int32_t j = 0; j < k; ++j) memcpy(centroids + (size_t)j * d, train + rows[j] * d, (size_t)d * sizeof(float));
+    float maxabs = 0.0f;
+    for (int64_t i = 0; i < m * d; ++i) {
+        const float a = fabsf(train[i]);
+        if (a > maxabs) maxabs = a;
+    }
+    int e = 0;
+    frexpf(maxabs, &e);
+    int bits = 0;
+    while (((int64_t)1 << bits) < m) ++bits;
+    const int sexp = 62 - bits - e;
+    const double scale = ldexp(1.0, sexp), inv = ldexp(1.0, -sexp);
+    uint64_t split = seed + 2;
+    for (int32_t it = 0; it < niter; ++it) {
+        orc_ivf_assign(centroids, k, train, m, d, lists, dist, threads);
+        double obj = 0.0;
+        for (int64_t r = 0; r < m; ++r) obj += dist[r];
+        if (objective) objective[it] = obj;
+        memset(sums, 0, (size_t)k * d * sizeof(int64_t));
+        memset(counts, 0, (size_t)k * sizeof(long long));
+        for (int64_t r = 0; r < m; ++r) {
+            const int32_t l = lists[r];
+            ++counts[l];
+            for (int32_t c = 0; c < d; ++c) sums[(size_t)l * d + c] += llrint((double)train[r * d + c] * scale);
+        }
+        int empty = 0;
+        for (int32_t j = 0; j < k; ++j) {
+            empty |= counts[j] == 0;
+            for (int32_t c = 0; c < d; ++c)
+                centroids[(size_t)j * d + c] =
+                    counts[j] > 0 ? (float)(((double)sums[(size_t)j * d + c] / (double)counts[j]) * inv) : 0.0f;
+        }
+        if (!empty) continue;
+        for (int32_t j = 0; j < k; ++j) w[j] = (double)counts[j];
+        for (int32_t ci = 0; ci < k; ++ci) {
+            if (w[ci] != 0.0) continue;
+            int32_t cj = 0;
+            int found = 0;
+            const long long trials = 64LL * k + 1024;
+            for (long long t = 0; t < trials; ++t, cj = (cj + 1) % k) {
+                const double p = (w[cj] - 1.0) / (double)(m - k);
+                if ((double)orc_uniform(&split) < p) {
+                    found = 1;
+                    break;
+                }
+            }
+            if (!found) {
+                cj = 0;
+                for (int32_t j = 1; j < k; ++j)
+                    if (w[j] > w[cj]) cj = j;
+            }
+            float *a = centroids + (size_t)ci * d, *b = centroids + (size_t)cj * d;
+            memcpy(a, b, (size_t)d * sizeof(float));
+            for (int32_t j = 0; j < d; ++j) {
+                if (j % 2 == 0) {
+                    a[j] *= 1.0f + 1.0f / 1024.0f;
+                    b[j] *= 1.0f - 1.0f / 1024.0f;
+                } else {
+                    a[j] *= 1.0f - 1.0f / 1024.0f;
+                    b[j] *= 1.0f + 1.0f / 1024.0f;
+                }
+            }
+            w[ci] = w[cj] / 2.0;
+            w[cj] -= w[ci];
+        }
+    }
+    free(sample);
+    free(rows);
+    free(lists);
+    free(dist);
+    free(sums);
+    free(counts);
+    free(w);
+    return 0;
+fail:
+    free(sample);
+    free(rows);
+    free(lists);
+    free(dist);
+    free(sums);
+    free(counts);
+    free(w);
+    return -1;
 }

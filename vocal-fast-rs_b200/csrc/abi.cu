@@ -12,6 +12,7 @@
 #include <mutex>
 #include <string>
 
+#include "index_build.h"
 #include "ingest.h"
 #include "kernels.h"
 #include "tc_path.h"
@@ -39,25 +40,6 @@ SharedRows::~SharedRows() {
         if (p) cudaFree(p);
     cudaSetDevice(previous);
 }
-
-namespace {
-
-// Makes the index's device current for the duration of a call.
-class DeviceGuard {
-public:
-    explicit DeviceGuard(int device) {
-        cuda_check(cudaGetDevice(&previous_));
-        if (previous_ != device) cuda_check(cudaSetDevice(device));
-        device_ = device;
-    }
-    ~DeviceGuard() {
-        if (previous_ != device_) cudaSetDevice(previous_);
-    }
-
-private:
-    int previous_ = 0;
-    int device_ = 0;
-};
 
 void free_index(VfrIndex *ix) noexcept {
     if (!ix) return;
@@ -333,6 +315,20 @@ ExactArgs exact_args(VfrIndex *ix, const float *queries, float *out, const float
     return a;
 }
 
+void search_rows(VfrIndex *ix, const float *queries, size_t frames, int k, float *dist, int64_t *labels,
+                 cudaStream_t s) {
+    if (ix->have_tc && use_tc(ix, frames)) {
+        run_tc(ix, queries, nullptr, nullptr, kModeSearch, k, dist, labels, frames, s);
+    } else {
+        ExactArgs a = exact_args(ix, queries, nullptr, nullptr, kModeSearch);
+        a.k = k;
+        a.dist_out = dist;
+        a.label_out = labels;
+        launch_exact(a, static_cast<long long>(frames), s);
+    }
+    cuda_check(cudaGetLastError());
+}
+
 void blend_impl(VfrIndex *ix, const float *queries, float *out, size_t frames, int32_t width, const float *rate,
                 VfrStream *stream, float *raw = nullptr) {
     require(ix && queries && out && frames > 0 && rate, "invalid FAISS GPU blend arguments");
@@ -358,7 +354,6 @@ void blend_impl(VfrIndex *ix, const float *queries, float *out, size_t frames, i
     cuda_check(cudaGetLastError());
 }
 
-}  // namespace
 }  // namespace vfr
 
 using vfr::guarded;
@@ -467,16 +462,7 @@ extern "C" int vfr_retrieval_search(VfrIndex *index, const float *queries, size_
         require(k >= 1 && k <= vfr::kTopK, "search k must be in 1..8");
         cudaStream_t s = vfr::stream_of(stream);
         vfr::DeviceGuard guard(index->device);
-        if (index->have_tc && vfr::use_tc(index, frames)) {
-            vfr::run_tc(index, queries, nullptr, nullptr, vfr::kModeSearch, k, distances, labels, frames, s);
-        } else {
-            vfr::ExactArgs a = vfr::exact_args(index, queries, nullptr, nullptr, vfr::kModeSearch);
-            a.k = k;
-            a.dist_out = distances;
-            a.label_out = labels;
-            vfr::launch_exact(a, static_cast<long long>(frames), s);
-        }
-        vfr::cuda_check(cudaGetLastError());
+        vfr::search_rows(index, queries, frames, k, distances, labels, s);
     });
 }
 
@@ -655,6 +641,43 @@ extern "C" int vfr_index_load_file(const char *path, int32_t feature_dims, const
         } else {
             *out = vfr::load_index(file.data, file.size, feature_dims, options);
         }
+    });
+}
+
+// ---- IVF training --------------------------------------------------------
+
+extern "C" int vfr_kmeans(const float *x, int64_t n, int32_t d, int32_t k, int32_t niter,
+                          int32_t max_points_per_centroid, uint64_t seed, float *centroids, double *objective,
+                          VfrStream *stream, char **error) {
+    return guarded(error, [&] {
+        cudaStream_t s = vfr::stream_of(stream);
+        vfr::kmeans(x, n, d, k, niter, max_points_per_centroid, seed, centroids, objective, s);
+    });
+}
+
+extern "C" int vfr_ivf_assign(const float *centroids, int32_t k, const float *x, int64_t n, int32_t d,
+                              int32_t *lists, float *distances, VfrStream *stream, char **error) {
+    return guarded(error, [&] {
+        cudaStream_t s = vfr::stream_of(stream);
+        vfr::ivf_assign(centroids, k, x, n, d, lists, distances, s);
+    });
+}
+
+extern "C" int vfr_ivf_build(const float *centroids, int32_t k, const float *x, int64_t n, int32_t d, int32_t nprobe,
+                             const VfrOptions *options, VfrIndex **out, char **error) {
+    return guarded(error, [&] {
+        require(out, "null FAISS GPU index output");
+        *out = nullptr;
+        *out = vfr::ivf_build(centroids, k, x, n, d, nprobe, options);
+    });
+}
+
+extern "C" int vfr_ivf_write(const float *centroids, int32_t k, const float *x, int64_t n, int32_t d,
+                             const int32_t *lists, int32_t nprobe, uint8_t *out, size_t capacity, size_t *size,
+                             char **error) {
+    return guarded(error, [&] {
+        require(size, "null size output");
+        *size = vfr::ivf_write(centroids, k, x, n, d, lists, nprobe, out, capacity);
     });
 }
 

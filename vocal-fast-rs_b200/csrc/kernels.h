@@ -65,6 +65,17 @@ void launch_engine_frontend(const float *blended, const float *raw, const float 
 // synchronous, on the legacy stream of the current device (ingest_kernels.cu).
 unsigned long long first_nonfinite(const float *x, unsigned long long count, int sm_count);
 
+// IVF trainer (training_kernels.cu): out[r] = x[rows[r]]; fixed-point
+// centroid sums (sums[labels[r]][c] += rint(x[r][c] * scale)); means
+// (sum / count * inv_scale, 0 for empty clusters); int64 -> int32 labels.
+void launch_gather_rows(const float *x, const int64_t *rows, long long count, int d, float *out,
+                        cudaStream_t stream);
+void launch_fixed_sums(const float *x, const int64_t *labels, long long rows, int d, double scale,
+                       unsigned long long *sums, cudaStream_t stream);
+void launch_means(const unsigned long long *sums, const long long *counts, int k, int d, double inv_scale,
+                  float *centroids, cudaStream_t stream);
+void launch_narrow_labels(const int64_t *wide, long long n, int32_t *out, cudaStream_t stream);
+
 // Sharded helpers (shard_kernels.cu).
 void launch_merge_topk(const float *dist, const int64_t *labels, int shards, long long frames, float *out_dist,
                        int64_t *out_labels, cudaStream_t stream);

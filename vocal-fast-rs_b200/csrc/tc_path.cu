@@ -1909,6 +1909,9 @@ void build_shadow(const float *x, int64_t rows, int64_t rows_pad, int d, int d_p
     out[2] = out[2] * 1.0001f + 1e-30f;
 }
 
+
+}  // namespace
+
 float max_abs(const float *x, size_t count) {
     unsigned int *m = nullptr;
     cuda_check(cudaMalloc(reinterpret_cast<void **>(&m), sizeof(unsigned int)));
@@ -1923,8 +1926,6 @@ float max_abs(const float *x, size_t count) {
     std::memcpy(&v, &bits, 4);
     return v;
 }
-
-}  // namespace
 
 void build_tc(VfrIndex *ix) {
     const bool ivf = ix->nlist > 1;
