@@ -1045,7 +1045,8 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreads ? 3 : 1) merge_kernel(
     const float inf = __int_as_float(0x7f800000);
     const int real_slots = a.lists * a.keep;
 
-    launch_dependents();
+    // no early trigger: the exact kernel behind launches as these CTAs exit,
+    // so its CTAs never hold SM slots that merge CTAs still need
     if (tid == 0) {
         tc::mbar_init(&gather_bar, 1);
         tc::mbar_init(&stage_bar, 1);
@@ -1368,14 +1369,12 @@ void launch_merge(VfrIndex *ix, MergeArgs &ma, size_t frames, cudaStream_t strea
     }
     const size_t smem = merge_smem(ma.sort_size, ma.thr_stride, ix->d, ma.stage_rows).total;
     require(smem <= static_cast<size_t>(ix->merge_smem_max), "candidate lists exceed the merge's shared memory");
-    // A plain launch: with programmatic launch the merge CTAs, resident early
-    // and parked in their dependency wait through the candidate stream, ran
-    // their phases slower afterwards (a c4 block took 64 us instead of 58).
     if (ma.stage_rows > 0)
-        merge_kernel<kMergeThreadsMax><<<static_cast<unsigned>(frames), kMergeThreadsMax, smem, stream>>>(ma);
+        cuda_check(launch_pdl(merge_kernel<kMergeThreadsMax>, dim3(static_cast<unsigned>(frames)),
+                              dim3(kMergeThreadsMax), smem, stream, ma));
     else
-        merge_kernel<kMergeThreads><<<static_cast<unsigned>(frames), kMergeThreads, smem, stream>>>(ma);
-    cuda_check(cudaGetLastError());
+        cuda_check(launch_pdl(merge_kernel<kMergeThreads>, dim3(static_cast<unsigned>(frames)), dim3(kMergeThreads),
+                              smem, stream, ma));
 }
 
 // Launches the flat candidate kernel behind prep_queries_kernel (it starts
