@@ -1,0 +1,70 @@
+"""Re-runs of uncertified frames (the exact kernel behind the tensor-core
+engine).  Frames whose candidate set cannot be certified -- here more than
+kRerankMax rows at exactly the same distance -- are re-run exactly; when at
+most 64 frames fall back, each frame's probed rows are split across many
+CTAs and the slices' top-8 lists merged (exact_split), otherwise one CTA
+scans each frame.  Both must give the reference's results bit for bit:
+search (distances, scan-order ties, labels) and blend against the oracle
+(crates/vocal-cpu/src/retrieval.rs:27-83), flat and IVF.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def tie_heavy(n, d, nlist, seed, copies=150, clusters=3):
+    """Random rows plus `clusters` rows repeated `copies` times each, so a
+    query next to one of them has >kRerankMax exactly tied neighbours."""
+    from vfr import synth
+
+    rng = np.random.default_rng(seed)
+    rows = rng.standard_normal((n, d), dtype=np.float32)
+    tied = rng.standard_normal((clusters, d), dtype=np.float32) * 3
+    pos = rng.choice(n, clusters * copies, replace=False)
+    rows[pos] = np.repeat(tied, copies, axis=0)
+    if nlist == 1:
+        ix = synth.flat_arrays(rows)
+    else:
+        centroids = rows[rng.choice(n, nlist, replace=False)].copy()
+        ix = synth.ivf_arrays(rows, centroids, 1)
+    return ix, tied, rng
+
+
+@pytest.mark.parametrize("nlist,nprobe", [(1, 1), (16, 4), (16, 8), (16, 16)])
+@pytest.mark.parametrize("frames,tied_frames", [(40, 10), (70, 70), (12, 1)])
+def test_rerun_matches_oracle(cuda, oracle, nlist, nprobe, frames, tied_frames):
+    from vfr import GpuRetrievalIndex, lib
+
+    ix, tied, rng = tie_heavy(60_000, 64, nlist, 100 + nlist + frames)
+    q = rng.standard_normal((frames, 64), dtype=np.float32)
+    sel = rng.choice(frames, tied_frames, replace=False)
+    q[sel] = tied[rng.integers(0, len(tied), tied_frames)] + np.float32(1e-3)
+    g = GpuRetrievalIndex.from_arrays(ix.centroids, ix.offsets, ix.vectors, ix.ids, nprobe, engine=lib.ENGINE_TENSOR)
+    o = oracle.OracleIndex.from_arrays(ix.centroids, ix.offsets, ix.vectors, ix.ids, nprobe)
+    torch = cuda
+    s = torch.cuda.Stream()
+    dq = torch.from_numpy(q).cuda()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        gd, gl = g.search(dq, stream=s)
+    s.synchronize()
+    dist, _, labels, count = o.search(q, threads=8)
+    assert np.array_equal(gl.cpu().numpy(), labels)
+    assert np.array_equal(gd.cpu().numpy().view(np.uint32), dist.view(np.uint32))
+    # nprobe > 8 runs on the exact engine from the start: nothing falls back
+    tensor_path = nprobe <= 8
+    before = g.diagnostics()["fallback_frames"]
+    assert before >= tied_frames if tensor_path else before == 0
+    feats = torch.from_numpy(q.copy()).cuda()
+    rate = torch.tensor([0.75], device="cuda")
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        g.blend(feats, frames, rate, stream=s)
+    s.synchronize()
+    expected, status = o.blend(q, 0.75, threads=8)
+    ok = status == 0
+    assert np.array_equal(feats.cpu().numpy()[ok].view(np.uint32), expected[ok].view(np.uint32))
+    if tensor_path:
+        assert g.diagnostics()["fallback_frames"] - before >= tied_frames
+    g.close()

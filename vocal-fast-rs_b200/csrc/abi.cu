@@ -53,6 +53,8 @@ void free_index(VfrIndex *ix) noexcept {
                         static_cast<void *>(ix->row_of_id)})
             if (p) cudaFree(p);
     if (ix->counters) cudaFree(ix->counters);
+    if (ix->split_keys) cudaFree(ix->split_keys);
+    if (ix->split_done) cudaFree(ix->split_done);
     ix->shared.reset();
     cudaSetDevice(previous);
     delete ix;
@@ -134,6 +136,9 @@ void finish_index(VfrIndex *ix, const VfrOptions &o) {
     cuda_check(cudaMemset(ix->counters, 0, sizeof(DeviceCounters)));
     if (!ix->shared && ix->engine != VFR_ENGINE_EXACT) build_tc(ix);
     if (o.max_frames > 0) reserve_tc(ix, static_cast<size_t>(o.max_frames));
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->split_keys), kSplitKeyBytes), "cudaMalloc re-run scratch");
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->split_done), kSplitFrames * sizeof(int32_t)));
+    cuda_check(cudaMemset(ix->split_done, 0, kSplitFrames * sizeof(int32_t)));
     cuda_check(cudaDeviceSynchronize());
 }
 
@@ -202,6 +207,8 @@ void publish_shared(VfrIndex *ix, const ShareKey &key) {
     auto rows = std::make_shared<SharedRows>();
     rows->proto = *ix;
     rows->proto.counters = nullptr;
+    rows->proto.split_keys = nullptr;
+    rows->proto.split_done = nullptr;
     rows->proto.ws = Workspace{};
     rows->proto.prof.pool.clear();
     rows->proto.prof.marks.clear();

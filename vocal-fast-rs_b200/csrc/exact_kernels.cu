@@ -53,61 +53,47 @@ __device__ __forceinline__ unsigned long long warp_sort_u64(unsigned long long v
     return v;
 }
 
-__device__ void exact_frame(const ExactArgs &a, const long long frame) {
-    extern __shared__ float q[];  // [d] copy of the frame
-    __shared__ unsigned long long probe_keys[kMaxProbe];
-    __shared__ unsigned long long wave_keys[kOctets];
-    __shared__ int probe_list[kMaxProbe];
-    __shared__ uint32_t probe_base[kMaxProbe + 1];
-    __shared__ unsigned long long octet_best[kOctets * 8];
-    __shared__ unsigned long long best[8];
-    __shared__ int32_t best_row[8];
-    __shared__ double weights[8];
-    __shared__ double weight_sum;
+// Shared state of one CTA's frame (declared once in the kernel).
+struct FrameSmem {
+    unsigned long long probe_keys[kMaxProbe];
+    unsigned long long wave_keys[kOctets];
+    int probe_list[kMaxProbe];
+    uint32_t probe_base[kMaxProbe + 1];
+    unsigned long long octet_best[kOctets * 8];
+    unsigned long long best[8];
+    unsigned long long red[kThreads / 32];
+    int32_t best_row[8];
+    double weights[8];
+    double weight_sum;
+    int last;
+};
 
-    const int tid = threadIdx.x;
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
-    const int octet = tid >> 3;
-    const int j = tid & 7;
+// The coarse stage: the first nprobe lists in (distance, list id) order and
+// the scan position where each starts (probe_base[probes] = rows scanned).
+// Returns the number of probed lists.  Called by every thread.
+__device__ int coarse_stage(const ExactArgs &a, const float *q, FrameSmem &sm) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
     const int octet_base = lane & ~7;
     const int d = a.d;
-    const float *src = a.queries + frame * d;
-    float *dst = a.out + frame * d;
-
-    if (tid == 0 && a.frame_list && a.counters) atomicAdd(&a.counters->fallback_frames, 1ull);
-    float ratio = 1.0f;
-    if (a.mode == kModeBlend) {
-        ratio = load_ratio(a.index_rate);
-        if (!(ratio > 0.0f)) {
-            if (dst != src)
-                for (int i = tid; i < d; i += kThreads) dst[i] = src[i];
-            return;
-        }
-    }
-    for (int i = tid; i < d; i += kThreads) q[i] = src[i];
-    __syncthreads();
-
-    // ---- coarse stage ---------------------------------------------------
     int probes = a.nprobe < a.nlist ? a.nprobe : a.nlist;
     if (a.nlist == 1) {
-        if (tid == 0) probe_list[0] = 0;
+        if (tid == 0) sm.probe_list[0] = 0;
         probes = 1;
     } else {
-        if (tid < kMaxProbe) probe_keys[tid] = kEmptyKey;
+        if (tid < kMaxProbe) sm.probe_keys[tid] = kEmptyKey;
         __syncthreads();
         for (int base = 0; base < a.nlist; base += kOctets) {
             const int list = base + octet;
             const int clamped = list < a.nlist ? list : a.nlist - 1;
             float dist = octet_l2(q, a.centroids + static_cast<size_t>(clamped) * d, d, j, octet_base, kFullMask);
-            if (j == 0) wave_keys[octet] = list < a.nlist ? make_key(dist, static_cast<uint32_t>(list)) : kEmptyKey;
+            if (j == 0) sm.wave_keys[octet] = list < a.nlist ? make_key(dist, static_cast<uint32_t>(list)) : kEmptyKey;
             __syncthreads();
             if (warp == 0) {
                 // merge the sorted running top-`probes` with this wave's keys
-                unsigned long long nk = warp_sort_u64(wave_keys[lane], lane);
-                unsigned long long ok = lane < probes ? probe_keys[lane] : kEmptyKey;
+                unsigned long long nk = warp_sort_u64(sm.wave_keys[lane], lane);
+                unsigned long long ok = lane < probes ? sm.probe_keys[lane] : kEmptyKey;
                 int rank_new = 0, rank_old = 0;
-                for (int i = 0; i < probes; ++i) rank_new += probe_keys[i] < nk;
+                for (int i = 0; i < probes; ++i) rank_new += sm.probe_keys[i] < nk;
                 for (int i = 0; i < 32; ++i) {
                     unsigned long long other = __shfl_sync(kFullMask, nk, i);
                     rank_old += other <= ok;
@@ -115,32 +101,42 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame) {
                 __syncwarp();
                 int pn = lane + rank_new;
                 int po = lane + rank_old;
-                if (pn < probes) probe_keys[pn] = nk;
-                if (lane < probes && po < probes) probe_keys[po] = ok;
+                if (pn < probes) sm.probe_keys[pn] = nk;
+                if (lane < probes && po < probes) sm.probe_keys[po] = ok;
             }
             __syncthreads();
         }
-        if (tid < probes) probe_list[tid] = static_cast<int>(key_pos(probe_keys[tid]));
+        if (tid < probes) sm.probe_list[tid] = static_cast<int>(key_pos(sm.probe_keys[tid]));
     }
     __syncthreads();
     if (tid == 0) {
         uint32_t acc = 0;
         for (int r = 0; r < probes; ++r) {
-            probe_base[r] = acc;
-            acc += static_cast<uint32_t>(a.offsets[probe_list[r] + 1] - a.offsets[probe_list[r]]);
+            sm.probe_base[r] = acc;
+            acc += static_cast<uint32_t>(a.offsets[sm.probe_list[r] + 1] - a.offsets[sm.probe_list[r]]);
         }
-        probe_base[probes] = acc;
+        sm.probe_base[probes] = acc;
     }
     __syncthreads();
+    return probes;
+}
 
-    // ---- list scan ------------------------------------------------------
+// Scans scan positions [p0, p1) of the probed lists (list r covers
+// positions probe_base[r] .. probe_base[r + 1], rows in storage order) and
+// leaves the CTA's top 8 keys (distance, scan position) in sm.best.
+__device__ void scan_range(const ExactArgs &a, const float *q, FrameSmem &sm, int probes, uint32_t p0, uint32_t p1) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
+    const int octet_base = lane & ~7;
+    const int d = a.d;
     Top8 top;
     top.init();
     for (int r = 0; r < probes; ++r) {
-        const int list = probe_list[r];
-        const int begin = a.offsets[list];
-        const int end = a.offsets[list + 1];
-        const uint32_t base = probe_base[r];
+        const uint32_t lb = sm.probe_base[r], le = sm.probe_base[r + 1];
+        const uint32_t from = lb > p0 ? lb : p0, to = le < p1 ? le : p1;
+        if (from >= to) continue;
+        const int first = a.offsets[sm.probe_list[r]];
+        const int begin = first + static_cast<int>(from - lb);
+        const int end = first + static_cast<int>(to - lb);
         for (int row0 = begin; row0 < end; row0 += 4 * kOctets) {
             const float *xs[4];
 #pragma unroll
@@ -155,44 +151,56 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame) {
                 const int row = row0 + octet + k * kOctets;
                 // the reference never admits +inf (best starts at +inf, `>=` rejects)
                 if (row < end && dist[k] < __int_as_float(0x7f800000))
-                    top.insert(make_key(dist[k], base + static_cast<uint32_t>(row - begin)));
+                    top.insert(make_key(dist[k], lb + static_cast<uint32_t>(row - first)));
             }
         }
     }
     if (j == 0)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) octet_best[octet * 8 + i] = top.k[i];
+        for (int i = 0; i < 8; ++i) sm.octet_best[octet * 8 + i] = top.k[i];
     __syncthreads();
     if (warp == 0) {
         int head = 0;
         for (int i = 0; i < 8; ++i) {
-            unsigned long long mine = head < 8 ? octet_best[lane * 8 + head] : kEmptyKey;
+            unsigned long long mine = head < 8 ? sm.octet_best[lane * 8 + head] : kEmptyKey;
             unsigned long long m = warp_min_u64(mine);
             if (mine == m && m != kEmptyKey) ++head;
-            if (lane == 0) best[i] = m;
+            if (lane == 0) sm.best[i] = m;
         }
-        if (lane < 8) {
-            unsigned long long key = best[lane];
-            int32_t row = -1;
-            if (key != kEmptyKey) {
-                uint32_t pos = key_pos(key);
-                int r = 0;
-                while (r + 1 < probes && probe_base[r + 1] <= pos) ++r;
-                row = a.offsets[probe_list[r]] + static_cast<int32_t>(pos - probe_base[r]);
-            }
-            best_row[lane] = row;
+    }
+    __syncthreads();
+}
+
+// From the frame's top 8 keys in sm.best: rows, then the search outputs or
+// the blend (retrieval.rs:65-81).
+__device__ void finish_frame(const ExactArgs &a, long long frame, const float *q, float ratio, FrameSmem &sm,
+                             int probes) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int d = a.d;
+    const float *src = a.queries + frame * d;
+    float *dst = a.out + frame * d;
+    if (warp == 0 && lane < 8) {
+        unsigned long long key = sm.best[lane];
+        int32_t row = -1;
+        if (key != kEmptyKey) {
+            uint32_t pos = key_pos(key);
+            int r = 0;
+            while (r + 1 < probes && sm.probe_base[r + 1] <= pos) ++r;
+            row = a.offsets[sm.probe_list[r]] + static_cast<int32_t>(pos - sm.probe_base[r]);
         }
+        sm.best_row[lane] = row;
     }
     __syncthreads();
     int count = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) count += best_row[i] >= 0;
+    for (int i = 0; i < 8; ++i) count += sm.best_row[i] >= 0;
 
     if (a.mode == kModeSearch) {
         if (tid < a.k) {
             const bool have = tid < count;
-            a.dist_out[frame * a.k + tid] = have ? key_dist(best[tid]) : __int_as_float(0x7f800000);
-            a.label_out[frame * a.k + tid] = have ? static_cast<int64_t>(a.ids[best_row[tid]]) + a.label_base : -1;
+            a.dist_out[frame * a.k + tid] = have ? key_dist(sm.best[tid]) : __int_as_float(0x7f800000);
+            a.label_out[frame * a.k + tid] =
+                have ? static_cast<int64_t>(a.ids[sm.best_row[tid]]) + a.label_base : -1;
         }
         return;
     }
@@ -206,20 +214,20 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame) {
         float dist[8];
         double w[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dist[i] = key_dist(best[i]);
-        weight_sum = reference_weights(dist, count, w);
+        for (int i = 0; i < 8; ++i) dist[i] = key_dist(sm.best[i]);
+        sm.weight_sum = reference_weights(dist, count, w);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) weights[i] = w[i];
+        for (int i = 0; i < 8; ++i) sm.weights[i] = w[i];
     }
     __syncthreads();
     double w[8];
     int32_t rows[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        w[i] = weights[i];
-        rows[i] = best_row[i];
+        w[i] = sm.weights[i];
+        rows[i] = sm.best_row[i];
     }
-    const WeightDivisor sum = weight_divisor(weight_sum);
+    const WeightDivisor sum = weight_divisor(sm.weight_sum);
     for (int i = tid; i < d; i += kThreads) {
         float v[8];
 #pragma unroll
@@ -228,18 +236,107 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame) {
     }
 }
 
+// Loads the frame into q; false when a blend at index_rate <= 0 leaves it
+// as it is (then dst holds the frame).
+__device__ bool frame_prologue(const ExactArgs &a, long long frame, float *q, float &ratio, bool copy_through) {
+    const int tid = threadIdx.x;
+    const int d = a.d;
+    const float *src = a.queries + frame * d;
+    float *dst = a.out + frame * d;
+    ratio = 1.0f;
+    if (a.mode == kModeBlend) {
+        ratio = load_ratio(a.index_rate);
+        if (!(ratio > 0.0f)) {
+            if (copy_through && dst != src)
+                for (int i = tid; i < d; i += kThreads) dst[i] = src[i];
+            return false;
+        }
+    }
+    for (int i = tid; i < d; i += kThreads) q[i] = src[i];
+    __syncthreads();
+    return true;
+}
+
+__device__ void exact_frame(const ExactArgs &a, const long long frame, float *q, FrameSmem &sm) {
+    if (threadIdx.x == 0 && a.frame_list && a.counters) atomicAdd(&a.counters->fallback_frames, 1ull);
+    float ratio;
+    if (!frame_prologue(a, frame, q, ratio, true)) return;
+    const int probes = coarse_stage(a, q, sm);
+    scan_range(a, q, sm, probes, 0u, sm.probe_base[probes]);
+    finish_frame(a, frame, q, ratio, sm, probes);
+}
+
+// Slice `s` of `nsplit` of fallback frame `i` (of at most kSplitFrames): the
+// CTA scans its share of the frame's probed rows and stores its top 8; the
+// last CTA of the frame to finish (device-scope fence and counter, no
+// waiting) merges the slices' lists and finishes the frame.  The keys carry
+// scan positions, so the merged list is the whole scan's top 8.
+__device__ void exact_split(const ExactArgs &a, long long frame, int i, int s, int nsplit, float *q, FrameSmem &sm) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float ratio;
+    if (!frame_prologue(a, frame, q, ratio, s == 0)) return;
+    const int probes = coarse_stage(a, q, sm);
+    const uint64_t total = sm.probe_base[probes];
+    const uint32_t p0 = static_cast<uint32_t>(total * s / nsplit);
+    const uint32_t p1 = static_cast<uint32_t>(total * (s + 1) / nsplit);
+    scan_range(a, q, sm, probes, p0, p1);
+    unsigned long long *slot = a.split_keys + (static_cast<size_t>(i) * kExactSplitGrid + s) * 8;
+    if (tid < 8) slot[tid] = sm.best[tid];
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sm.last = atomicAdd(a.split_done + i, 1) == nsplit - 1;
+    __syncthreads();
+    if (!sm.last) return;
+    __threadfence();
+    if (tid == 0) {
+        a.split_done[i] = 0;  // ready for the next call
+        if (a.counters) atomicAdd(&a.counters->fallback_frames, 1ull);
+    }
+    // the slices' lists, merged: each thread keeps the top 8 of a strided
+    // share, then eight rounds of a block-wide minimum
+    Top8 mine;
+    mine.init();
+    const unsigned long long *all = a.split_keys + static_cast<size_t>(i) * kExactSplitGrid * 8;
+    for (int e = tid; e < nsplit * 8; e += kThreads) mine.insert(__ldcg(all + e));
+    int head = 0;
+    for (int r = 0; r < 8; ++r) {
+        unsigned long long cand = kEmptyKey;
+#pragma unroll
+        for (int h = 0; h < 8; ++h) cand = h == head ? mine.k[h] : cand;
+        const unsigned long long wmin = warp_min_u64(cand);
+        if (lane == 0) sm.red[warp] = wmin;
+        __syncthreads();
+        unsigned long long m = lane < kThreads / 32 ? sm.red[lane] : kEmptyKey;
+        m = warp_min_u64(m);
+        if (cand == m && m != kEmptyKey) ++head;  // keys are distinct: one owner
+        if (tid == 0) sm.best[r] = m;
+        __syncthreads();
+    }
+    finish_frame(a, frame, q, ratio, sm, probes);
+}
+
 // One CTA per frame, or, with a device frame list (the frames the
-// tensor-core engine could not certify), a fixed grid striding over it.
-__global__ void __launch_bounds__(kThreads) exact_kernel(ExactArgs a) {
+// tensor-core engine could not certify), a fixed grid over it: with at most
+// kSplitFrames listed frames (and split scratch), every frame gets
+// gridDim.x / count CTAs, each scanning a slice; otherwise one CTA per frame.
+__global__ void __launch_bounds__(kThreads, 1) exact_kernel(ExactArgs a) {
+    extern __shared__ float q[];  // [d] copy of the frame
+    __shared__ FrameSmem sm;
     grid_dependency_wait();  // the frame list and the outputs belong to the kernel before
     if (a.frame_list) {
         const int count = *a.frame_count;
-        for (int i = blockIdx.x; i < count; i += gridDim.x) {
-            exact_frame(a, a.frame_list[i]);
-            __syncthreads();
+        if (count > 0 && count <= kSplitFrames && a.split_keys && static_cast<int>(gridDim.x) >= 2 * count) {
+            const int nsplit = static_cast<int>(gridDim.x) / count;
+            const int i = static_cast<int>(blockIdx.x) % count, s = static_cast<int>(blockIdx.x) / count;
+            if (s < nsplit) exact_split(a, a.frame_list[i], i, s, nsplit, q, sm);
+        } else {
+            for (int i = blockIdx.x; i < count; i += gridDim.x) {
+                exact_frame(a, a.frame_list[i], q, sm);
+                __syncthreads();
+            }
         }
     } else {
-        exact_frame(a, blockIdx.x);
+        exact_frame(a, blockIdx.x, q, sm);
     }
 }
 
@@ -249,7 +346,7 @@ void launch_exact(const ExactArgs &args, long long frames, cudaStream_t stream, 
     if (frames <= 0) return;
     size_t smem = static_cast<size_t>(args.d) * sizeof(float);
     unsigned grid = static_cast<unsigned>(frames);
-    if (args.frame_list) grid = static_cast<unsigned>(frames < 1184 ? frames : 1184);
+    if (args.frame_list) grid = static_cast<unsigned>(frames < kExactSplitGrid ? frames : kExactSplitGrid);
     if (after_kernel) {
         const cudaError_t rc = launch_pdl(exact_kernel, dim3(grid), dim3(kThreads), smem, stream, args);
         if (rc != cudaSuccess) throw std::runtime_error(std::string("exact kernel launch: ") + cudaGetErrorString(rc));

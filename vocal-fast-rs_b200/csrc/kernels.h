@@ -40,7 +40,15 @@ struct ExactArgs {
     DeviceCounters *counters;
     const int32_t *frame_list;   // optional: frames to process (device)
     const int32_t *frame_count;  // with frame_list: its length (device)
+    // optional, with frame_list: scratch that lets up to kSplitFrames listed
+    // frames share the grid ([kSplitFrames][kExactSplitGrid][8] keys and
+    // kSplitFrames counters, zero between calls)
+    unsigned long long *split_keys;
+    int32_t *split_done;
 };
+constexpr int kSplitFrames = 64;       // listed frames that share the grid
+constexpr int kExactSplitGrid = 1184;  // CTAs of a frame-list launch at most
+constexpr size_t kSplitKeyBytes = static_cast<size_t>(kSplitFrames) * kExactSplitGrid * 8 * 8;
 // frames: the frame count, or with a frame list the largest possible length.
 // after_kernel: launched behind another kernel of the same call, which it may
 // overlap until its own dependency wait (programmatic dependent launch).

@@ -2231,6 +2231,8 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     ea.counters = ix->counters;
     ea.frame_list = flist;
     ea.frame_count = fcount;
+    ea.split_keys = ix->split_keys;
+    ea.split_done = ix->split_done;
     ix->prof.begin(kProfExact, stream);
     launch_exact(ea, static_cast<long long>(frames), stream);
     ix->prof.end(stream);
@@ -2346,6 +2348,8 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ea.counters = ix->counters;
     ea.frame_list = flist;
     ea.frame_count = fcount;
+    ea.split_keys = ix->split_keys;
+    ea.split_done = ix->split_done;
     ix->prof.begin(kProfExact, stream);
     launch_exact(ea, static_cast<long long>(frames), stream, true);
     ix->prof.end(stream);
@@ -2502,6 +2506,8 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ea.counters = ix->counters;
     ea.frame_list = flist;
     ea.frame_count = fcount;
+    ea.split_keys = ix->split_keys;
+    ea.split_done = ix->split_done;
     launch_exact(ea, static_cast<long long>(frames), stream, true);
     cuda_check(cudaGetLastError());
 }

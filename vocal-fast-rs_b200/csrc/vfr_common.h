@@ -162,6 +162,10 @@ struct VfrIndex {
     // shared with other handles loaded from the same content; they are then
     // freed with the last handle, not by this one.
     std::shared_ptr<vfr::SharedRows> shared;
+    // Re-run scratch of the exact kernel, per handle: lets a few uncertified
+    // frames share its grid (ExactArgs::split_keys / split_done).
+    unsigned long long *split_keys = nullptr;
+    int32_t *split_done = nullptr;
 };
 
 namespace vfr {
