@@ -36,7 +36,7 @@ SharedRows::~SharedRows() {
                     static_cast<void *>(proto.vectors), static_cast<void *>(proto.ids),
                     static_cast<void *>(proto.row_of_id), static_cast<void *>(proto.vectors_h),
                     static_cast<void *>(proto.row_norms), static_cast<void *>(proto.centroids_h),
-                    static_cast<void *>(proto.centroid_norms)})
+                    static_cast<void *>(proto.centroid_norms), static_cast<void *>(proto.list_order)})
         if (p) cudaFree(p);
     cudaSetDevice(previous);
 }

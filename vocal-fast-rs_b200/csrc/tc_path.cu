@@ -138,7 +138,8 @@ struct CandArgs {
     const int2 *items;
     const int *item_count;
     const int32_t *list_offsets;  // database row offsets [nlist + 1]
-    const int32_t *list_start;    // pair offsets [nlist + 1]
+    const int32_t *list_start;    // pair offsets [nlist + 1] (lists in size order, not id order)
+    const int32_t *list_count;    // pairs per list [nlist]
     int pair_stride;              // output stride: pairs capacity
 };
 
@@ -159,13 +160,19 @@ __device__ __forceinline__ int item_total(const CandArgs &a) {
     else return a.segments * a.n_qtiles;
 }
 
+// IVF items come largest first (the item table follows the lists in
+// descending size); CTA g takes items g, g + G, ... of a "snake" order that
+// reverses every other round of G, so each CTA's load evens out.
 template <bool kIvf>
-__device__ __forceinline__ Item item_at(const CandArgs &a, int item) {
+__device__ __forceinline__ Item item_at(const CandArgs &a, int item, int total) {
     Item it{};
     if constexpr (kIvf) {
-        const int2 e = a.items[item];
+        const int g = static_cast<int>(gridDim.x);
+        const int round = item / g, pos = item - round * g;
+        const int in_round = min(g, total - round * g);
+        const int2 e = a.items[(round & 1) ? round * g + (in_round - 1 - pos) : item];
         it.a_row0 = a.list_start[e.x] + e.y * kTileM;
-        it.a_rows = min(kTileM, a.list_start[e.x + 1] - it.a_row0);
+        it.a_rows = min(kTileM, a.list_start[e.x] + a.list_count[e.x] - it.a_row0);
         it.b_row0 = a.list_offsets[e.x];
         it.b_end = a.list_offsets[e.x + 1];
         it.seg = 0;
@@ -335,7 +342,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             int early = 0;
             if constexpr (!kIvf) {
                 if (static_cast<int>(blockIdx.x) < items) {
-                    const Item it0 = item_at<kIvf>(a, blockIdx.x);
+                    const Item it0 = item_at<kIvf>(a, blockIdx.x, items);
                     early = min(kStages, it0.tiles * a.ksteps);
                     for (int s = 0; s < early; ++s) {
                         const int t = s / a.ksteps, k = s % a.ksteps;
@@ -350,7 +357,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             uint32_t phase = 0;
             int issued = 0;
             for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
-                const Item it = item_at<kIvf>(a, item);
+                const Item it = item_at<kIvf>(a, item, items);
                 for (int t = 0; t < it.tiles && !*abort_flag; ++t) {
                     for (int k = 0; k < a.ksteps; ++k, ++issued) {
                         if (!tc::mbar_wait(&empty[stage], phase ^ 1, kWaitLimitNs)) {
@@ -394,7 +401,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             uint32_t phase = 0;
             uint32_t acc_count = 0;
             for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
-                const Item it = item_at<kIvf>(a, item);
+                const Item it = item_at<kIvf>(a, item, items);
                 for (int t = 0; t < it.tiles && !*abort_flag; ++t) {
                     const uint32_t b = acc_count & 1;
                     if (!tc::mbar_wait(&acc_empty[b], ((acc_count >> 1) & 1) ^ 1, kWaitLimitNs)) {
@@ -446,7 +453,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         uint32_t acc_count = 0;
         const float inf = __int_as_float(0x7f800000);
         for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
-            const Item it = item_at<kIvf>(a, item);
+            const Item it = item_at<kIvf>(a, item, items);
             const int64_t row0 = it.b_row0;
             const int tiles = it.tiles;
             TopList<K> top;
@@ -1577,7 +1584,8 @@ __global__ void __launch_bounds__(kMergeThreads) coarse_select_kernel(CoarseArgs
 // One CTA of 1024 threads: pair offsets per list (exclusive scan of
 // list_count), reset of the scatter cursors, and the fine-stage work items
 // (list, frame tile within the list's pairs).
-__global__ void __launch_bounds__(1024) bucket_scan_kernel(const int32_t *__restrict__ list_count, int nlist,
+__global__ void __launch_bounds__(1024) bucket_scan_kernel(const int32_t *__restrict__ list_count,
+                                                           const int32_t *__restrict__ order, int nlist,
                                                            int32_t *__restrict__ list_start,
                                                            int32_t *__restrict__ list_cursor, int2 *__restrict__ items,
                                                            int *__restrict__ item_count) {
@@ -1586,8 +1594,8 @@ __global__ void __launch_bounds__(1024) bucket_scan_kernel(const int32_t *__rest
     const int per = (nlist + 1023) / 1024;
     const int l0 = min(nlist, tid * per), l1 = min(nlist, l0 + per);
     int pairs = 0, tiles = 0;
-    for (int l = l0; l < l1; ++l) {
-        const int c = list_count[l];
+    for (int o = l0; o < l1; ++o) {
+        const int c = list_count[order[o]];
         pairs += c;
         tiles += (c + kTileM - 1) / kTileM;
     }
@@ -1621,7 +1629,8 @@ __global__ void __launch_bounds__(1024) bucket_scan_kernel(const int32_t *__rest
     __syncthreads();
     int pbase = ip - pairs + (warp > 0 ? warp_pairs[warp - 1] : 0);
     int ibase = it - tiles + (warp > 0 ? warp_items[warp - 1] : 0);
-    for (int l = l0; l < l1; ++l) {
+    for (int o = l0; o < l1; ++o) {
+        const int l = order[o];
         const int c = list_count[l];
         list_start[l] = pbase;
         list_cursor[l] = 0;
@@ -1975,7 +1984,18 @@ void build_tc(VfrIndex *ix) {
         return;
     }
     encode_rows(&ix->tmap_vectors, ix->vectors_h, ix->d_pad, ix->n_pad, kTileN);
-    if (ivf) encode_rows(&ix->tmap_centroids, ix->centroids_h, ix->d_pad, ix->nlist_pad, kTileN);
+    if (ivf) {
+        encode_rows(&ix->tmap_centroids, ix->centroids_h, ix->d_pad, ix->nlist_pad, kTileN);
+        // lists by descending size (ties by id): the fine stage's item table
+        // follows this order, largest work first
+        std::vector<int32_t> order(static_cast<size_t>(ix->nlist));
+        for (int32_t l = 0; l < ix->nlist; ++l) order[l] = l;
+        const std::vector<int32_t> &off = ix->host_offsets;
+        std::stable_sort(order.begin(), order.end(),
+                         [&](int32_t x, int32_t y) { return off[x + 1] - off[x] > off[y + 1] - off[y]; });
+        cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->list_order), order.size() * sizeof(int32_t)));
+        cuda_check(cudaMemcpy(ix->list_order, order.data(), order.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
+    }
     constexpr int kBig = static_cast<int>(Pipe<kFullLayout>::kSmem), kSmall = static_cast<int>(Pipe<kSpreadLayout>::kSmem);
     cuda_check(cudaFuncSetAttribute(cand_kernel<false, kShortKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBig));
     cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBig));
@@ -2007,7 +2027,9 @@ void release_tc(VfrIndex *ix) noexcept {
         if (ix->row_norms) cudaFree(ix->row_norms);
         if (ix->centroids_h) cudaFree(ix->centroids_h);
         if (ix->centroid_norms) cudaFree(ix->centroid_norms);
+        if (ix->list_order) cudaFree(ix->list_order);
     }
+    ix->list_order = nullptr;
     ix->centroids_h = nullptr;
     ix->centroid_norms = nullptr;
     if (ix->ws.base) cudaFree(ix->ws.base);
@@ -2141,7 +2163,8 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
                            static_cast<size_t>(cs.slots) * 8 + static_cast<size_t>(ix->d) * 4, stream>>>(cs);
     cuda_check(cudaGetLastError());
     // 4. pairs bucketed by list, frames gathered into list order
-    bucket_scan_kernel<<<1, 1024, 0, stream>>>(list_count, ix->nlist, list_start, list_cursor, items, item_count);
+    bucket_scan_kernel<<<1, 1024, 0, stream>>>(list_count, ix->list_order, ix->nlist, list_start, list_cursor, items,
+                                                item_count);
     cuda_check(cudaGetLastError());
     const long long npairs = static_cast<long long>(frames) * P;
     bucket_scatter_kernel<<<static_cast<unsigned>((npairs + 255) / 256), 256, 0, stream>>>(
@@ -2168,6 +2191,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     cf.item_count = item_count;
     cf.list_offsets = ix->offsets;
     cf.list_start = list_start;
+    cf.list_count = list_count;
     cf.pair_stride = static_cast<int>(pair_cap);
     ix->prof.begin(kProfCand, stream);
     cand_kernel<true, kIvfKeep><<<ix->sm_count, kThreadsTC, Pipe<kFullLayout>::kSmem, stream>>>(tmap_qp, ix->tmap_vectors, cf);

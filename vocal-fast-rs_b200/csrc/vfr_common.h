@@ -153,6 +153,7 @@ struct VfrIndex {
     float *centroid_norms = nullptr;
     int32_t nlist_pad = 0;
     float max_cent_norm = 0.f, max_cent_hat = 0.f, max_cent_residual = 0.f;
+    int32_t *list_order = nullptr;  // [nlist] list ids by descending size (IVF fine-stage order)
     alignas(64) CUtensorMap tmap_centroids;
     alignas(64) CUtensorMap tmap_vectors;  // fp16 rows, box [256 rows][64]
     bool have_tc = false;
