@@ -966,13 +966,61 @@ __device__ __forceinline__ void merge_octet_lists(const unsigned long long *octe
 // approximate distance >= bound; qs = (||q||^2, ||q^||, ||q - q^||); the
 // database bounds are max ||x||, max ||x^||, max ||x - x^||.  True when no
 // dropped candidate can reach (or tie) the `rank`-th exact distance dk.
+// The bound e on |(d~ + ||q||^2) - true distance| for an approximate key
+// distance d~ of this frame (the certificate's error model).
+__device__ __forceinline__ float approx_error(float4 qs, float max_norm, float max_hat, float max_residual,
+                                              float acc_rel, float norm_rel) {
+    return 2.f * (qs.y * max_residual + qs.z * max_norm) + 2.f * acc_rel * qs.y * max_hat +
+           norm_rel * (max_norm * max_norm + qs.x) + 6e-8f * (max_norm * max_norm + 2.f * qs.y * max_hat);
+}
+
 __device__ __forceinline__ bool certify(float bound, float dk, float4 qs, float max_norm, float max_hat,
                                         float max_residual, float acc_rel, float norm_rel, float exact_rel) {
     if (!(bound < __int_as_float(0x7f800000)) && bound == bound) return true;  // nothing was dropped
-    const float e = 2.f * (qs.y * max_residual + qs.z * max_norm) + 2.f * acc_rel * qs.y * max_hat +
-                    norm_rel * (max_norm * max_norm + qs.x) + 6e-8f * (max_norm * max_norm + 2.f * qs.y * max_hat);
+    const float e = approx_error(qs, max_norm, max_hat, max_residual, acc_rel, norm_rel);
     const float lower = bound + qs.x - e;
     return lower > dk * (1.f + 4.f * exact_rel) + 1e-30f;
+}
+
+// Shared scratch of narrow_rerank.
+struct NarrowState {
+    unsigned long long keys[kRerankMax];
+    int count;
+    float upper;
+};
+
+// Drops from sel_keys[0 .. m) the candidates that cannot reach the frame's
+// `rank`-th exact distance, so their rows are never fetched: with U the
+// rank-th smallest upper bound d~ + ||q||^2 + e among them, a candidate
+// whose lower bound d~ + ||q||^2 - e exceeds U (1 + 4 exact_rel) has an
+// exact distance (reference order, relative error within exact_rel) above
+// at least `rank` of the others, so it is neither in nor tied with the
+// top `rank`.  The certificate over the candidates the selection dropped is
+// unchanged.  Compacts sel_keys (order not kept); returns the count.  Called
+// by every thread.
+template <int kT>
+__device__ int narrow_rerank(unsigned long long *sel_keys, int m, int rank, float qsx, float e, float exact_rel,
+                             NarrowState &ns) {
+    if (m <= rank) return m;
+    const int tid = threadIdx.x;
+    if (tid == 0) ns.count = 0;
+    for (int c = tid; c < m; c += kT) {
+        const unsigned long long key = sel_keys[c];
+        int rk = 0;
+        for (int i = 0; i < m; ++i) rk += sel_keys[i] < key;
+        if (rk == rank - 1) ns.upper = key_dist(key);
+    }
+    __syncthreads();
+    const float limit = (ns.upper + qsx + e) * (1.f + 4.f * exact_rel) + 1e-30f;
+    for (int c = tid; c < m; c += kT) {
+        const unsigned long long key = sel_keys[c];
+        if (!(key_dist(key) + qsx - e > limit)) ns.keys[atomicAdd(&ns.count, 1)] = key;
+    }
+    __syncthreads();
+    const int kept = ns.count;
+    for (int c = tid; c < kept; c += kT) sel_keys[c] = ns.keys[c];
+    __syncthreads();
+    return kept;
 }
 
 // Exact distances of staged rows [0, rows) (stage rows of `stride` floats;
@@ -1039,6 +1087,7 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreads ? 3 : 1) merge_kernel(
     __shared__ int certified_s;
     __shared__ SelectState sel;
     __shared__ unsigned long long sel_keys[kRerankMax];
+    __shared__ NarrowState narrow;
     __shared__ double weights[8];
     __shared__ int best_slot[8];
     __shared__ __align__(8) uint64_t gather_bar;
@@ -1112,8 +1161,14 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreads ? 3 : 1) merge_kernel(
     float cut;
     bool too_many_ties;
     const int stop = a.stage_rows >= kRerank ? min(kRerankStop, a.stage_rows) : kRerankStop;
-    const int m = select_rerank<kT>(keys, a.sort_size, ks, sel_keys, sel, cut, too_many_ties, wide, stop);
+    int m = select_rerank<kT>(keys, a.sort_size, ks, sel_keys, sel, cut, too_many_ties, wide, stop);
     const float t_final = fminf(ks.tmin, cut);
+    {
+        const float4 qs = a.qstats[frame];
+        m = narrow_rerank<kT>(sel_keys, m, 8, qs.x,
+                              approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel),
+                              a.exact_rel, narrow);
+    }
 
     // exact re-rank in the reference order (flat scan position == row): one
     // octet per distance, each written to exact_keys; +inf and NaN distances
@@ -1529,9 +1584,11 @@ __global__ void __launch_bounds__(kMergeThreads) coarse_select_kernel(CoarseArgs
     const KeyStats ks = key_stats<kMergeThreads>(keys, a.slots, tmin, sel);
     float cut;
     bool too_many;
-    const int m = select_rerank<kMergeThreads>(keys, a.slots, ks, sel_keys, sel, cut, too_many);
+    int m = select_rerank<kMergeThreads>(keys, a.slots, ks, sel_keys, sel, cut, too_many);
     const float bound = fminf(ks.tmin, cut);
-    // exact centroid distances; every centroid takes part, as in the
+    const float4 qs = a.qstats[frame];
+    // exact centroid distances (no narrowing: the centroid rows come from
+    // L2, so the extra pass costs more than it saves); every centroid takes part, as in the
     // reference's sort (no +inf filter here)
     for (int c0 = 0; c0 < m; c0 += 64) {
         uint32_t lists[2];
@@ -1563,8 +1620,7 @@ __global__ void __launch_bounds__(kMergeThreads) coarse_select_kernel(CoarseArgs
         bool ok = !too_many && m >= P;
         if (ok) {
             const float dp = key_dist(top_keys[P - 1]);
-            ok = certify(bound, dp, a.qstats[frame], a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel,
-                         a.exact_rel);
+            ok = certify(bound, dp, qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel, a.exact_rel);
         }
         ok_s = ok;
         a.probe_ok[frame] = ok ? 1 : 0;
@@ -1707,6 +1763,7 @@ __global__ void __launch_bounds__(kMergeThreads, 3) ivf_merge_kernel(IvfMergeArg
     __shared__ unsigned long long sel_keys[kRerankMax];
     __shared__ unsigned long long octet_best[32 * 8];
     __shared__ unsigned long long best[8];
+    __shared__ NarrowState narrow;
     __shared__ int32_t pstart[kIvfMaxProbe], pend[kIvfMaxProbe];
     __shared__ uint32_t pbase[kIvfMaxProbe + 1];
     __shared__ int certified_s;
@@ -1749,8 +1806,12 @@ __global__ void __launch_bounds__(kMergeThreads, 3) ivf_merge_kernel(IvfMergeArg
     const KeyStats ks = key_stats<kMergeThreads>(keys, kSlots, tmin, sel);
     float cut;
     bool too_many;
-    const int m = select_rerank<kMergeThreads>(keys, kSlots, ks, sel_keys, sel, cut, too_many);
+    int m = select_rerank<kMergeThreads>(keys, kSlots, ks, sel_keys, sel, cut, too_many);
     const float bound = fminf(ks.tmin, cut);
+    const float4 qs = a.qstats[frame];
+    m = narrow_rerank<kMergeThreads>(sel_keys, m, 8, qs.x,
+                                     approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel),
+                                     a.exact_rel, narrow);
     // exact re-rank; the key's position is the reference's scan position
     Top8 top;
     top.init();
@@ -1785,7 +1846,7 @@ __global__ void __launch_bounds__(kMergeThreads, 3) ivf_merge_kernel(IvfMergeArg
         int count = 0;
         while (count < 8 && best[count] != kEmptyKey) ++count;
         const float d8 = count == 8 ? key_dist(best[7]) : inf;
-        const bool ok = !too_many && certify(bound, d8, a.qstats[frame], a.max_norm, a.max_hat, a.max_residual,
+        const bool ok = !too_many && certify(bound, d8, qs, a.max_norm, a.max_hat, a.max_residual,
                                              a.acc_rel, a.norm_rel, a.exact_rel);
         certified_s = ok ? count + 1 : 0;
     }
