@@ -71,7 +71,7 @@ struct FrameSmem {
 // The coarse stage: the first nprobe lists in (distance, list id) order and
 // the scan position where each starts (probe_base[probes] = rows scanned).
 // Returns the number of probed lists.  Called by every thread.
-__device__ int coarse_stage(const ExactArgs &a, const float *q, FrameSmem &sm) {
+__device__ int coarse_stage(const ExactArgs &a, long long frame, const float *q, FrameSmem &sm) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
     const int octet_base = lane & ~7;
     const int d = a.d;
@@ -79,6 +79,10 @@ __device__ int coarse_stage(const ExactArgs &a, const float *q, FrameSmem &sm) {
     if (a.nlist == 1) {
         if (tid == 0) sm.probe_list[0] = 0;
         probes = 1;
+    } else if (a.probes && a.probe_ok[frame]) {
+        // the tensor-core coarse stage certified this frame's lists (the same
+        // exact order): only its fine stage was left open
+        if (tid < probes) sm.probe_list[tid] = a.probes[frame * a.nprobe + tid];
     } else {
         if (tid < kMaxProbe) sm.probe_keys[tid] = kEmptyKey;
         __syncthreads();
@@ -261,7 +265,7 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame, float *q,
     if (threadIdx.x == 0 && a.frame_list && a.counters) atomicAdd(&a.counters->fallback_frames, 1ull);
     float ratio;
     if (!frame_prologue(a, frame, q, ratio, true)) return;
-    const int probes = coarse_stage(a, q, sm);
+    const int probes = coarse_stage(a, frame, q, sm);
     scan_range(a, q, sm, probes, 0u, sm.probe_base[probes]);
     finish_frame(a, frame, q, ratio, sm, probes);
 }
@@ -275,7 +279,7 @@ __device__ void exact_split(const ExactArgs &a, long long frame, int i, int s, i
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float ratio;
     if (!frame_prologue(a, frame, q, ratio, s == 0)) return;
-    const int probes = coarse_stage(a, q, sm);
+    const int probes = coarse_stage(a, frame, q, sm);
     const uint64_t total = sm.probe_base[probes];
     const uint32_t p0 = static_cast<uint32_t>(total * s / nsplit);
     const uint32_t p1 = static_cast<uint32_t>(total * (s + 1) / nsplit);

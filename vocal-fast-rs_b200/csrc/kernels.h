@@ -45,6 +45,10 @@ struct ExactArgs {
     // kSplitFrames counters, zero between calls)
     unsigned long long *split_keys;
     int32_t *split_done;
+    // optional (IVF): the coarse stage's lists per frame ([frame][nprobe], in
+    // coarse order) and whether they are set; reused instead of recomputed
+    const int32_t *probes;
+    const int32_t *probe_ok;
 };
 constexpr int kSplitFrames = 64;       // listed frames that share the grid
 constexpr int kExactSplitGrid = 1184;  // CTAs of a frame-list launch at most

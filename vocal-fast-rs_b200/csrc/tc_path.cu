@@ -2318,6 +2318,8 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     ea.frame_count = fcount;
     ea.split_keys = ix->split_keys;
     ea.split_done = ix->split_done;
+    ea.probes = probes;
+    ea.probe_ok = probe_ok;
     ix->prof.begin(kProfExact, stream);
     launch_exact(ea, static_cast<long long>(frames), stream);
     ix->prof.end(stream);
