@@ -183,6 +183,11 @@ VFR_API int vfr_index_load_vfrm(const uint8_t *image, size_t length, int32_t fea
 VFR_API int vfr_index_load_file(const char *path, int32_t feature_dims, const VfrOptions *options, VfrIndex **out,
                                 char **error);
 
+/* The 128-bit content hash VFR_SHARE_STORAGE keys shared storage by
+ * (hash[0], hash[1]); the same bytes give the same hash on every host and
+ * thread count.  Host memory only; usable without a GPU. */
+VFR_API int vfr_index_content_hash(const uint8_t *bytes, size_t length, uint64_t *hash, char **error);
+
 /* IVF training (the offline FAISS step the reference runs with
  * IndexIVFFlat::train/add; recipe in crates/vocal-directml/tests/fixtures/
  * README.md and scripts/benchmark-retrieval.py:56-65), on the device.

@@ -299,3 +299,61 @@ def test_shared_storage(cuda):
     assert np.array_equal(_blend(c2, q, 0.75, cuda), want)
     for g in (c2, plain, exact, other):
         g.close()
+
+
+# ------------------------------------------------------- host-only checks
+
+
+def _hash(data) -> tuple:
+    from vfr import lib
+
+    buf = np.frombuffer(bytes(data), np.uint8) if len(data) else np.zeros(0, np.uint8)
+    out = np.zeros(2, np.uint64)
+    lib.call(lib.load_library().vfr_index_content_hash, buf.ctypes.data if buf.size else None, buf.size,
+             out.ctypes.data)
+    return int(out[0]), int(out[1])
+
+
+def test_content_hash_keys_bytes():
+    """The share key: stable for the same bytes, different for any change
+    (every byte flipped in turn on a small image, random flips across 1 MiB
+    blocks on a large one), the length included."""
+    rng = np.random.default_rng(17)
+    small = rng.integers(0, 256, 300, dtype=np.uint8).tobytes()
+    base = _hash(small)
+    assert _hash(small) == base and _hash(bytearray(small)) == base
+    seen = {base}
+    for i in range(len(small)):
+        b = bytearray(small)
+        b[i] ^= 0x01
+        seen.add(_hash(b))
+    assert len(seen) == len(small) + 1
+    assert _hash(small + b"\0") != base and _hash(small[:-1]) != base and _hash(b"") != _hash(b"\0")
+    big = rng.integers(0, 256, (5 << 20) + 123, dtype=np.uint8)
+    hb = _hash(big)
+    assert _hash(big.copy()) == hb
+    for pos in rng.integers(0, big.size, 8):
+        b = big.copy()
+        b[pos] ^= 0x80
+        assert _hash(b) != hb
+
+
+def test_file_loader_errors_without_device(tmp_path):
+    """Errors raised before any device work carry the parser's message; a
+    missing file names the path."""
+    import ctypes
+
+    from vfr import lib
+
+    L = lib.load_library()
+    out = ctypes.c_void_p()
+    with pytest.raises(lib.NativeError, match="cannot open retrieval index file"):
+        lib.call(L.vfr_index_load_file, str(tmp_path / "missing.index").encode(), 0, None, ctypes.byref(out))
+    flat = golden("parser_flat.bin")
+    (tmp_path / "cut.index").write_bytes(flat[:20])
+    with pytest.raises(lib.NativeError) as e:
+        lib.call(L.vfr_index_load_file, str(tmp_path / "cut.index").encode(), 0, None, ctypes.byref(out))
+    assert str(e.value) == _parse_error(flat[:20])
+    (tmp_path / "empty.index").write_bytes(b"")
+    with pytest.raises(lib.NativeError, match="truncated index"):
+        lib.call(L.vfr_index_load_file, str(tmp_path / "empty.index").encode(), 0, None, ctypes.byref(out))

@@ -651,6 +651,15 @@ extern "C" int vfr_index_load_file(const char *path, int32_t feature_dims, const
     });
 }
 
+extern "C" int vfr_index_content_hash(const uint8_t *bytes, size_t length, uint64_t *hash, char **error) {
+    return guarded(error, [&] {
+        require(hash && (bytes || length == 0), "null hash input or output");
+        const vfr::ContentHash h = vfr::content_hash(bytes, length);
+        hash[0] = h.lo;
+        hash[1] = h.hi;
+    });
+}
+
 // ---- IVF training --------------------------------------------------------
 
 extern "C" int vfr_kmeans(const float *x, int64_t n, int32_t d, int32_t k, int32_t niter,

@@ -83,6 +83,7 @@ def load_library(path: str | None = None):
         "vfr_index_load": ([vp, sz, P(Options), P(vp), err], ctypes.c_int),
         "vfr_index_load_vfrm": ([vp, sz, i32, P(Options), P(vp), err], ctypes.c_int),
         "vfr_index_load_file": ([ctypes.c_char_p, i32, P(Options), P(vp), err], ctypes.c_int),
+        "vfr_index_content_hash": ([vp, sz, vp, err], ctypes.c_int),
         "vfr_kmeans": ([vp, i64, i32, i32, i32, i32, ctypes.c_uint64, vp, vp, P(Stream), err], ctypes.c_int),
         "vfr_ivf_assign": ([vp, i32, vp, i64, i32, vp, vp, P(Stream), err], ctypes.c_int),
         "vfr_ivf_build": ([vp, i32, vp, i64, i32, i32, P(Options), P(vp), err], ctypes.c_int),
