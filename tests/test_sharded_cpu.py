@@ -142,3 +142,80 @@ def test_shard_rows_cover_everything():
             assert spans[0][0] == 0 and spans[-1][1] == n
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
     assert padded_frames(30000, 8) == 30000 and padded_frames(30001, 8) == 30008
+
+
+class OracleReplica:
+    """A full replica for query sharding: the oracle's blend on CPU tensors."""
+
+    def __init__(self, oracle_index, ratio):
+        self.o = oracle_index
+        self.ratio = ratio
+
+    def blend(self, feats, frames, rate, stream=None):
+        out, _ = self.o.blend(feats.numpy()[:frames], float(rate[0]))
+        feats[:frames] = torch.from_numpy(out)
+
+
+def _query_worker(rank, world, port, arrays, queries, ratio, gather, results):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "vocal-fast-rs_b200"), root, os.path.join(root, "tests")]
+    import datetime
+
+    import torch.distributed as dist
+    from oracle import oracle as orc
+    from test_sharded_cpu import OracleReplica
+    from vfr.sharded import query_sharded_blend
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    centroids, offsets, vectors, ids, nprobe = arrays
+    replica = OracleReplica(orc.OracleIndex.from_arrays(centroids, offsets, vectors, ids, nprobe), ratio)
+    out = query_sharded_blend(replica, torch.from_numpy(queries), torch.tensor([ratio]), dist.group.WORLD, world,
+                              rank, gather=gather)
+    results[rank] = out.numpy()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,frames,gather", [(2, 41, False), (2, 41, True), (3, 10, True)])
+def test_query_sharded_choreography_matches_single_index(oracle, world, frames, gather):
+    """Each rank blends its contiguous share of the frames against a full
+    replica (here the oracle); the shares in rank order, or the gathered
+    batch on every rank, equal the single-index blend (an IVF index, so the
+    mode's use case, offline IVF batches, is the one exercised)."""
+    from vfr import synth
+
+    ix, q = synth.make_np("c3", n=4000, q=frames, nprobe=2)
+    ratio = 0.75
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _free_port()
+    arrays = (ix.centroids, ix.offsets, ix.vectors, ix.ids, ix.nprobe)
+    procs = [ctx.Process(target=_query_worker, args=(r, world, port, arrays, q, ratio, gather, results))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+        assert p.exitcode == 0
+    expected, status = oracle.OracleIndex.from_arrays(ix.centroids, ix.offsets, ix.vectors, ix.ids, ix.nprobe).blend(
+        q, ratio)
+    if gather:
+        for r in range(world):
+            assert np.array_equal(results[r].view(np.uint32), expected.view(np.uint32))
+    else:
+        got = np.concatenate([results[r] for r in range(world)])
+        assert np.array_equal(got.view(np.uint32), expected.view(np.uint32))
+
+
+def test_shard_frames_cover_everything():
+    from vfr.sharded import shard_frames
+
+    for q in (0, 1, 7, 30_000):
+        for world in (1, 2, 3, 8):
+            spans = [shard_frames(q, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == q
+            assert all(spans[r][1] == spans[r + 1][0] for r in range(world - 1))
+            assert max(b - a for a, b in spans) - min(b - a for a, b in spans) <= 1

@@ -20,6 +20,11 @@ rank r is frames [r*Q/G, (r+1)*Q/G).  The reference is single-GPU; this is the
 multi-GPU extension of its path.  Collectives are taken in the same order on
 every rank.  `ops` selects the per-rank compute: `LibraryOps` (CUDA library,
 the product) or a test double with the same interface.
+
+Query sharding (`query_sharded_blend`) is the other mode, for large offline
+batches against an index that fits one GPU (c3): every rank holds a full
+replica and blends its contiguous share of the frames; no collective is
+needed unless every rank wants the whole output (`gather=True`).
 """
 from __future__ import annotations
 
@@ -119,3 +124,32 @@ def sharded_blend(ops, queries, rate, group, world: int, rank: int, stream=None)
     lo = rank * m
     out = ops.blend(queries[lo:lo + m], md[lo:lo + m].contiguous(), mine, rate, stream)
     return out, md, ml
+
+
+def shard_frames(q: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous frame range of `rank` in query sharding (sizes differ by at
+    most one)."""
+    return q * rank // world, q * (rank + 1) // world
+
+
+def query_sharded_blend(index, queries, rate, group, world: int, rank: int, stream=None, gather: bool = False):
+    """Query-sharded blend: `index` is this rank's full replica (a
+    GpuRetrievalIndex, or a test double with its `blend`), `queries` [Q, d]
+    the whole batch on every rank.  Returns this rank's blended frames
+    [hi - lo, d] (frames [lo, hi) of shard_frames), or with gather=True the
+    whole blended batch [Q, d] on every rank (one all-gather of equal-size,
+    padded slices)."""
+    q = queries.shape[0]
+    lo, hi = shard_frames(q, world, rank)
+    out = queries[lo:hi].clone()
+    if hi > lo:
+        index.blend(out, hi - lo, rate, stream=stream)
+    if not gather:
+        return out
+    import torch
+
+    m = (q + world - 1) // world
+    padded = torch.zeros((m,) + tuple(queries.shape[1:]), dtype=queries.dtype, device=queries.device)
+    padded[: hi - lo] = out
+    parts = _all_gather(padded, group, world)
+    return torch.cat([parts[r][: shard_frames(q, world, r)[1] - shard_frames(q, world, r)[0]] for r in range(world)])
