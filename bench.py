@@ -18,7 +18,13 @@ steps; cpu_baseline = the CPU oracle (restatement of the reference's CPU
 retrieval) on a bounded sample of frames against the same database, all host
 cores; streaming = the c4 realtime config (Q=32 frames per block, N=100,000)
 replayed as a CUDA graph, p50/p95 per-block latency over 1,000 blocks; ivf =
-the c3 IVF-Flat config (200k rows, nlist 256, 30k frames) at nprobe 1 and 8.
+the c3 IVF-Flat config (200k rows, nlist 256, 30k frames) at nprobe 1 and 8,
+each with a roofline from the lists the frames actually probe; c1 / c2 = those
+configs' blends (graph replay, L2 flushed or warm) with the candidate
+kernel's roofline; published_shape = a seeded stand-in for the reference's
+published IVF511 timings (34 and 140 frames); parity (every N) = rank 0's
+first 64 output frames of a full-size step against the CPU oracle's exact
+scan of all rows.
 
 `--impl reference` times the reference's CPU retrieval (the oracle port; the
 Rust original cannot be built here) on the same workload instead.
@@ -57,6 +63,8 @@ def args_parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ingest", action="store_true", help="skip the c5 index-ingest timing")
     ap.add_argument("--no-training", action="store_true", help="skip the IVF training timing")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of rank 0's first frames")
+    ap.add_argument("--no-configs", action="store_true", help="skip the c1/c2/published-shape timings")
     return ap.parse_args()
 
 
@@ -199,6 +207,34 @@ def cpu_baseline(vectors, queries, ratio, n):
     return {"value": sample / dt, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"first {sample} frames against all {n} rows ({dt:.1f} s), AVX2-order C restatement, "
                       f"{cores} threads"}
+
+
+PARITY_FRAMES = 64
+STEP_TIMEOUT_S = 120.0  # host deadline of one row-sharded step's collectives
+
+
+def parity_check(vectors, q, out, dist, labels, ratio, n):
+    """Bit-level comparison of the benchmarked path's output for frames
+    `q` (blended `out`, top-8 `dist`/`labels` of the same full-size step)
+    with the oracle (C restatement of crates/vocal-cpu/src/retrieval.rs:27-83)
+    scanning all n rows on every host thread."""
+    import numpy as np
+
+    from oracle import oracle
+    from vfr import synth
+
+    cores = os.cpu_count() or 1
+    flat = synth.flat_arrays(vectors)
+    orc = oracle.OracleIndex.from_arrays(flat.centroids, flat.offsets, flat.vectors, flat.ids, 1)
+    t0 = time.perf_counter()
+    expected, status = orc.blend(q, ratio, threads=cores)
+    od, _, ol, _ = orc.search(q, threads=cores)
+    dt = time.perf_counter() - t0
+    return {"frames": int(q.shape[0]), "rows": n, "label_mismatches": int((ol != labels).any(1).sum()),
+            "distance_bit_mismatches": int((od.view(np.uint32) != dist.view(np.uint32)).any(1).sum()),
+            "blend_bit_mismatches": int((expected.view(np.uint32) != out.view(np.uint32)).any(1).sum()),
+            "oracle_status_nonzero": int((status != 0).sum()), "oracle_s": dt, "oracle_threads": cores,
+            "what": "rank 0's first output frames of one full-size step vs the CPU oracle's exact scan of all rows"}
 
 
 def streaming(device):
@@ -434,6 +470,187 @@ def training(device, cpu_threads: int):
     return out
 
 
+def _replay_latency(fn, s, reps, pre=None):
+    """Captures fn() into a CUDA graph on stream s, replays it 20 times, then
+    times `reps` replays with CUDA events on s; `pre` (an L2 flush, an input
+    reset) runs before each timed replay, outside the events.  Returns
+    (p50, p95, mean) in ms."""
+    import torch
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        fn()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            fn()
+        for _ in range(20):
+            graph.replay()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for a, b in ev:
+            if pre is not None:
+                pre()
+            a.record(s)
+            graph.replay()
+            b.record(s)
+    s.synchronize()
+    lat = sorted(a.elapsed_time(b) for a, b in ev)
+    del graph
+    return lat[len(lat) // 2], lat[int(len(lat) * 0.95)], sum(lat) / len(lat)
+
+
+L2_FLUSH_BYTES = 256 << 20  # written between timed replays: twice the 126 MB L2
+
+
+def _flat_roofline(q, n, d, kernel_s, peaks, peak_kind, flops_key="bf16_tflops"):
+    """Roofline of one flat candidate launch: 2*Q*N*d FLOP on the tensor pipe
+    against N*(2*d_pad + 4) bytes of streamed fp16 rows and fp32 norms; the
+    bound is whichever takes longer at the measured peaks."""
+    d_pad = (d + 63) // 64 * 64
+    flops = 2.0 * q * n * d
+    nbytes = float(n) * (2 * d_pad + 4)
+    tf = peaks.get(flops_key, 1590.0)
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    t_f, t_b = flops / (tf * 1e12), nbytes / (hbm * 1e9)
+    if t_f >= t_b:
+        ach = flops / kernel_s / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": tf, "unit": "TFLOP/s", "frac": ach / tf,
+                "peak_source": f"{peak_kind} {flops_key}", "algorithmic_flop": flops, "algorithmic_bytes": nbytes,
+                "bound_us": t_f * 1e6, "kernel_us": kernel_s * 1e6}
+    ach = nbytes / kernel_s / 1e9
+    return {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+            "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_flop": flops, "algorithmic_bytes": nbytes,
+            "bound_us": t_b * 1e6, "kernel_us": kernel_s * 1e6}
+
+
+def flat_config(device, key):
+    """c1 (20,000 x 768, 250 frames, ratio 0.75) or c2 (50,000 x 256, 1,000
+    frames, ratio 0.5): one out-of-place blend of the config's frames,
+    replayed from a CUDA graph.  `cold` overwrites a 256 MB buffer between
+    replays (outside the events), so the index (30.7 / 25.6 MB of fp16 rows)
+    is not left in L2 by the previous call; `warm` leaves it there, as back
+    to back realtime blocks would.  The roofline is the candidate kernel's
+    CUDA-event time over 20 eager calls (L2 flushed before each) against the
+    larger of the tensor and HBM bounds at the burst peaks (a kernel timed
+    on its own)."""
+    import torch
+
+    from vfr import GpuRetrievalIndex, synth
+
+    w = synth.CONFIGS[key]
+    arrays, queries = synth.make_torch(key, device)
+    idx = GpuRetrievalIndex.from_arrays(arrays["centroids"], arrays["offsets"], arrays["vectors"], arrays["ids"], 1,
+                                        max_frames=w.q)
+    del arrays
+    out = torch.empty_like(queries)
+    rate = torch.tensor([w.ratio], device=device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    s = torch.cuda.Stream()
+
+    def call():
+        idx.blend_from(queries, out, rate, stream=s)
+
+    cold = _replay_latency(call, s, 200, pre=lambda: flush.fill_(1.0))
+    warm = _replay_latency(call, s, 200)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        idx.profile(True)
+        for _ in range(20):
+            flush.fill_(1.0)
+            call()
+    s.synchronize()
+    prof = idx.profile(False)
+    diag = idx.diagnostics()
+    idx.close()
+    cand = prof["cand_kernel"]
+    cand_s = cand["ms"] / max(1, cand["launches"]) / 1000.0
+    peaks, peak_kind = measured_peaks()
+    roof = _flat_roofline(w.q, w.n, w.d, cand_s, peaks, peak_kind)
+    roof["kernel"] = "cand_kernel"
+    roof["call_frac_at_cold_p50"] = roof["bound_us"] / (cold[0] * 1000.0)
+    return {"workload": f"{w.key} {w.name}: flat N={w.n} x {w.d}, Q={w.q} frames per call, k=8, "
+                        f"index_rate={w.ratio}, graph replay (200 timed)",
+            "queries_per_s_cold_p50": w.q / (cold[0] / 1000.0), "cold_p50_ms": cold[0], "cold_p95_ms": cold[1],
+            "queries_per_s_warm_p50": w.q / (warm[0] / 1000.0), "warm_p50_ms": warm[0], "warm_p95_ms": warm[1],
+            "l2": f"cold: {L2_FLUSH_BYTES >> 20} MB written between replays; warm: index left L2-resident",
+            "kernels_ms": {k: v["ms"] / max(1, v["launches"]) for k, v in prof.items()},
+            "plan": diag["last_plan"], "fallback_frames": diag["fallback_frames"], "roofline": roof}
+
+
+def published_shape(device):
+    """Stand-in for the reference's only published timings of this path
+    (docs/faiss-gpu-retrieval.md:59-79: RTX 3060, a real IVF511,Flat
+    nprobe=1 index of 19,949 768-d vectors, ratio 0.5, CUDA-graph replay
+    medians 0.127 ms for 34 frames and 0.242 ms for 140): a seeded mixture
+    index of the same shape (511 lists from 20 k-means iterations), the same
+    block sizes and ratio, graph replay of vocal_faiss_gpu_blend with the
+    frames reset before each replay (outside the events), p50/p95 over 500
+    replays, for the default engine and the exact SIMT engine."""
+    import torch
+
+    from vfr import GpuRetrievalIndex, lib, synth
+
+    w = synth.CONFIGS["ivf511"]
+    arrays, queries = synth.make_torch("ivf511", device, q=max(w.extra["blocks"]))
+    rate = torch.tensor([w.ratio], device=device)
+    s = torch.cuda.Stream()
+    out = {"workload": f"IVF-Flat N={w.n} x {w.d}, nlist={w.nlist}, nprobe=1, ratio {w.ratio}; seeded stand-in "
+                       f"for the reference's published IVF511 index",
+           "reference_published_ms_p50": {"34": 0.127, "140": 0.242},
+           "reference_hardware": "RTX 3060 (docs/faiss-gpu-retrieval.md:69-72)"}
+    for name, engine in (("auto", lib.ENGINE_AUTO), ("exact", lib.ENGINE_EXACT)):
+        idx = GpuRetrievalIndex.from_arrays(arrays["centroids"], arrays["offsets"], arrays["vectors"], arrays["ids"],
+                                            1, engine=engine, max_frames=max(w.extra["blocks"]))
+        res = {}
+        for frames in w.extra["blocks"]:
+            src = queries[:frames].contiguous()
+            feats = src.clone()
+            p50, p95, mean = _replay_latency(lambda: idx.blend(feats, frames, rate, stream=s), s, 500,
+                                             pre=lambda: feats.copy_(src))
+            res[str(frames)] = {"p50_ms": p50, "p95_ms": p95, "mean_ms": mean}
+        res["fallback_frames"] = idx.diagnostics()["fallback_frames"]
+        out[name] = res
+        idx.close()
+    return out
+
+
+def _ivf_roofline(arrays, queries, nprobe, ms, peaks, peak_kind):
+    """c3 bounds from the lists the frames actually probe (coarse order
+    computed here in float64 with torch; a work count, not a parity claim):
+    FLOP = 2 d (Q nlist + sum over frames of the probed lists' rows); bytes =
+    the fp16 rows and fp32 norms of every list probed at least once, the
+    fp16 centroids, the fp32 frames read and written, and the fp32 rows of
+    each frame's 8 neighbours read by the blend.  The bound is the larger of
+    the two times at the measured sustained tensor and HBM peaks."""
+    import torch
+
+    c = arrays["centroids"].double()
+    q = queries.double()
+    sizes = (arrays["offsets"][1:] - arrays["offsets"][:-1]).long()
+    nq, d = queries.shape
+    nlist = c.shape[0]
+    probed = torch.empty((nq, nprobe), dtype=torch.long, device=queries.device)
+    cn = (c * c).sum(1)
+    for s0 in range(0, nq, 4096):
+        dq = cn[None, :] - 2.0 * q[s0:s0 + 4096] @ c.T
+        probed[s0:s0 + 4096] = dq.topk(nprobe, largest=False).indices
+    scanned = int(sizes[probed].sum().item())
+    touched = torch.zeros(nlist, dtype=torch.bool, device=queries.device)
+    touched[probed.flatten()] = True
+    d_pad = (d + 63) // 64 * 64
+    flops = 2.0 * d * (nq * nlist + scanned)
+    nbytes = (float(sizes[touched].sum().item()) * (2 * d_pad + 4) + nlist * d_pad * 2 + 2.0 * nq * d * 4
+              + nq * 8.0 * d * 4)
+    tf = peaks.get("bf16_tflops_sustained", 1400.0)
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    t_f, t_b = flops / (tf * 1e12), nbytes / (hbm * 1e9)
+    bound_s = max(t_f, t_b)
+    return {"bound": "tensor" if t_f >= t_b else "hbm", "rows_scanned": scanned,
+            "rows_scanned_per_frame": scanned / nq, "lists_touched": int(touched.sum().item()),
+            "algorithmic_flop": flops, "algorithmic_bytes": nbytes, "t_flop_us": t_f * 1e6, "t_bytes_us": t_b * 1e6,
+            "bound_us": bound_s * 1e6, "measured_us": ms * 1000.0, "frac": bound_s / (ms / 1000.0),
+            "peak_source": f"{peak_kind} bf16_tflops_sustained and hbm_gbs"}
+
+
 def ivf(device):
     """c3: IVF-Flat 200k x 768, nlist 256 (20 seeded k-means iterations), 30k
     frames, nprobe 1 and 8; frames/s of the blend (CUDA events)."""
@@ -466,6 +683,8 @@ def ivf(device):
                                   "exact_rerun_frames": diag["fallback_frames"] // 6,
                                   "certified_frames": diag["candidate_frames"] // 6}
         idx.close()
+        peaks, peak_kind = measured_peaks()
+        out[f"nprobe{nprobe}"]["roofline"] = _ivf_roofline(arrays, queries, nprobe, ms, peaks, peak_kind)
     return out
 
 
@@ -497,14 +716,15 @@ def main():
     arrays, queries = synth.make_torch(a.workload, device, n=n, q=q)
     lo, hi = shard_rows(n, world, rank)
     host_vectors = arrays["vectors"][lo:hi].cpu().numpy()
+    # rank 0 keeps every row on the host for the oracle (parity check and,
+    # at N=1, the CPU baseline)
     full_host = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        full_host = host_vectors
+    if rank == 0 and (not a.no_parity or (world == 1 and not a.no_cpu_baseline)):
+        full_host = host_vectors if world == 1 else arrays["vectors"].cpu().numpy()
     del arrays
     torch.cuda.empty_cache()
     ops = LibraryOps(host_vectors, label_base=lo, max_frames=q)
-    if full_host is None:
-        del host_vectors
+    del host_vectors
     rate = torch.tensor([w.ratio], device=device)
     out = torch.empty_like(queries)
     s = torch.cuda.Stream(device)
@@ -514,8 +734,8 @@ def main():
         if world == 1:
             ops.index.blend_from(queries, out, rate, stream=s)
             return 4  # prep_queries, cand_kernel, merge_kernel, exact_kernel
-        sharded_blend(ops, queries, rate, group, world, rank, stream=s)
-        return 7  # + merge_topk, gather_owned, blend_gathered
+        sharded_blend(ops, queries, rate, group, world, rank, stream=s, timeout_s=STEP_TIMEOUT_S)
+        return 7  # + merge_topk, gather_owned, blend_gathered_rows
 
     with torch.cuda.stream(s):
         for _ in range(a.warmup):
@@ -588,18 +808,24 @@ def main():
     # ---- e2e through the drop-in C ABI with pinned host buffers
     e2e = None
     if not a.no_e2e:
-        host_in = queries.cpu().pin_memory()
+        # each rank uploads its own share of the frames from pinned host
+        # memory and the shares are all-gathered over NVLink; each rank
+        # reads back the frames it blended
         m = q // world
-        host_out = torch.empty((m if world > 1 else q, w.d), dtype=torch.float32).pin_memory()
+        host_in = queries[rank * m:(rank + 1) * m].cpu().pin_memory()
+        host_out = torch.empty((m, w.d), dtype=torch.float32).pin_memory()
         feats = torch.empty_like(queries)
+        feats_local = torch.empty((m, w.d), dtype=torch.float32, device=device)
 
         def e2e_step():
-            feats.copy_(host_in, non_blocking=True)
             if world == 1:
+                feats.copy_(host_in, non_blocking=True)
                 ops.index.blend(feats, q, rate, stream=s)  # vocal_faiss_gpu_blend, in place
                 host_out.copy_(feats, non_blocking=True)
             else:
-                o, _, _ = sharded_blend(ops, feats, rate, group, world, rank, stream=s)
+                feats_local.copy_(host_in, non_blocking=True)
+                dist.all_gather_into_tensor(feats, feats_local, group=group)
+                o, _, _ = sharded_blend(ops, feats, rate, group, world, rank, stream=s, timeout_s=STEP_TIMEOUT_S)
                 host_out.copy_(o, non_blocking=True)
 
         with torch.cuda.stream(s):
@@ -618,8 +844,30 @@ def main():
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e = {"value": q * a.steps / (float(te.item()) / 1000.0), "unit": UNIT,
-               "h2d_bytes_per_step": int(host_in.numel() * 4), "d2h_bytes_per_step": int(host_out.numel() * 4),
-               "api": "vocal_faiss_gpu_blend" if world == 1 else "vfr_retrieval_search + NCCL + vfr_blend_gathered"}
+               "h2d_bytes_per_step": int(host_in.numel() * 4) * world,
+               "d2h_bytes_per_step": int(host_out.numel() * 4) * world,
+               "bytes": "summed over ranks (each rank copies its own share of the frames each way)",
+               "api": "vocal_faiss_gpu_blend" if world == 1 else
+               "NCCL all-gather of the frames + vfr_retrieval_search + NCCL top-8 all-gather + vfr_merge_topk + "
+               "NCCL all-to-all of owned winners + vfr_blend_gathered_rows"}
+
+    # ---- correctness beside the timed numbers: rank 0's first PARITY_FRAMES
+    # output frames of a full-size step (labels from the same step's search)
+    # against the oracle's exact scan of every row
+    parity_out = None
+    if not a.no_parity:
+        with torch.cuda.stream(s):
+            if world == 1:
+                ops.index.blend_from(queries, out, rate, stream=s)
+                pd, pl = ops.index.search(queries, k=8, stream=s)
+                mine = out
+            else:
+                mine, pd, pl = sharded_blend(ops, queries, rate, group, world, rank, stream=s,
+                                             timeout_s=STEP_TIMEOUT_S)
+        torch.cuda.synchronize()
+        if rank == 0:
+            f = min(PARITY_FRAMES, mine.shape[0])
+            parity_out = (mine[:f].cpu().numpy(), pd[:f].cpu().numpy(), pl[:f].cpu().numpy())
 
     diag = ops.index.diagnostics()
     extra = {}
@@ -631,9 +879,16 @@ def main():
             extra["ingest"] = ingest(device)
         if not a.no_training:
             extra["training"] = training(device, 0 if a.no_cpu_baseline else (os.cpu_count() or 1))
+    if rank == 0 and world == 1 and not a.no_configs and not a.no_streaming:
+        extra["c1"] = flat_config(device, "c1")
+        extra["c2"] = flat_config(device, "c2")
+        extra["published_shape"] = published_shape(device)
     cpu = None
-    if rank == 0 and world == 1 and full_host is not None:
+    if rank == 0 and world == 1 and full_host is not None and not a.no_cpu_baseline:
         cpu = cpu_baseline(full_host, queries.cpu().numpy(), w.ratio, n)
+    if parity_out is not None:
+        extra["parity"] = parity_check(full_host, queries[:parity_out[0].shape[0]].cpu().numpy(), *parity_out,
+                                       w.ratio, n)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -65,7 +65,7 @@ typedef struct VfrStream {
 /* Replaces vocal_faiss_gpu_create (crates/vocal-tensorrt/native/retrieval.cu:34-90).
  * Validates the normalised arrays (d in 1..4096, 0 < nprobe <= min(nlist, 32),
  * 0 < n <= INT32_MAX, payload sizes, monotone offsets covering n), copies them
- * to the current CUDA device and builds the derived device layout (bf16
+ * to the current CUDA device and builds the derived device layout (fp16
  * shadow, row norms, tensor-map descriptors). */
 VFR_API int vocal_faiss_gpu_create(int32_t dimensions, int32_t nlist, int32_t nprobe, size_t vector_count,
                            const float *centroids, size_t centroid_count, const int32_t *offsets,
@@ -289,8 +289,10 @@ VFR_API size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t len
  * an index with the tensor-core layout (flat, engine auto or tensor), at most
  * 256 frames per call and feature width up to 1024.  Its working memory is a
  * 5.3 MiB static device array that every GPU loading the library holds until
- * exit; the first call on a device looks up that array's address, so make it
- * before any stream capture.  All calls share the array: calls whose kernels
+ * exit; the first call on a device looks up that array's address, and the
+ * first launch of each kernel may load its code (which the driver can back
+ * with device memory), so make one warm-up call before any stream capture or
+ * deadline-bound use.  All calls share the array: calls whose kernels
  * overlap on the GPU race and must be serialised by the caller. */
 VFR_API int vfr_retrieval_blend_noalloc(VfrIndex *index, float *features, size_t frames, int32_t width,
                                         const float *index_rate, VfrStream *stream, char **error);
@@ -320,6 +322,15 @@ VFR_API int vfr_gather_owned(VfrIndex *index, const int64_t *labels, size_t fram
                      char **error);
 VFR_API int vfr_blend_gathered(const float *queries, float *out, const float *dist, const float *neighbours,
                        size_t frames, int32_t width, const float *index_rate, VfrStream *stream, char **error);
+/* vfr_blend_gathered over a compact buffer of gathered rows (rows
+ * [row_count][width], e.g. what an all-to-all of the owned winners
+ * delivered): slot (frame, k) reads row slot_rows[frame * 8 + k] (device
+ * i32 [frames][8]); slots past the frame's count are not read.  Same
+ * weights, blend and results as vfr_blend_gathered (the reference's
+ * crates/vocal-cpu/src/retrieval.rs:65-81). */
+VFR_API int vfr_blend_gathered_rows(const float *queries, float *out, const float *dist, const float *rows,
+                                    size_t row_count, const int32_t *slot_rows, size_t frames, int32_t width,
+                                    const float *index_rate, VfrStream *stream, char **error);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,6 @@ for p in (os.path.join(ROOT, "vocal-fast-rs_b200"), ROOT):
         sys.path.insert(0, p)
 
 GOLDEN = os.path.join(ROOT, "tests", "golden")
-REFERENCE = "/".join(["", "root", "reference"])  # present only in the build container
 
 
 def pytest_configure(config):

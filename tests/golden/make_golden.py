@@ -12,8 +12,7 @@ tests, so the fixtures pin the reader and the search semantics without FAISS:
   fixtures (crates/vocal-directml/tests/fixtures/README.md): centroids
   (0,0),(10,0),(20,0),(30,0); vectors (0,1),(0,2),(10,1),(10,2),(30,1),(30,2)
   added in that order; persisted nprobe 1 and 2.  tests/test_golden.py checks
-  these equal the reference's checked-in files byte for byte whenever the
-  reference tree is available (it is not on GPU machines).
+  that they hash (SHA-256) to the reference's checked-in files.
 
 Run: python tests/golden/make_golden.py
 """

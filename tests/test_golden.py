@@ -8,12 +8,13 @@ Reference tests restated here:
   crates/vocal-tensorrt/src/retrieval/tests.rs:8-13  buffer-capacity checks
 """
 import os
+import sys
 import struct
 
 import numpy as np
 import pytest
 
-from conftest import REFERENCE, golden
+from conftest import golden
 
 
 # ---------------------------------------------------------------- parser tests
@@ -186,14 +187,28 @@ def test_dml_fixture_expectations_on_oracle(oracle):
             assert abs(out[2, 0] - 30.0) < 2e-5
 
 
+# SHA-256 of the reference's checked-in DirectML fixtures
+# (crates/vocal-directml/tests/fixtures/ivf-small-probe{1,2}.index, 299 bytes
+# each); the committed golden files must hash to the same values.
+REFERENCE_FIXTURE_SHA256 = {
+    "ivf-small-probe1.index": "d700e66c191c80bc75ab7a22d9e0e31d145eec90e0af1f56f0b9f0e3314cacbd",
+    "ivf-small-probe2.index": "c7ffa837f091abf7e56a4f84b68bf1ee282adb4241ec3732276a9dc632bab550",
+}
+
+
 def test_reference_fixture_bytes():
-    """The committed fixtures equal the reference's checked-in files."""
-    ref = os.path.join(REFERENCE, "crates/vocal-directml/tests/fixtures")
-    if not os.path.isdir(ref):
-        pytest.skip("reference tree not mounted (only in the build container)")
-    for name in ("ivf-small-probe1.index", "ivf-small-probe2.index"):
-        with open(os.path.join(ref, name), "rb") as f:
-            assert f.read() == golden(name)
+    """The committed fixtures equal the reference's checked-in files (by
+    SHA-256), and this repository's FAISS writer regenerates them."""
+    import hashlib
+
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import make_golden
+
+    for name, digest in REFERENCE_FIXTURE_SHA256.items():
+        data = golden(name)
+        assert len(data) == 299
+        assert hashlib.sha256(data).hexdigest() == digest
+        assert make_golden.FIXTURES[name]() == data
 
 
 # ---------------------------------------------------------------- boundary checks

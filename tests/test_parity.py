@@ -264,6 +264,46 @@ def test_row_sharded_blocks_reproduce_single_index(cuda, oracle, engine):
     assert_blend_parity(expected, status, out.cpu().numpy(), q)
 
 
+def test_row_sharded_winner_exchange_on_one_gpu(cuda, oracle):
+    """The multi-GPU winner exchange emulated on one GPU with three row
+    shards: every shard packs the winners it owns by destination
+    (LibraryOps.gather_rows over the compact label list), the receive buffer
+    of each destination is assembled source by source as the all-to-all
+    delivers it, and vfr_blend_gathered_rows blends each destination's
+    frames through its slot -> row map; the concatenated output equals the
+    single-index blend bit for bit."""
+    import torch
+    from vfr.sharded import LibraryOps, _send_labels, _slot_rows, exchange_plan, shard_rows
+
+    ix, q, ratio = make_scaled("c1")
+    world = 3
+    q = q[:249]  # a multiple of the world size
+    m = q.shape[0] // world
+    bounds = [shard_rows(ix.n, world, r)[0] for r in range(world)] + [ix.n]
+    s = torch.cuda.Stream()
+    qd = torch.from_numpy(q).cuda()
+    rate = torch.tensor([ratio], device="cuda")
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        ops = [LibraryOps(ix.vectors[bounds[r]:bounds[r + 1]], bounds[r]) for r in range(world)]
+        results = [o.search(qd, s) for o in ops]
+        md, ml = ops[0].merge(torch.stack([r[0] for r in results]).contiguous(),
+                              torch.stack([r[1] for r in results]).contiguous(), s)
+        counts, owner = exchange_plan(ml, bounds, world, 0)
+        counts = counts.cpu().tolist()
+        sends = [o.gather_rows(_send_labels(ml, owner, r, sum(counts[r])), s) for r, o in enumerate(ops)]
+        outs = []
+        for t in range(world):
+            recv = torch.cat([sends[o][sum(counts[o][:t]):sum(counts[o][:t + 1])] for o in range(world)])
+            slots = _slot_rows(owner, t, m, world)
+            outs.append(ops[t].blend_rows(qd[t * m:(t + 1) * m], md[t * m:(t + 1) * m].contiguous(), recv, slots,
+                                          rate, s))
+        out = torch.cat(outs)
+    s.synchronize()
+    expected, status = oracle_index(oracle, ix).blend(q, ratio, threads=THREADS)
+    assert_blend_parity(expected, status, out.cpu().numpy(), q)
+
+
 @pytest.mark.parametrize("key", ["c1", "c3-np1", "c3-np8"])
 def test_tensor_core_stage_serves_the_frames(cuda, oracle, key):
     """The certified tensor-core stage (not the exact re-run) settles the

@@ -54,6 +54,76 @@ def test_noalloc_blend_matches_allocating_blend_twice(cuda):
         assert np.array_equal(o.view(np.uint32), e.view(np.uint32))
 
 
+def _two_calls_match(torch, L, g, q, rate, stream, splits):
+    """For each frame range in `splits` (two calls in a row): the allocating
+    blend and the no-allocation blend of the same frames agree bit for bit."""
+    for lo, hi in splits:
+        src = torch.from_numpy(np.ascontiguousarray(q[lo:hi])).cuda()
+        expected = src.clone()
+        got = src.clone()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            assert _call_blend(L.vocal_faiss_gpu_blend, g, expected, rate, stream) == (0, "")
+            assert _call_blend(L.vfr_retrieval_blend_noalloc, g, got, rate, stream) == (0, "")
+        stream.synchronize()
+        e, o = expected.cpu().numpy(), got.cpu().numpy()
+        assert not np.array_equal(e, q[lo:hi])
+        assert np.array_equal(o.view(np.uint32), e.view(np.uint32))
+    return g.diagnostics()["last_plan"]
+
+
+@pytest.mark.parametrize("rows,frames,keep,layout", [
+    (200_000, 256, 16, "full"),   # 16 candidates per list, 72 segments x 2 frame tiles
+    (340_000, 128, 16, "full"),   # exactly the 148-work-item cap: the key region is full
+    (340_000, 16, 16, "spread"),  # a small block (spread A layout) with long work items
+    (100_000, 32, 8, "spread"),   # a realtime block against c4's database size
+])
+def test_noalloc_blend_plans_at_the_scratch_limits(cuda, rows, frames, keep, layout):
+    torch = cuda
+    from vfr import GpuRetrievalIndex, lib, synth
+
+    L = lib.load_library()
+    arrays, q = synth.make_torch("c4", "cuda", n=rows, q=2 * frames)
+    g = GpuRetrievalIndex.from_arrays(arrays["centroids"], arrays["offsets"], arrays["vectors"], arrays["ids"], 1)
+    del arrays
+    q = q.cpu().numpy()
+    rate = torch.tensor([0.75], device="cuda")
+    stream = torch.cuda.Stream()
+    plan = _two_calls_match(torch, L, g, q, rate, stream, [(0, frames), (frames, 2 * frames)])
+    assert plan["keep"] == keep and plan["layout"] == layout, plan
+    if rows == 340_000 and frames == 128:
+        assert plan["segments"] == 148, plan
+    g.close()
+
+
+def test_noalloc_blend_allocates_no_device_memory(cuda):
+    """A fresh index that only ever sees the no-allocation entry point keeps
+    no workspace, and device free memory does not move across its calls
+    (after one warm-up call, which may load kernel code on first use)."""
+    torch = cuda
+    from vfr import GpuRetrievalIndex, lib, synth
+
+    L = lib.load_library()
+    ix, q = synth.make_np("c1", n=30_000, q=3 * 64)
+    g = GpuRetrievalIndex.from_arrays(ix.centroids, ix.offsets, ix.vectors, ix.ids, 1)
+    rate = torch.tensor([0.75], device="cuda")
+    stream = torch.cuda.Stream()
+    bufs = [torch.from_numpy(np.ascontiguousarray(q[i * 64:(i + 1) * 64])).cuda() for i in range(3)]
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        assert _call_blend(L.vfr_retrieval_blend_noalloc, g, bufs[0], rate, stream) == (0, "")
+    stream.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    with torch.cuda.stream(stream):
+        for b in bufs[1:]:
+            assert _call_blend(L.vfr_retrieval_blend_noalloc, g, b, rate, stream) == (0, "")
+    stream.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    diag = g.diagnostics()
+    assert diag["workspace_bytes"] == 0 and diag["workspace_frames"] == 0, diag
+    g.close()
+
+
 def test_noalloc_blend_rejects_what_it_cannot_hold(cuda):
     torch = cuda
     from vfr import GpuRetrievalIndex, lib, synth

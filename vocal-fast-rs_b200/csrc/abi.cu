@@ -499,12 +499,15 @@ extern "C" size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t 
                           "\"nprobe\":%d,\"vectors\":%lld,\"label_base\":%lld,\"device\":%d,\"workspace_frames\":%zu,"
                           "\"workspace_bytes\":%zu,\"empty_frames\":%llu,\"fallback_frames\":%llu,"
                           "\"candidate_frames\":%llu,\"timeouts\":%llu,\"max_row_norm\":%.9g,"
-                          "\"max_row_residual\":%.9g,\"shared_handles\":%ld}",
+                          "\"max_row_residual\":%.9g,\"shared_handles\":%ld,\"last_plan\":{\"keep\":%d,"
+                          "\"segments\":%d,\"tiles_per_segment\":%d,\"layout\":\"%s\"}}",
                           engine, index->have_tc ? "true" : "false", index->candidates, index->d, index->nlist,
                           index->nprobe, static_cast<long long>(index->n), static_cast<long long>(index->label_base),
                           index->device, index->ws.frames, index->ws.bytes, c.empty_frames, c.fallback_frames,
                           c.candidate_frames, c.timeouts, index->max_row_norm, index->max_row_residual,
-                          static_cast<long>(index->shared ? index->shared.use_count() : 0));
+                          static_cast<long>(index->shared ? index->shared.use_count() : 0), index->last_keep,
+                          index->last_segments, index->last_tiles_per_seg,
+                          index->last_layout < 0 ? "none" : index->last_layout == 0 ? "full" : "spread");
     size_t need = m > 0 ? static_cast<size_t>(m) : 0;
     if (json && length) {
         size_t w = std::min(need, length - 1);
@@ -733,6 +736,21 @@ extern "C" int vfr_blend_gathered(const float *queries, float *out, const float 
         require(frames <= static_cast<size_t>(INT32_MAX), "frame count exceeds CUDA grid limit");
         vfr::launch_blend_gathered(queries, out, dist, neighbours, static_cast<long long>(frames), width, index_rate,
                                    vfr::stream_of(stream));
+        vfr::cuda_check(cudaGetLastError());
+    });
+}
+
+extern "C" int vfr_blend_gathered_rows(const float *queries, float *out, const float *dist, const float *rows,
+                                       size_t row_count, const int32_t *slot_rows, size_t frames, int32_t width,
+                                       const float *index_rate, VfrStream *stream, char **error) {
+    return guarded(error, [&] {
+        require(queries && out && dist && slot_rows && index_rate && (rows || row_count == 0),
+                "invalid blend arguments");
+        require(width > 0 && width <= 4096, "invalid feature width");
+        require(frames <= static_cast<size_t>(INT32_MAX), "frame count exceeds CUDA grid limit");
+        require(row_count <= static_cast<size_t>(INT32_MAX), "gathered row count exceeds the slot index range");
+        vfr::launch_blend_gathered_rows(queries, out, dist, rows, slot_rows, static_cast<long long>(row_count),
+                                        static_cast<long long>(frames), width, index_rate, vfr::stream_of(stream));
         vfr::cuda_check(cudaGetLastError());
     });
 }

@@ -95,5 +95,8 @@ void launch_gather_owned(const float *vectors, const int32_t *row_of_id, int64_t
                          const int64_t *labels, long long frames, float *out, cudaStream_t stream);
 void launch_blend_gathered(const float *queries, float *out, const float *dist, const float *neighbours,
                            long long frames, int d, const float *index_rate, cudaStream_t stream);
+void launch_blend_gathered_rows(const float *queries, float *out, const float *dist, const float *rows_buf,
+                                const int32_t *slot_rows, long long rows, long long frames, int d,
+                                const float *index_rate, cudaStream_t stream);
 
 }  // namespace vfr

@@ -60,8 +60,12 @@ __global__ void gather_owned_kernel(const float *__restrict__ vectors, const int
     }
 }
 
+// neighbours: [frames][8][d] when slot_rows is null; otherwise [rows][d],
+// with slot (f, k) reading row slot_rows[f * 8 + k] (rows outside [0, rows)
+// read as zero; the host never produces them for a valid slot).
 __global__ void blend_gathered_kernel(const float *__restrict__ queries, float *out, const float *__restrict__ dist,
-                                      const float *__restrict__ neighbours, int d, const float *index_rate) {
+                                      const float *__restrict__ neighbours, const int32_t *__restrict__ slot_rows,
+                                      long long rows, int d, const float *index_rate) {
     __shared__ double weights[8];
     __shared__ double weight_sum;
     __shared__ int count_s;
@@ -91,11 +95,20 @@ __global__ void blend_gathered_kernel(const float *__restrict__ queries, float *
     double w[8];
     for (int k = 0; k < 8; ++k) w[k] = weights[k];
     const WeightDivisor sum = weight_divisor(weight_sum);
-    const float *nb = neighbours + f * 8 * static_cast<long long>(d);
+    const float *nb[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        long long row = f * 8 + k;
+        if (slot_rows != nullptr) {
+            const int32_t r = slot_rows[f * 8 + k];
+            row = (r >= 0 && r < rows) ? r : -1;
+        }
+        nb[k] = (k < count && row >= 0) ? neighbours + row * static_cast<long long>(d) : nullptr;
+    }
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
         float v[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = k < count ? nb[static_cast<long long>(k) * d + i] : 0.f;
+        for (int k = 0; k < 8; ++k) v[k] = nb[k] != nullptr ? nb[k][i] : 0.f;
         dst[i] = reference_blend_element(src[i], v, w, sum, count, ratio);
     }
 }
@@ -120,8 +133,16 @@ void launch_gather_owned(const float *vectors, const int32_t *row_of_id, int64_t
 void launch_blend_gathered(const float *queries, float *out, const float *dist, const float *neighbours,
                            long long frames, int d, const float *index_rate, cudaStream_t stream) {
     if (frames <= 0) return;
-    blend_gathered_kernel<<<static_cast<unsigned>(frames), 256, 0, stream>>>(queries, out, dist, neighbours, d,
-                                                                             index_rate);
+    blend_gathered_kernel<<<static_cast<unsigned>(frames), 256, 0, stream>>>(queries, out, dist, neighbours, nullptr,
+                                                                             0, d, index_rate);
+}
+
+void launch_blend_gathered_rows(const float *queries, float *out, const float *dist, const float *rows_buf,
+                                const int32_t *slot_rows, long long rows, long long frames, int d,
+                                const float *index_rate, cudaStream_t stream) {
+    if (frames <= 0) return;
+    blend_gathered_kernel<<<static_cast<unsigned>(frames), 256, 0, stream>>>(queries, out, dist, rows_buf, slot_rows,
+                                                                             rows, d, index_rate);
 }
 
 }  // namespace vfr

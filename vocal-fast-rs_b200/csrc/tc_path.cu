@@ -1481,6 +1481,14 @@ Plan make_plan(size_t frames, int64_t n, int sms) {
     return p;
 }
 
+// Records a flat call's plan in the index (reported by diagnostics).
+void note_plan(VfrIndex *ix, const Plan &p, size_t frames) {
+    ix->last_keep = p.tiles_per_seg <= kShortItemTiles ? kShortKeep : kIvfKeep;
+    ix->last_segments = p.segments;
+    ix->last_tiles_per_seg = p.tiles_per_seg;
+    ix->last_layout = frames <= static_cast<size_t>(kSmallBlock) ? kSpreadLayout : kFullLayout;
+}
+
 int64_t items_cap(size_t frames, int sms) {
     const int64_t qt = static_cast<int64_t>((frames + kTileM - 1) / kTileM);
     return std::max<int64_t>(qt * 16, static_cast<int64_t>(sms) * 8);
@@ -2169,6 +2177,10 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
 
     // 2. coarse candidates over the centroids
     const Plan pc = make_plan(frames, ix->nlist, ix->sm_count);
+    ix->last_keep = kIvfKeep;
+    ix->last_segments = pc.segments;
+    ix->last_tiles_per_seg = pc.tiles_per_seg;
+    ix->last_layout = kFullLayout;
     CUtensorMap tmap_q;
     encode_rows(&tmap_q, q16, ix->d_pad, frames, kTileM);
     CandArgs ca{};
@@ -2378,6 +2390,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
     const int grid = std::min(items, ix->sm_count);
+    note_plan(ix, p, frames);
     ix->prof.begin(kProfCand, stream);
     launch_cand_flat(p, grid, q16, ix->d_pad, ix->tmap_vectors, ca, stream);
     ix->prof.end(stream);
@@ -2546,6 +2559,7 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
     const int items = p.segments * p.n_qtiles;
+    note_plan(ix, p, frames);
     launch_cand_flat(p, std::min(items, ix->sm_count), q16, ix->d_pad, ix->tmap_vectors, ca, stream);
 
     MergeArgs ma{};

@@ -1,4 +1,4 @@
-// Tensor-core engine: bf16 shadow of the database, tcgen05/TMEM distance GEMM
+// Tensor-core engine: fp16 shadow of the database, tcgen05/TMEM distance GEMM
 // with fused per-frame candidate selection, exact fp32 re-rank and blend.
 #pragma once
 

@@ -167,6 +167,10 @@ struct VfrIndex {
     // frames share its grid (ExactArgs::split_keys / split_done).
     unsigned long long *split_keys = nullptr;
     int32_t *split_done = nullptr;
+    // Plan of the last tensor-core call on the host (diagnostics): candidate
+    // list size per (work item, frame), database segments, tiles per
+    // segment, and the A-tile layout (0 full, 1 spread, -1 no call yet).
+    int32_t last_keep = 0, last_segments = 0, last_tiles_per_seg = 0, last_layout = -1;
 };
 
 namespace vfr {

@@ -291,3 +291,12 @@ def blend_gathered(queries, out, dist, neighbours, index_rate, stream=None) -> N
     s = stream_struct(stream)
     call(L.vfr_blend_gathered, _ptr(queries), _ptr(out), _ptr(dist), _ptr(neighbours), queries.shape[0],
          queries.shape[1], _ptr(index_rate), ctypes.byref(s))
+
+
+def blend_gathered_rows(queries, out, dist, rows, slot_rows, index_rate, stream=None) -> None:
+    """vfr_blend_gathered over a compact row buffer: slot (f, k) reads
+    rows[slot_rows[f, k]] (int32 CUDA tensor [frames, 8])."""
+    L = load_library()
+    s = stream_struct(stream)
+    call(L.vfr_blend_gathered_rows, _ptr(queries), _ptr(out), _ptr(dist), _ptr(rows) if rows.numel() else 0,
+         rows.shape[0], _ptr(slot_rows), queries.shape[0], queries.shape[1], _ptr(index_rate), ctypes.byref(s))

@@ -99,6 +99,7 @@ def load_library(path: str | None = None):
         "vfr_merge_topk": ([vp, vp, i32, sz, vp, vp, P(Stream), err], ctypes.c_int),
         "vfr_gather_owned": ([vp, vp, sz, vp, P(Stream), err], ctypes.c_int),
         "vfr_blend_gathered": ([vp, vp, vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
+        "vfr_blend_gathered_rows": ([vp, vp, vp, vp, sz, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

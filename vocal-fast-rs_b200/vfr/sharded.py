@@ -9,17 +9,26 @@ For a batch of Q frames (replicated on every rank) one step is:
   2. all-gather of the G per-shard top-8 lists (NCCL, 12 B per entry);
   3. k-way merge by (distance, global row) -> the single-index top-8, which is
      the reference's scan order for a flat index (`vfr_merge_topk`);
-  4. each rank writes the winning vectors it owns, -0.0 elsewhere
-     (`vfr_gather_owned`), and a reduce-scatter (sum) hands rank r the exact
-     fp32 neighbour vectors of its Q/G frames (x + -0.0 == x bit for bit);
-  5. the reference's f64 weights + f32 blend for those frames
-     (`vfr_blend_gathered`).
+  4. the winners' vectors go to the rank that blends their frame: every rank
+     knows the merged labels, hence who owns each winner and who needs it,
+     so each rank packs only the winners it owns, grouped by destination
+     (`vfr_gather_owned` on the compact label list), and one all-to-all with
+     those uneven splits delivers them (Q*8*d*4 bytes over all ranks, each
+     vector sent once; a rank keeps its own);
+  5. the reference's f64 weights + f32 blend for the rank's Q/G frames, each
+     slot reading its vector from the receive buffer through a slot -> row
+     map (`vfr_blend_gathered_rows`).
 
 Frames are therefore blended exactly as by a single index; the output of
 rank r is frames [r*Q/G, (r+1)*Q/G).  The reference is single-GPU; this is the
 multi-GPU extension of its path.  Collectives are taken in the same order on
-every rank.  `ops` selects the per-rank compute: `LibraryOps` (CUDA library,
-the product) or a test double with the same interface.
+every rank.  The split sizes of step 4 come to the host once per step (a
+G x G count matrix); that copy is the step's one host wait, and with a
+`timeout_s` it is a bounded poll: if a peer never joins the collectives
+before it, the process group is aborted and `ShardTimeout` is raised instead
+of waiting forever (the all-to-all is then awaited against the same deadline).
+`ops` selects the per-rank compute: `LibraryOps` (CUDA library, the product)
+or a test double with the same interface.
 
 Query sharding (`query_sharded_blend`) is the other mode, for large offline
 batches against an index that fits one GPU (c3): every rank holds a full
@@ -28,10 +37,18 @@ needed unless every rank wants the whole output (`gather=True`).
 """
 from __future__ import annotations
 
+import contextlib
+import time
+
 import numpy as np
 
 from . import lib as _l
-from .index import GpuRetrievalIndex, blend_gathered, merge_topk
+from .index import GpuRetrievalIndex, blend_gathered_rows, merge_topk
+
+
+class ShardTimeout(RuntimeError):
+    """A peer rank did not take part in a collective before the deadline;
+    the process group has been aborted."""
 
 
 def shard_rows(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -52,6 +69,8 @@ class LibraryOps:
             np.zeros((1, d), np.float32), np.array([0, n_local], np.int32), vectors_slice,
             np.arange(n_local, dtype=np.int32), 1, engine=engine, label_base=label_base, max_frames=max_frames)
         self.d = d
+        self.label_base = label_base
+        self.rows = n_local
 
     def search(self, q, stream):
         return self.index.search(q, k=8, stream=stream)
@@ -64,65 +83,187 @@ class LibraryOps:
         merge_topk(dists, labels, md, ml, stream=stream)
         return md, ml
 
-    def gather_owned(self, labels, stream):
+    def gather_rows(self, labels, stream):
+        """[L, d] fp32 vectors of the (owned, global) labels [L], in order."""
         import torch
 
-        out = torch.empty((labels.shape[0], 8, self.d), dtype=torch.float32, device=labels.device)
-        self.index.gather_owned(labels, out, stream=stream)
-        return out
+        count = labels.shape[0]
+        padded = (count + 7) // 8 * 8
+        lab = torch.full((padded,), -1, dtype=torch.int64, device=labels.device)
+        lab[:count] = labels
+        out = torch.empty((padded, self.d), dtype=torch.float32, device=labels.device)
+        if padded:
+            self.index.gather_owned(lab.view(-1, 8), out.view(-1, 8, self.d), stream=stream)
+        return out[:count]
 
-    def blend(self, q, dist, neighbours, rate, stream):
+    def blend_rows(self, q, dist, rows, slot_rows, rate, stream):
         import torch
 
         out = torch.empty_like(q)
-        blend_gathered(q, out, dist, neighbours, rate, stream=stream)
+        blend_gathered_rows(q, out, dist, rows, slot_rows, rate, stream=stream)
         return out
 
 
-def _all_gather(t, group, world):
+def _stream_ctx(stream):
+    """Runs the torch ops of a step on `stream` (a CUDA stream) so they are
+    ordered with the library calls made on it; no-op for CPU tensors."""
+    if stream is None:
+        return contextlib.nullcontext()
+    import torch
+
+    return torch.cuda.stream(stream)
+
+
+def _abort(group):
+    import torch.distributed as dist
+
+    try:
+        dist.distributed_c10d._abort_process_group(group)
+    except Exception:  # noqa: BLE001 - best effort: the caller raises ShardTimeout either way
+        pass
+
+
+def _poll(done, deadline, group, what):
+    """Spins on `done()` (a CUDA event query or a collective's completion)
+    until it holds or the deadline passes; then aborts the group and raises.
+    Busy for the first millisecond, so a wait that ends soon costs
+    microseconds, then in 50 us sleeps."""
+    spin_until = time.monotonic() + 1e-3
+    while not done():
+        now = time.monotonic()
+        if now > deadline:
+            _abort(group)
+            raise ShardTimeout(f"{what}: a peer rank did not join before the deadline; process group aborted")
+        if now > spin_until:
+            time.sleep(5e-5)
+
+
+def _all_gather(t, group, world, deadline=None, what="all-gather"):
     import torch
     import torch.distributed as dist
 
     if dist.get_backend(group) == "nccl":
         out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(out, t.contiguous(), group=group)
-        return out
-    parts = [torch.empty_like(t) for _ in range(world)]
-    dist.all_gather(parts, t.contiguous(), group=group)
-    return torch.stack(parts)
+        work = dist.all_gather_into_tensor(out, t.contiguous(), group=group, async_op=deadline is not None)
+    else:
+        parts = [torch.empty_like(t) for _ in range(world)]
+        work = dist.all_gather(parts, t.contiguous(), group=group, async_op=deadline is not None)
+    if deadline is not None:
+        _poll(work.is_completed, deadline, group, what)
+        work.wait()
+    return out if dist.get_backend(group) == "nccl" else torch.stack(parts)
 
 
-def _reduce_scatter_sum(t, group, world, rank):
-    """Sum over ranks of t [world*m, ...], returning this rank's m rows."""
+def _bounds(ops, group, world, deadline=None):
+    """Global row bounds [G+1] of the shards (gathered once, cached on ops)."""
     import torch
     import torch.distributed as dist
 
-    m = t.shape[0] // world
-    if dist.get_backend(group) == "nccl":
-        out = torch.empty((m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
-        dist.reduce_scatter_tensor(out, t.contiguous(), op=dist.ReduceOp.SUM, group=group)
-        return out
-    full = t.clone()
-    dist.all_reduce(full, op=dist.ReduceOp.SUM, group=group)
-    return full[rank * m:(rank + 1) * m].clone()
+    b = getattr(ops, "_shard_bounds", None)
+    if b is None:
+        mine = torch.tensor([ops.label_base, ops.label_base + ops.rows], dtype=torch.int64)
+        if dist.get_backend(group) == "nccl":
+            mine = mine.cuda()
+        spans = _all_gather(mine, group, world, deadline, "row-shard bounds").cpu()
+        b = [int(spans[0, 0])] + [int(spans[r, 1]) for r in range(world)]
+        if any(int(spans[r, 0]) != b[r] for r in range(world)):
+            raise ValueError("row shards must be contiguous and in rank order")
+        ops._shard_bounds = b
+    return b
 
 
-def sharded_blend(ops, queries, rate, group, world: int, rank: int, stream=None):
+def exchange_plan(ml, bounds, world: int, rank: int):
+    """Who sends which winner where, from the merged labels ml [Q, 8]
+    (identical on every rank).  Entry e = f*8 + k belongs to destination
+    rank f // (Q/G) and is owned by the shard whose rows hold ml[f, k].
+    Returns (counts [G, G] int64 on ml's device: counts[o, t] entries owned
+    by o for destination t; owner [Q*8] with G for empty slots)."""
+    import torch
+
+    q = ml.shape[0]
+    m = q // world
+    flat = ml.reshape(-1)
+    inner = torch.tensor(bounds[1:-1], dtype=torch.int64, device=ml.device)
+    owner = torch.searchsorted(inner, flat, right=True)
+    owner = torch.where(flat >= 0, owner, torch.full_like(owner, world))
+    dest = torch.arange(flat.numel(), device=ml.device) // (8 * m)
+    key = torch.where(owner < world, owner * world + dest, torch.full_like(owner, world * world))
+    counts = torch.bincount(key, minlength=world * world + 1)[: world * world].view(world, world)
+    return counts, owner
+
+
+def _send_labels(ml, owner, rank, total):
+    """The labels this rank owns, in entry order (destination-major),
+    without a host-side mask (the count is already known)."""
+    import torch
+
+    flat = ml.reshape(-1)
+    own = owner == rank
+    pos = torch.cumsum(own.to(torch.int64), 0) - 1
+    tgt = torch.where(own, pos, torch.full_like(pos, total))
+    idx = torch.zeros(total + 1, dtype=torch.int64, device=ml.device)
+    idx.scatter_(0, tgt, torch.arange(flat.numel(), device=ml.device))
+    return flat[idx[:total]]
+
+
+def _slot_rows(owner, rank, m, world):
+    """Receive-buffer row of every slot of this rank's frames: the buffer
+    holds, source by source, that source's entries in entry order, which is
+    the stable order of the owners; empty slots get -1."""
+    import torch
+
+    share = owner[rank * m * 8:(rank + 1) * m * 8]
+    perm = torch.sort(share, stable=True).indices
+    pos = torch.empty_like(perm)
+    pos[perm] = torch.arange(perm.numel(), device=owner.device)
+    pos = torch.where(share < world, pos, torch.full_like(pos, -1))
+    return pos.to(torch.int32).view(m, 8)
+
+
+def sharded_blend(ops, queries, rate, group, world: int, rank: int, stream=None, timeout_s: float | None = None):
     """One row-sharded step for `queries` [Q, d] (Q a multiple of world, the
     same tensor on every rank).  Returns (this rank's blended frames
-    [Q/world, d], merged distances [Q, 8], merged labels [Q, 8])."""
+    [Q/world, d], merged distances [Q, 8], merged labels [Q, 8]).  With
+    `timeout_s`, the step's host waits are bounded (ShardTimeout)."""
+    import torch
+    import torch.distributed as dist
+
     q = queries.shape[0]
     if q % world:
         raise ValueError("frame count must be a multiple of the world size; pad with padded_frames()")
-    d8, l8 = ops.search(queries, stream)
-    dists = _all_gather(d8, group, world)
-    labels = _all_gather(l8, group, world)
-    md, ml = ops.merge(dists, labels, stream)
-    owned = ops.gather_owned(ml, stream)
-    mine = _reduce_scatter_sum(owned, group, world, rank)
+    deadline = time.monotonic() + timeout_s if timeout_s is not None else None
     m = q // world
     lo = rank * m
-    out = ops.blend(queries[lo:lo + m], md[lo:lo + m].contiguous(), mine, rate, stream)
+    with _stream_ctx(stream):
+        bounds = _bounds(ops, group, world, deadline)
+        d8, l8 = ops.search(queries, stream)
+        # on NCCL the two gathers are only enqueued here: the bounded wait for
+        # the count matrix below covers them
+        gloo_deadline = deadline if dist.get_backend(group) != "nccl" else None
+        dists = _all_gather(d8, group, world, gloo_deadline, "top-8 distance all-gather")
+        labels = _all_gather(l8, group, world, gloo_deadline, "top-8 label all-gather")
+        md, ml = ops.merge(dists, labels, stream)
+        counts_dev, owner = exchange_plan(ml, bounds, world, rank)
+        if deadline is not None and counts_dev.is_cuda:
+            host = torch.empty(counts_dev.shape, dtype=counts_dev.dtype, pin_memory=True)
+            host.copy_(counts_dev, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            _poll(ev.query, deadline, group, "row-sharded top-8 exchange")
+            counts = host.tolist()
+        else:
+            counts = counts_dev.cpu().tolist()
+        send_n = counts[rank]
+        recv_n = [counts[o][rank] for o in range(world)]
+        send = ops.gather_rows(_send_labels(ml, owner, rank, sum(send_n)), stream)
+        recv = torch.empty((sum(recv_n), queries.shape[1]), dtype=torch.float32, device=queries.device)
+        work = dist.all_to_all_single(recv, send.contiguous(), recv_n, send_n, group=group,
+                                      async_op=deadline is not None)
+        if deadline is not None:
+            _poll(work.is_completed, deadline, group, "row-sharded winner exchange")
+            work.wait()
+        slots = _slot_rows(owner, rank, m, world)
+        out = ops.blend_rows(queries[lo:lo + m], md[lo:lo + m].contiguous(), recv, slots, rate, stream)
     return out, md, ml
 
 

@@ -39,13 +39,23 @@ CONFIGS = {
                    kmeans_iters=20),
     "c4": Workload("c4", "rvc-v2-stream-100k", 100_000, 768, 32, 512, 0.75, blocks=1_000, walk=0.05),
     "c5": Workload("c5", "rvc-v2-flat-4m", 4_000_000, 768, 30_000, 4_096, 0.75),
+    # Stand-in for the one shape the reference publishes timings on
+    # (docs/faiss-gpu-retrieval.md:59-79: a real IVF511,Flat nprobe=1 index of
+    # 19,949 768-d vectors, blocks of 34 and 140 frames, ratio 0.5): seeded
+    # mixture rows, 511 lists from 20 seeded k-means iterations.
+    "ivf511": Workload("ivf511", "rvc-v2-ivf511-20k", 19_949, 768, 140, 256, 0.5, nlist=511, nprobe=(1,),
+                       kmeans_iters=20, extra={"blocks": (34, 140)}),
 }
+
+_SEEDS = {"ivf511": (1511, 2511, 3511)}
 
 SIGMA = 0.3
 QUERY_NOISE = 0.1
 
 
 def seeds(key: str):
+    if key in _SEEDS:
+        return _SEEDS[key]
     c = int(key[1:])
     return 1000 + c, 2000 + c, 3000 + c
 
