@@ -38,7 +38,7 @@ def _worker(rank, world, port, vectors, queries, ratio, results):
     s = torch.cuda.Stream(dev)
     torch.cuda.synchronize()
     with torch.cuda.stream(s):
-        out, md, ml = sharded_blend(ops, q, rate, dist.group.WORLD, world, rank, stream=s)
+        out, md, ml = sharded_blend(ops, q, rate, dist.group.WORLD, world, rank, stream=s, timeout_s=60.0)
     s.synchronize()
     results[rank] = (out.cpu().numpy(), md.cpu().numpy(), ml.cpu().numpy())
     dist.barrier()
