@@ -735,7 +735,7 @@ def main():
             ops.index.blend_from(queries, out, rate, stream=s)
             return 4  # prep_queries, cand_kernel, merge_kernel, exact_kernel
         sharded_blend(ops, queries, rate, group, world, rank, stream=s, timeout_s=STEP_TIMEOUT_S)
-        return 7  # + merge_topk, gather_owned, blend_gathered_rows
+        return 6  # + merge_topk, blend_peer
 
     with torch.cuda.stream(s):
         for _ in range(a.warmup):
@@ -849,7 +849,7 @@ def main():
                "bytes": "summed over ranks (each rank copies its own share of the frames each way)",
                "api": "vocal_faiss_gpu_blend" if world == 1 else
                "NCCL all-gather of the frames + vfr_retrieval_search + NCCL top-8 all-gather + vfr_merge_topk + "
-               "NCCL all-to-all of owned winners + vfr_blend_gathered_rows"}
+               "vfr_blend_peer (winners read from their owner GPU over NVLink)"}
 
     # ---- correctness beside the timed numbers: rank 0's first PARITY_FRAMES
     # output frames of a full-size step (labels from the same step's search)
@@ -890,6 +890,7 @@ def main():
         extra["parity"] = parity_check(full_host, queries[:parity_out[0].shape[0]].cpu().numpy(), *parity_out,
                                        w.ratio, n)
     if world > 1:
+        ops.close(group)  # peer mappings released on every rank before any rank frees its rows
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:

@@ -332,6 +332,44 @@ VFR_API int vfr_blend_gathered_rows(const float *queries, float *out, const floa
                                     size_t row_count, const int32_t *slot_rows, size_t frames, int32_t width,
                                     const float *index_rate, VfrStream *stream, char **error);
 
+/* Row-sharded blend over peer memory (one process per GPU of a node).
+ * After the merge every rank knows the global labels of its frames'
+ * winners; instead of exchanging the winners' rows with a collective, each
+ * rank maps the other shards' fp32 row arrays (CUDA IPC) once, and
+ * vfr_blend_peer reads every winner straight from the GPU that owns it
+ * (plain loads over NVLink; no bulk or tensor copies of peer memory).  No
+ * counterpart in the reference, which is single-GPU; the arithmetic is the
+ * reference's blend (crates/vocal-cpu/src/retrieval.rs:65-81).
+ *
+ * vfr_index_ipc_export: the descriptor of this shard (its rows' IPC handle,
+ *   label_base, row count, width) for the other ranks; flat indexes only.
+ * vfr_peer_rows_open: maps the shards described by descs[0 .. shards) (in
+ *   label order, contiguous; descs[self] describes `local`).  Close every
+ *   mapping (vfr_peer_rows_close) on every rank before any rank destroys its
+ *   index, with the devices idle (e.g. synchronise, barrier, close,
+ *   barrier).
+ * vfr_blend_peer: queries/out [frames][width] (this rank's frames), dist
+ *   [frames][8] and labels [frames][8] their merged top-8 (vfr_merge_topk);
+ *   the same results as vfr_blend_gathered on the gathered vectors. */
+typedef struct VfrPeerRows VfrPeerRows;
+typedef struct VfrIpcRows {
+    uint8_t rows_handle[64]; /* cudaIpcMemHandle_t of the fp32 rows */
+    uint8_t ids_handle[64];  /* of the label -> row map, when has_ids */
+    int64_t label_base;
+    int64_t rows;
+    int32_t width;
+    int32_t has_ids;
+    int32_t device;
+    int32_t reserved;
+} VfrIpcRows;
+VFR_API int vfr_index_ipc_export(VfrIndex *index, VfrIpcRows *out, char **error);
+VFR_API int vfr_peer_rows_open(VfrIndex *local, int32_t shards, const VfrIpcRows *descs, int32_t self,
+                               VfrPeerRows **out, char **error);
+VFR_API void vfr_peer_rows_close(VfrPeerRows *peers);
+VFR_API int vfr_blend_peer(VfrPeerRows *peers, const float *queries, float *out, const float *dist,
+                           const int64_t *labels, size_t frames, int32_t width, const float *index_rate,
+                           VfrStream *stream, char **error);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,7 +17,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, vectors, queries, ratio, results):
+def _worker(rank, world, port, vectors, queries, ratio, results, exchange="auto"):
     import datetime
     import sys
 
@@ -38,14 +38,22 @@ def _worker(rank, world, port, vectors, queries, ratio, results):
     s = torch.cuda.Stream(dev)
     torch.cuda.synchronize()
     with torch.cuda.stream(s):
-        out, md, ml = sharded_blend(ops, q, rate, dist.group.WORLD, world, rank, stream=s, timeout_s=60.0)
+        out, md, ml = sharded_blend(ops, q, rate, dist.group.WORLD, world, rank, stream=s, timeout_s=60.0,
+                                    exchange=exchange)
+        # a second step with other frames through the same (already open) exchange
+        out2, _, _ = sharded_blend(ops, q.flip(0).contiguous(), rate, dist.group.WORLD, world, rank, stream=s,
+                                   timeout_s=60.0, exchange=exchange)
     s.synchronize()
-    results[rank] = (out.cpu().numpy(), md.cpu().numpy(), ml.cpu().numpy())
+    results[rank] = (out.cpu().numpy(), md.cpu().numpy(), ml.cpu().numpy(), out2.cpu().numpy())
+    ops.close(dist.group.WORLD)  # peer mappings released on every rank before any index is freed
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_two_gpu_row_sharded_blend_matches_oracle(oracle):
+@pytest.mark.parametrize("exchange", ["peer", "all_to_all"])
+def test_two_gpu_row_sharded_blend_matches_oracle(oracle, exchange):
+    """Both winner exchanges: rows read from the owner GPU inside the blend
+    kernel (peer), and packed rows sent with an NCCL all-to-all."""
     import torch
     import torch.multiprocessing as mp
 
@@ -60,7 +68,8 @@ def test_two_gpu_row_sharded_blend_matches_oracle(oracle):
     ctx = mp.get_context("spawn")
     results = ctx.Manager().dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, ix.vectors, q, ratio, results)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, ix.vectors, q, ratio, results, exchange))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -76,6 +85,9 @@ def test_two_gpu_row_sharded_blend_matches_oracle(oracle):
         assert np.array_equal(results[r][2], labels)
         assert np.array_equal(results[r][1].view(np.uint32), dist.view(np.uint32))
     assert labels[5, 0] == 11 and labels[5, 1] == 19_999
+    expected2, _ = orc.blend(q[::-1].copy(), ratio, threads=os.cpu_count() or 1)
+    got2 = np.concatenate([results[r][3] for r in range(2)])
+    assert np.array_equal(got2.view(np.uint32), expected2.view(np.uint32))
 
 
 def _query_worker(rank, world, port, arrays, queries, ratio, results):

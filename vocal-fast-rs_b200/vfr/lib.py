@@ -45,6 +45,20 @@ class Stream(ctypes.Structure):
     _fields_ = [("stream", ctypes.c_void_p)]
 
 
+class IpcRows(ctypes.Structure):
+    """VfrIpcRows: one shard's row storage as other processes map it."""
+    _fields_ = [
+        ("rows_handle", ctypes.c_uint8 * 64),
+        ("ids_handle", ctypes.c_uint8 * 64),
+        ("label_base", ctypes.c_int64),
+        ("rows", ctypes.c_int64),
+        ("width", ctypes.c_int32),
+        ("has_ids", ctypes.c_int32),
+        ("device", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
 def declared_symbols() -> list[str]:
     """Function names declared in include/vfr_retrieval.h."""
     text = open(HEADER).read()
@@ -100,6 +114,10 @@ def load_library(path: str | None = None):
         "vfr_gather_owned": ([vp, vp, sz, vp, P(Stream), err], ctypes.c_int),
         "vfr_blend_gathered": ([vp, vp, vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
         "vfr_blend_gathered_rows": ([vp, vp, vp, vp, sz, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
+        "vfr_index_ipc_export": ([vp, P(IpcRows), err], ctypes.c_int),
+        "vfr_peer_rows_open": ([vp, i32, P(IpcRows), i32, P(vp), err], ctypes.c_int),
+        "vfr_peer_rows_close": ([vp], None),
+        "vfr_blend_peer": ([vp, vp, vp, vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -9,24 +9,25 @@ For a batch of Q frames (replicated on every rank) one step is:
   2. all-gather of the G per-shard top-8 lists (NCCL, 12 B per entry);
   3. k-way merge by (distance, global row) -> the single-index top-8, which is
      the reference's scan order for a flat index (`vfr_merge_topk`);
-  4. the winners' vectors go to the rank that blends their frame: every rank
-     knows the merged labels, hence who owns each winner and who needs it,
-     so each rank packs only the winners it owns, grouped by destination
-     (`vfr_gather_owned` on the compact label list), and one all-to-all with
-     those uneven splits delivers them (Q*8*d*4 bytes over all ranks, each
-     vector sent once; a rank keeps its own);
-  5. the reference's f64 weights + f32 blend for the rank's Q/G frames, each
-     slot reading its vector from the receive buffer through a slot -> row
-     map (`vfr_blend_gathered_rows`).
+  4. the reference's f64 weights + f32 blend of the rank's Q/G frames, with
+     the winners' fp32 rows read where they live.  Default (NCCL groups, the
+     GPUs of one node): every rank has mapped the other shards' row arrays
+     once (CUDA IPC) and `vfr_blend_peer` loads each winner from its owner's
+     HBM over NVLink inside the blend kernel -- no staging, no collective, no
+     host wait.  Otherwise (`exchange="all_to_all"`, and gloo): every rank
+     knows who owns each winner and who needs it, packs the winners it owns
+     by destination (`vfr_gather_owned` on the compact label list), one
+     all-to-all with those uneven splits delivers them, and
+     `vfr_blend_gathered_rows` reads them through a slot -> row map.
 
 Frames are therefore blended exactly as by a single index; the output of
 rank r is frames [r*Q/G, (r+1)*Q/G).  The reference is single-GPU; this is the
 multi-GPU extension of its path.  Collectives are taken in the same order on
-every rank.  The split sizes of step 4 come to the host once per step (a
-G x G count matrix); that copy is the step's one host wait, and with a
-`timeout_s` it is a bounded poll: if a peer never joins the collectives
-before it, the process group is aborted and `ShardTimeout` is raised instead
-of waiting forever (the all-to-all is then awaited against the same deadline).
+every rank.  With a `timeout_s` every host wait of a step is a bounded poll
+(the peer path waits once, for the step's end; the all-to-all path for its G x
+G split sizes and for the all-to-all): if a peer never joins before the
+deadline, the process group is aborted and `ShardTimeout` is raised instead
+of waiting forever.
 `ops` selects the per-rank compute: `LibraryOps` (CUDA library, the product)
 or a test double with the same interface.
 
@@ -102,6 +103,80 @@ class LibraryOps:
         out = torch.empty_like(q)
         blend_gathered_rows(q, out, dist, rows, slot_rows, rate, stream=stream)
         return out
+
+    # -- peer-memory exchange (NCCL process groups: the GPUs of one node)
+    peers = None
+
+    def open_peers(self, group, world: int, rank: int, deadline=None):
+        """Maps every shard's rows into this process (collective: every rank
+        calls it once, in the same step)."""
+        self.peers = PeerRows(self.index, group, world, rank, deadline)
+
+    def blend_peer(self, q, dist, labels, rate, stream):
+        import torch
+
+        out = torch.empty_like(q)
+        self.peers.blend(q, out, dist, labels, rate, stream)
+        return out
+
+    def close(self, group=None):
+        """Releases the peer mappings on every rank before any rank frees its
+        rows (collective when peers are open): synchronise, barrier, close,
+        barrier."""
+        if self.peers is None:
+            return
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        self.peers.close()
+        self.peers = None
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+
+
+class PeerRows:
+    """This rank's mappings of every row shard's fp32 rows
+    (vfr_index_ipc_export on each rank, an all-gather of the descriptors,
+    vfr_peer_rows_open), used by vfr_blend_peer."""
+
+    def __init__(self, index, group, world: int, rank: int, deadline=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        L = _l.load_library()
+        desc = _l.IpcRows()
+        _l.call(L.vfr_index_ipc_export, index._h, ctypes.byref(desc))
+        raw = torch.frombuffer(bytearray(bytes(desc)), dtype=torch.uint8)
+        if dist.get_backend(group) == "nccl":
+            raw = raw.cuda()
+        every = _all_gather(raw, group, world, deadline, "peer row descriptors").cpu().numpy()
+        descs = (_l.IpcRows * world)()
+        for r in range(world):
+            ctypes.memmove(ctypes.addressof(descs[r]), every[r].tobytes(), ctypes.sizeof(_l.IpcRows))
+        self._h = ctypes.c_void_p()
+        _l.call(L.vfr_peer_rows_open, index._h, world, descs, rank, ctypes.byref(self._h))
+
+    def blend(self, q, out, dist, labels, rate, stream=None):
+        import ctypes
+
+        from .index import _ptr
+
+        L = _l.load_library()
+        s = _l.stream_struct(stream)
+        _l.call(L.vfr_blend_peer, self._h, _ptr(q), _ptr(out), _ptr(dist), _ptr(labels), q.shape[0], q.shape[1],
+                _ptr(rate), ctypes.byref(s))
+
+    def close(self):
+        if getattr(self, "_h", None) and self._h.value:
+            _l.load_library().vfr_peer_rows_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
 
 
 def _stream_ctx(stream):
@@ -220,11 +295,18 @@ def _slot_rows(owner, rank, m, world):
     return pos.to(torch.int32).view(m, 8)
 
 
-def sharded_blend(ops, queries, rate, group, world: int, rank: int, stream=None, timeout_s: float | None = None):
+def sharded_blend(ops, queries, rate, group, world: int, rank: int, stream=None, timeout_s: float | None = None,
+                  exchange: str = "auto"):
     """One row-sharded step for `queries` [Q, d] (Q a multiple of world, the
     same tensor on every rank).  Returns (this rank's blended frames
-    [Q/world, d], merged distances [Q, 8], merged labels [Q, 8]).  With
-    `timeout_s`, the step's host waits are bounded (ShardTimeout)."""
+    [Q/world, d], merged distances [Q, 8], merged labels [Q, 8]).
+
+    exchange: "peer" reads the winners from their owners' memory in the blend
+    kernel (NCCL groups with LibraryOps; the peer mappings are opened on the
+    first call, so every rank must make it), "all_to_all" sends them with a
+    collective, "auto" takes "peer" where it can.  With `timeout_s` the
+    step's host waits are bounded: ShardTimeout (and an aborted group) if a
+    peer never joins."""
     import torch
     import torch.distributed as dist
 
@@ -232,17 +314,30 @@ def sharded_blend(ops, queries, rate, group, world: int, rank: int, stream=None,
     if q % world:
         raise ValueError("frame count must be a multiple of the world size; pad with padded_frames()")
     deadline = time.monotonic() + timeout_s if timeout_s is not None else None
+    nccl = dist.get_backend(group) == "nccl"
+    if exchange == "auto":
+        exchange = "peer" if nccl and hasattr(ops, "open_peers") else "all_to_all"
     m = q // world
     lo = rank * m
     with _stream_ctx(stream):
         bounds = _bounds(ops, group, world, deadline)
+        if exchange == "peer" and ops.peers is None:
+            ops.open_peers(group, world, rank, deadline)
         d8, l8 = ops.search(queries, stream)
         # on NCCL the two gathers are only enqueued here: the bounded wait for
-        # the count matrix below covers them
-        gloo_deadline = deadline if dist.get_backend(group) != "nccl" else None
+        # the count matrix below (or the end of the step) covers them
+        gloo_deadline = deadline if not nccl else None
         dists = _all_gather(d8, group, world, gloo_deadline, "top-8 distance all-gather")
         labels = _all_gather(l8, group, world, gloo_deadline, "top-8 label all-gather")
         md, ml = ops.merge(dists, labels, stream)
+        if exchange == "peer":
+            out = ops.blend_peer(queries[lo:lo + m], md[lo:lo + m].contiguous(), ml[lo:lo + m].contiguous(), rate,
+                                 stream)
+            if deadline is not None:
+                ev = torch.cuda.Event()
+                ev.record()
+                _poll(ev.query, deadline, group, "row-sharded step")
+            return out, md, ml
         counts_dev, owner = exchange_plan(ml, bounds, world, rank)
         if deadline is not None and counts_dev.is_cuda:
             host = torch.empty(counts_dev.shape, dtype=counts_dev.dtype, pin_memory=True)
