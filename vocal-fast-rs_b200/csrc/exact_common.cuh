@@ -181,6 +181,11 @@ __device__ __forceinline__ bool markstein_ok(double t, const WeightDivisor &d) {
     return d.fast && (at == 0.0 || (at >= 0x1p-400 && at <= 0x1p400));
 }
 
+// t / S through the divide instruction sequence, out of line: the operands
+// Markstein's quotient does not admit are rare, and keeping the sequence out
+// of the unrolled blend keeps latency-bound kernels' code small.
+static __device__ __noinline__ double slow_quotient(double t, double s) { return __ddiv_rn(t, s); }
+
 // One output element of the blend: retrieved from the gathered neighbour
 // values v[k] (k < count), then q*(1-r) + retrieved*r; the quotients are
 // summed in the reference's order.  kSideBySide computes the 8 quotients as
@@ -203,7 +208,7 @@ __device__ __forceinline__ float reference_blend_element(float q, const float *v
         if (!ok) {
 #pragma unroll
             for (int k = 0; k < 8; ++k)
-                if (k < count) quo[k] = __ddiv_rn(t[k], sum.s);
+                if (k < count) quo[k] = slow_quotient(t[k], sum.s);
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k)

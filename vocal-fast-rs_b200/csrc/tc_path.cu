@@ -21,6 +21,7 @@
 //   4. the exact SIMT kernel, which re-runs them.
 // The result is therefore the reference's result for every frame.
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <limits>
 #include <mutex>
@@ -1319,6 +1320,361 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreads ? 3 : 1) merge_kernel(
     }
 }
 
+// ---------------------------------------------------------------- merge (small launches)
+//
+// merge_small_kernel: merge_kernel's job for launches of at most two frames
+// per SM (realtime blocks), where each CTA's chain of dependent steps sets
+// the time.  The re-rank set comes from one proof instead of a radix
+// selection and a narrowing pass: U = the 8th smallest approximate distance
+// among all the frame's candidate keys (found exactly by warp-level
+// extraction), and a key is re-ranked unless its lower bound d~ + ||q||^2 - e
+// exceeds (U + ||q||^2 + e) (1 + 4 exact_rel) -- the test narrow_rerank
+// applies, which shows such a row can neither enter nor tie the exact top 8.
+// The rows a candidate stage never kept are covered by the list thresholds
+// (the certificate, as in merge_kernel).  The thread that finds a kept key
+// issues the bulk copy of its row into the stage at once, so the row fetches
+// overlap the rest of the filter pass.
+
+// 64-bit minimum over the warp.
+__device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long v) {
+    const uint32_t hi = __reduce_min_sync(kFullMask, static_cast<uint32_t>(v >> 32));
+    const uint32_t lo =
+        __reduce_min_sync(kFullMask, static_cast<uint32_t>(v >> 32) == hi ? static_cast<uint32_t>(v) : 0xffffffffu);
+    return (static_cast<unsigned long long>(hi) << 32) | lo;
+}
+
+// The 8 smallest of keys[lane], keys[lane + 32], ... below `count`
+// (kEmptyKey entries never count; the other keys are distinct), ascending
+// and padded with kEmptyKey; every lane of the warp gets them.
+__device__ __noinline__ void warp_smallest8(const unsigned long long *keys, int count,
+                                            unsigned long long (&out)[8]) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long prev = 0;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        unsigned long long mn = kEmptyKey;
+        for (int i = lane; i < count; i += 32) {
+            const unsigned long long k = keys[i];
+            if ((r == 0 || k > prev) && k < mn) mn = k;
+        }
+        mn = warp_min_u64(mn);
+        out[r] = mn;
+        prev = mn;
+    }
+}
+
+// Compare-exchange of two keys (ascending).
+__device__ __forceinline__ void key_cx(unsigned long long &a, unsigned long long &b) {
+    const unsigned long long lo = a < b ? a : b, hi = a < b ? b : a;
+    a = lo;
+    b = hi;
+}
+
+// warp_smallest8 for a warp whose lanes hold at most 8 keys each: the keys
+// go to registers once, each lane sorts its 8 (a 19-exchange network), and
+// the warp merges the 32 sorted lists, one warp minimum per output key.
+__device__ __noinline__ void warp_smallest8_reg(const unsigned long long *keys, int count,
+                                                unsigned long long (&out)[8]) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const int i = lane + 32 * e;
+        v[e] = i < count ? keys[i] : kEmptyKey;
+    }
+    // Batcher's odd-even merge network for 8 inputs
+    key_cx(v[0], v[1]); key_cx(v[2], v[3]); key_cx(v[4], v[5]); key_cx(v[6], v[7]);
+    key_cx(v[0], v[2]); key_cx(v[1], v[3]); key_cx(v[4], v[6]); key_cx(v[5], v[7]);
+    key_cx(v[1], v[2]); key_cx(v[5], v[6]);
+    key_cx(v[0], v[4]); key_cx(v[1], v[5]); key_cx(v[2], v[6]); key_cx(v[3], v[7]);
+    key_cx(v[2], v[4]); key_cx(v[3], v[5]);
+    key_cx(v[1], v[2]); key_cx(v[3], v[4]); key_cx(v[5], v[6]);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const unsigned long long mn = warp_min_u64(v[0]);
+        out[r] = mn;
+        if (v[0] == mn && mn != kEmptyKey) {  // the owner pops its head (keys are distinct)
+#pragma unroll
+            for (int e = 0; e < 7; ++e) v[e] = v[e + 1];
+            v[7] = kEmptyKey;
+        }
+    }
+}
+
+// Dynamic shared memory of merge_small_kernel: thresholds, query row, key
+// slots, then the stage (its own region, so copies land while keys are read).
+struct SmallSmem {
+    size_t thr, q, keys, stage, total;
+};
+__host__ __device__ inline SmallSmem small_smem(int sort_size, int thr_stride, int d, int stage_rows) {
+    SmallSmem m{};
+    m.thr = 0;
+    m.q = static_cast<size_t>(thr_stride) * 4;
+    m.keys = (m.q + static_cast<size_t>((d + 3) & ~3) * 4 + 15) & ~size_t(15);
+    m.stage = (m.keys + static_cast<size_t>(sort_size) * 8 + 15) & ~size_t(15);
+    m.total = m.stage + static_cast<size_t>(stage_rows) * stage_stride(d) * 4;
+    return m;
+}
+
+// Out-of-line pieces of merge_small_kernel's rare paths (a frame handed to
+// the exact re-run, a timed-out copy, search output, rows beyond the stage):
+// that kernel runs each instruction about once per launch, so its time
+// follows its code size, and these stay out of the common path's lines.
+__device__ __noinline__ void hand_to_rerun(const MergeArgs &a, long long frame, bool timed_out) {
+    if (timed_out && a.counters) atomicAdd(&a.counters->timeouts, 1ull);
+    const int pos = atomicAdd(a.fallback_count, 1);
+    a.fallback_list[pos] = static_cast<int32_t>(frame);
+}
+
+__device__ __noinline__ void write_search(const MergeArgs &a, long long frame, const unsigned long long *best,
+                                          int count) {
+    const int t = threadIdx.x;
+    if (t < a.k) {
+        const bool have = t < count;
+        a.dist_out[frame * a.k + t] = have ? key_dist(best[t]) : __int_as_float(0x7f800000);
+        a.label_out[frame * a.k + t] = have ? static_cast<int64_t>(a.ids[key_pos(best[t])]) + a.label_base : -1;
+    }
+}
+
+// Exact distances of re-rank keys [c0, m) read from global memory (the
+// kept rows the stage could not hold), one octet per row.
+template <int kOct>
+__device__ __noinline__ void global_distances(const MergeArgs &a, const float *q, int c0, int m,
+                                              const unsigned long long *sel_keys, unsigned long long *exact_keys) {
+    const int tid = threadIdx.x, lane = tid & 31, octet = tid >> 3, j = tid & 7;
+    for (; c0 < m; c0 += kOct) {
+        const int c = c0 + octet;
+        const uint32_t row = key_pos(sel_keys[c < m ? c : c0]);
+        const float *xs[1] = {a.vectors + static_cast<size_t>(row) * a.d};
+        float dist[1];
+        octet_l2n<1>(q, xs, a.d, j, lane & ~7, kFullMask, dist);
+        if (j == 0 && c < m) exact_keys[c] = dist[0] < __int_as_float(0x7f800000) ? make_key(dist[0], row) : kEmptyKey;
+    }
+}
+
+constexpr int kSmallStageMin = 16;  // fewer stage rows than this: merge_kernel instead
+constexpr int kSmallStageMax = 64;
+
+template <int kT>
+__global__ void __launch_bounds__(kT, 1) merge_small_kernel(MergeArgs a) {
+    constexpr int kOct = kT / 8;
+    constexpr int kWarps = kT / 32;
+    extern __shared__ __align__(16) uint8_t msm[];
+    const SmallSmem lay = small_smem(a.sort_size, a.thr_stride, a.d, a.stage_rows);
+    unsigned long long *keys = reinterpret_cast<unsigned long long *>(msm + lay.keys);
+    float *thr = reinterpret_cast<float *>(msm + lay.thr);
+    float *q = reinterpret_cast<float *>(msm + lay.q);
+    float *stage = reinterpret_cast<float *>(msm + lay.stage);
+    __shared__ unsigned long long exact_keys[kRerankMax];
+    __shared__ unsigned long long sel_keys[kRerankMax];
+    __shared__ unsigned long long best[8];
+    __shared__ int best_slot[8];
+    __shared__ double weights[8];
+    __shared__ unsigned long long warp_top[kWarps * 8];
+    __shared__ float warp_tmin[kWarps];
+    __shared__ unsigned long long u8_s;
+    __shared__ float tmin_s;
+    __shared__ int count_s, certified_s;
+    __shared__ __align__(8) uint64_t gather_bar;
+    __shared__ __align__(8) uint64_t stage_bar;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
+    const long long frame = blockIdx.x;
+    const int d = a.d;
+    const float *src = a.queries + frame * d;
+    float *dst = a.out + frame * d;
+    const float inf = __int_as_float(0x7f800000);
+    const int real_slots = a.lists * a.keep;
+    const int stride = stage_stride(d);
+
+    if (tid == 0) {
+        tc::mbar_init(&gather_bar, 1);
+        tc::mbar_init(&stage_bar, 1);
+        tc::fence_mbarrier_init();
+        count_s = 0;
+    }
+    if (tid < 8) best[tid] = kEmptyKey;
+    // the caller's inputs first, while the candidate kernel may still run
+    const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
+    float *raw_row = a.raw_out ? a.raw_out + frame * d : nullptr;
+    for (int i = tid; i < d; i += kT) {
+        const float v = src[i];
+        q[i] = v;
+        if (raw_row) raw_row[i] = v;
+    }
+    for (int i = real_slots + tid; i < a.sort_size; i += kT) keys[i] = kEmptyKey;
+    grid_dependency_wait();
+    const float4 qs = a.qstats[frame];
+    bool landed = true;
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t kbytes = static_cast<uint32_t>(real_slots) * 8;
+            const uint32_t tbytes = static_cast<uint32_t>(a.thr_stride) * 4;
+            tc::mbar_arrive_expect_tx(&gather_bar, kbytes + tbytes);
+            tc::bulk_load(keys, a.keys + static_cast<size_t>(frame) * real_slots, kbytes, &gather_bar);
+            tc::bulk_load(thr, a.thr + static_cast<size_t>(frame) * a.thr_stride, tbytes, &gather_bar);
+        }
+        __syncwarp();
+        landed = tc::mbar_wait(&gather_bar, 0, kWaitLimitNs);
+    }
+    if (__syncthreads_or(!landed)) {
+        if (warp == 0) tc::mbar_wait(&gather_bar, 0, kWaitLimitNs);
+        if (tid == 0) hand_to_rerun(a, frame, true);
+        return;
+    }
+    if (a.mode == kModeBlend && !(ratio > 0.f)) {
+        if (dst != src)
+            for (int i = tid; i < d; i += kT) dst[i] = q[i];
+        return;
+    }
+    // per warp: the smallest list threshold and the 8 smallest keys of its
+    // slice of the key slots; then warp 0 reduces them
+    {
+        float tmin = inf;
+        for (int s = tid; s < a.lists; s += kT) tmin = fminf(tmin, thr[s]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, o));
+        const int chunk = (a.sort_size + kWarps - 1) / kWarps;
+        const int lo = warp * chunk;
+        const int n = max(0, min(chunk, a.sort_size - lo));
+        unsigned long long top[8];
+        if (chunk <= 256)  // warp-uniform
+            warp_smallest8_reg(keys + lo, n, top);
+        else
+            warp_smallest8(keys + lo, n, top);
+        if (lane == 0) {
+            warp_tmin[warp] = tmin;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) warp_top[warp * 8 + r] = top[r];
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        static_assert(kWarps * 8 <= 256, "one register list per lane");
+        unsigned long long top[8];
+        warp_smallest8_reg(warp_top, kWarps * 8, top);
+        float tmin = lane < kWarps ? warp_tmin[lane] : inf;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, o));
+        if (lane == 0) {
+            u8_s = top[7];
+            tmin_s = tmin;
+        }
+    }
+    __syncthreads();
+    // the re-rank set: every key that can still reach or tie the exact top 8
+    const unsigned long long u8 = u8_s;
+    const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
+    const float limit = u8 == kEmptyKey ? inf : (key_dist(u8) + qs.x + e) * (1.f + 4.f * a.exact_rel) + 1e-30f;
+    for (int base = 0; base < a.sort_size; base += kT) {  // sort_size and kT are multiples of 32
+        const int i = base + tid;
+        const unsigned long long k = i < a.sort_size ? keys[i] : kEmptyKey;
+        const bool keep = k != kEmptyKey && !(key_dist(k) + qs.x - e > limit);
+        const unsigned ball = __ballot_sync(kFullMask, keep);
+        if (ball == 0u) continue;
+        int first = 0;
+        if (lane == 0) first = atomicAdd(&count_s, __popc(ball));
+        first = __shfl_sync(kFullMask, first, 0);
+        if (keep) {
+            const int pos = first + __popc(ball & ((1u << lane) - 1u));
+            if (pos < kRerankMax) sel_keys[pos] = k;
+            if (pos < a.stage_rows) {
+                tc::mbar_expect_tx(&stage_bar, static_cast<uint32_t>(d) * 4);
+                tc::bulk_load(stage + pos * stride, a.vectors + static_cast<size_t>(key_pos(k)) * d,
+                              static_cast<uint32_t>(d) * 4, &stage_bar);
+            }
+        }
+    }
+    __syncthreads();  // the count is final and every expect_tx precedes the arrival below
+    const int total = count_s;
+    const bool too_many = total > kRerankMax;
+    const int m = min(total, kRerankMax);
+    const int staged = min(m, a.stage_rows);
+    bool arrived = true;
+    if (warp == 0) {
+        if (lane == 0) tc::mbar_arrive(&stage_bar);
+        __syncwarp();
+        arrived = tc::mbar_wait(&stage_bar, 0, kWaitLimitNs);
+    }
+    if (__syncthreads_or(!arrived)) {
+        // a copy never completed: let the copies in flight land (bounded)
+        // before the shared memory is released, and hand the frame on
+        if (warp == 0) tc::mbar_wait(&stage_bar, 0, kWaitLimitNs);
+        if (tid == 0) hand_to_rerun(a, frame, true);
+        return;
+    }
+    // exact distances in the reference order: staged rows from shared
+    // memory, any others from global memory (flat scan position == row)
+    // (a warp whose four octets have no staged row skips the pass: the
+    // chains are long and issue-bound, so idle octets would slow the rest)
+    static_assert(kSmallStageMax <= kOct, "one staged row per octet");
+    if (warp * 4 < staged)
+        stage_distances<1, kOct>(q, stage, stride, staged, 0, d, octet, j, lane, sel_keys, exact_keys);
+    if (staged < m) global_distances<kOct>(a, q, staged, m, sel_keys, exact_keys);
+    __syncthreads();
+    // the frame's top 8 by rank counting (keys are distinct: one row each)
+    for (int c = tid; c < m; c += kT) {
+        const unsigned long long key = exact_keys[c];
+        if (key == kEmptyKey) continue;
+        int rank = 0;
+        for (int i = 0; i < m; ++i) rank += exact_keys[i] < key;
+        if (rank < 8) {
+            best[rank] = key;
+            best_slot[rank] = c;
+        }
+    }
+    __syncthreads();
+    int count = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) count += best[i] != kEmptyKey;
+    if (tid == 32) {
+        const float d8 = count == 8 ? key_dist(best[7]) : inf;
+        const bool ok = !too_many && certify(tmin_s, d8, qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel,
+                                             a.norm_rel, a.exact_rel);
+        certified_s = ok ? 1 : 0;
+    }
+    if (tid < 8) weights[tid] = tid < count ? reference_weight(key_dist(best[tid])) : 0.0;
+    __syncthreads();
+    if (certified_s == 0) {
+        if (tid == 0) hand_to_rerun(a, frame, false);
+        return;
+    }
+    if (tid == 0 && a.counters) atomicAdd(&a.counters->candidate_frames, 1ull);
+    if (a.mode == kModeSearch) {
+        if (warp == 0) write_search(a, frame, best, count);
+        return;
+    }
+    if (count == 0) {
+        if (tid == 0 && a.counters) atomicAdd(&a.counters->empty_frames, 1ull);
+        if (dst != src)
+            for (int i = tid; i < d; i += kT) dst[i] = q[i];
+        return;
+    }
+    double w[8];
+    double wsum = -0.0;  // the reference's order: S = w0 + w1 + ... (zeros past count)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        w[i] = weights[i];
+        wsum = __dadd_rn(wsum, w[i]);
+    }
+    const WeightDivisor sum = weight_divisor(wsum);
+    // each neighbour's row: in the stage, or in global memory when it was
+    // kept beyond the stage (generic loads read either)
+    const float *vrow[8];
+#pragma unroll
+    for (int kq = 0; kq < 8; ++kq) {
+        const int slot = kq < count ? best_slot[kq] : 0;
+        vrow[kq] = slot < staged ? stage + slot * stride
+                                 : a.vectors + static_cast<size_t>(key_pos(best[kq])) * d;
+    }
+    for (int i = tid; i < d; i += kT) {
+        float v[8];
+#pragma unroll
+        for (int kq = 0; kq < 8; ++kq) v[kq] = kq < count ? vrow[kq][i] : 0.f;
+        dst[i] = reference_blend_element<true>(q[i], v, w, sum, count, ratio);
+    }
+}
+
 // ---------------------------------------------------------------- index build
 __global__ void max_abs_kernel(const float *__restrict__ x, size_t count, unsigned int *out) {
     float m = 0.f;
@@ -1418,8 +1774,21 @@ struct Plan {
 // global memory.
 void launch_merge(VfrIndex *ix, MergeArgs &ma, size_t frames, cudaStream_t stream) {
     ma.stage_rows = 0;
-    if (ix->d % 4 == 0 && reinterpret_cast<uintptr_t>(ix->vectors) % 16 == 0 &&
-        frames <= static_cast<size_t>(ix->sm_count) * 2) {
+    const bool few = ix->d % 4 == 0 && reinterpret_cast<uintptr_t>(ix->vectors) % 16 == 0 &&
+                     frames <= static_cast<size_t>(ix->sm_count) * 2;
+    if (few && ix->small_merge) {
+        // merge_small_kernel, with as many stage rows as fit (at least kSmallStageMin)
+        for (int rows = kSmallStageMax; rows >= kSmallStageMin; --rows) {
+            const size_t need = small_smem(ma.sort_size, ma.thr_stride, ix->d, rows).total;
+            if (need <= static_cast<size_t>(ix->merge_smem_max)) {
+                ma.stage_rows = rows;
+                cuda_check(launch_pdl(merge_small_kernel<kMergeThreadsMax>, dim3(static_cast<unsigned>(frames)),
+                                      dim3(kMergeThreadsMax), need, stream, ma));
+                return;
+            }
+        }
+    }
+    if (few) {
         // as many rows as fit, up to kRerankStop (the usual re-rank set); at
         // least 32, else the rows stay in global memory
         for (int rows = kRerankStop; rows >= 32; --rows)
@@ -2076,16 +2445,24 @@ void build_tc(VfrIndex *ix) {
     {
         int optin = 0;
         cuda_check(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ix->device));
-        cudaFuncAttributes fa{}, fb{};
+        cudaFuncAttributes fa{}, fb{}, fc{};
         cuda_check(cudaFuncGetAttributes(&fa, merge_kernel<kMergeThreads>));
         cuda_check(cudaFuncGetAttributes(&fb, merge_kernel<kMergeThreadsMax>));
-        ix->merge_smem_max = optin - static_cast<int>(std::max(fa.sharedSizeBytes, fb.sharedSizeBytes));
+        cuda_check(cudaFuncGetAttributes(&fc, merge_small_kernel<kMergeThreadsMax>));
+        ix->merge_smem_max =
+            optin - static_cast<int>(std::max({fa.sharedSizeBytes, fb.sharedSizeBytes, fc.sharedSizeBytes}));
         cuda_check(cudaFuncSetAttribute(merge_kernel<kMergeThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         ix->merge_smem_max));
         cuda_check(cudaFuncSetAttribute(merge_kernel<kMergeThreadsMax>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         ix->merge_smem_max));
+        cuda_check(cudaFuncSetAttribute(merge_small_kernel<kMergeThreadsMax>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, ix->merge_smem_max));
     }
     cuda_check(cudaFuncSetAttribute(coarse_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    {
+        const char *env = std::getenv("VFR_SMALL_MERGE");
+        ix->small_merge = !(env && env[0] == '0');
+    }
     cuda_check(cudaDeviceSynchronize());
     ix->have_tc = true;
 }

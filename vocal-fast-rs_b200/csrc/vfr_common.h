@@ -148,6 +148,10 @@ struct VfrIndex {
     float max_row_residual = 0.f;  // max ||x - fp16(s x) / s||
     int sm_count = 148;
     int merge_smem_max = 96 * 1024;  // dynamic shared memory merge_kernel may use (set by build_tc)
+    // Small launches (at most two frames per SM) use merge_small_kernel;
+    // VFR_SMALL_MERGE=0 in the environment at index creation selects
+    // merge_kernel for them instead (comparison runs).
+    bool small_merge = true;
     // IVF: the same layout for the coarse centroids (nlist_pad rows).
     __half *centroids_h = nullptr;
     float *centroid_norms = nullptr;
