@@ -607,7 +607,9 @@ def published_shape(device):
             p50, p95, mean = _replay_latency(lambda: idx.blend(feats, frames, rate, stream=s), s, 500,
                                              pre=lambda: feats.copy_(src))
             res[str(frames)] = {"p50_ms": p50, "p95_ms": p95, "mean_ms": mean}
-        res["fallback_frames"] = idx.diagnostics()["fallback_frames"]
+        diag = idx.diagnostics()
+        res["fallback_frames"] = diag["fallback_frames"]
+        res["engine_used"] = diag["last_engine"]
         out[name] = res
         idx.close()
     return out

@@ -6,12 +6,14 @@
 // crates/vocal-tensorrt/native/bridge.h:24-32.
 #include <algorithm>
 #include <cmath>
+#include <functional>
 #include <cstdio>
 #include <map>
 #include <memory>
 #include <mutex>
 #include <string>
 
+#include "exact2d.h"
 #include "index_build.h"
 #include "ingest.h"
 #include "kernels.h"
@@ -53,6 +55,7 @@ void free_index(VfrIndex *ix) noexcept {
                         static_cast<void *>(ix->row_of_id)})
             if (p) cudaFree(p);
     if (ix->counters) cudaFree(ix->counters);
+    if (ix->x2_ws) cudaFree(ix->x2_ws);
     if (ix->split_keys) cudaFree(ix->split_keys);
     if (ix->split_done) cudaFree(ix->split_done);
     ix->shared.reset();
@@ -130,12 +133,54 @@ VfrIndex *new_handle(int32_t d, int32_t nlist, int32_t nprobe, size_t n, const i
     return ix;
 }
 
+// The most rows one frame's probed lists can hold: the nprobe largest lists.
+int64_t max_probed_rows(const std::vector<int32_t> &offsets, int nprobe) {
+    std::vector<int64_t> sizes;
+    for (size_t l = 0; l + 1 < offsets.size(); ++l) sizes.push_back(offsets[l + 1] - offsets[l]);
+    const size_t p = std::min(sizes.size(), static_cast<size_t>(std::max(nprobe, 1)));
+    std::partial_sort(sizes.begin(), sizes.begin() + p, sizes.end(), std::greater<int64_t>());
+    int64_t total = 0;
+    for (size_t i = 0; i < p; ++i) total += sizes[i];
+    return total;
+}
+
+// Bytes of exact row and centroid reads above which a small IVF batch goes
+// to the tensor-core path instead of the 2-D exact engine.
+constexpr double kExact2dBytes = 400e6;
+
+size_t exact2d_frame_limit(const VfrIndex *ix) {
+    if (ix->nlist <= 1 || ix->engine != VFR_ENGINE_AUTO) return 0;
+    const double per_frame = static_cast<double>(ix->nlist + ix->max_probed_rows) * ix->d * 4.0;
+    return static_cast<size_t>(std::min(65535.0, std::floor(kExact2dBytes / per_frame)));
+}
+
+bool use_exact2d(const VfrIndex *ix, size_t frames) { return frames <= exact2d_frame_limit(ix); }
+
+void reserve_exact2d(VfrIndex *ix, size_t frames) {
+    const size_t f = std::min(frames, exact2d_frame_limit(ix));
+    if (f == 0) return;
+    const size_t bytes = exact2d_layout(f, ix->nlist, ix->nprobe, ix->max_probed_rows).total;
+    if (bytes <= ix->x2_bytes) return;
+    void *p = nullptr;
+    cuda_check(cudaMalloc(&p, bytes), "cudaMalloc exact2d scratch");
+    if (ix->x2_ws) {
+        cuda_check(cudaDeviceSynchronize());
+        cudaFree(ix->x2_ws);
+    }
+    ix->x2_ws = p;
+    ix->x2_bytes = bytes;
+}
+
 // Counters, the tensor-core layout and the workspace reservation.
 void finish_index(VfrIndex *ix, const VfrOptions &o) {
     cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->counters), sizeof(DeviceCounters)));
     cuda_check(cudaMemset(ix->counters, 0, sizeof(DeviceCounters)));
+    ix->max_probed_rows = max_probed_rows(ix->host_offsets, ix->nprobe);
     if (!ix->shared && ix->engine != VFR_ENGINE_EXACT) build_tc(ix);
-    if (o.max_frames > 0) reserve_tc(ix, static_cast<size_t>(o.max_frames));
+    if (o.max_frames > 0) {
+        reserve_tc(ix, static_cast<size_t>(o.max_frames));
+        reserve_exact2d(ix, static_cast<size_t>(o.max_frames));
+    }
     cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->split_keys), kSplitKeyBytes), "cudaMalloc re-run scratch");
     cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->split_done), kSplitFrames * sizeof(int32_t)));
     cuda_check(cudaMemset(ix->split_done, 0, kSplitFrames * sizeof(int32_t)));
@@ -322,11 +367,36 @@ ExactArgs exact_args(VfrIndex *ix, const float *queries, float *out, const float
     return a;
 }
 
+// The 2-D exact engine's call: scratch grown outside stream capture.
+void run_exact2d(VfrIndex *ix, const ExactArgs &a, size_t frames, cudaStream_t s) {
+    const Exact2dLayout l = exact2d_layout(frames, ix->nlist, ix->nprobe, ix->max_probed_rows);
+    if (l.total > ix->x2_bytes) {
+        cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+        cuda_check(cudaStreamIsCapturing(s, &st));
+        require(st == cudaStreamCaptureStatusNone,
+                "retrieval workspace too small for this frame count during stream capture; call "
+                "vfr_retrieval_reserve first");
+        reserve_exact2d(ix, frames);
+    }
+    ix->last_engine = 3;
+    ix->prof.begin(kProfExact, s);
+    launch_exact2d(a, ix->x2_ws, l, static_cast<long long>(frames), s);
+    ix->prof.end(s);
+}
+
 void search_rows(VfrIndex *ix, const float *queries, size_t frames, int k, float *dist, int64_t *labels,
                  cudaStream_t s) {
-    if (ix->have_tc && use_tc(ix, frames)) {
+    if (use_exact2d(ix, frames)) {
+        ExactArgs a = exact_args(ix, queries, nullptr, nullptr, kModeSearch);
+        a.k = k;
+        a.dist_out = dist;
+        a.label_out = labels;
+        run_exact2d(ix, a, frames, s);
+    } else if (ix->have_tc && use_tc(ix, frames)) {
+        ix->last_engine = 2;
         run_tc(ix, queries, nullptr, nullptr, kModeSearch, k, dist, labels, frames, s);
     } else {
+        ix->last_engine = 1;
         ExactArgs a = exact_args(ix, queries, nullptr, nullptr, kModeSearch);
         a.k = k;
         a.dist_out = dist;
@@ -348,9 +418,16 @@ void blend_impl(VfrIndex *ix, const float *queries, float *out, size_t frames, i
         const auto *r = reinterpret_cast<const uint8_t *>(raw), *q = reinterpret_cast<const uint8_t *>(queries);
         require(r + bytes <= q || q + bytes <= r, "raw feature buffer overlaps the features");
     }
-    if (ix->have_tc && use_tc(ix, frames)) {
+    if (use_exact2d(ix, frames)) {
+        if (raw)
+            cuda_check(cudaMemcpyAsync(raw, queries, frames * static_cast<size_t>(width) * sizeof(float),
+                                       cudaMemcpyDeviceToDevice, s));
+        run_exact2d(ix, exact_args(ix, queries, out, rate, kModeBlend), frames, s);
+    } else if (ix->have_tc && use_tc(ix, frames)) {
+        ix->last_engine = 2;
         run_tc(ix, queries, out, rate, kModeBlend, 8, nullptr, nullptr, frames, s, raw);
     } else {
+        ix->last_engine = 1;
         if (raw)
             cuda_check(cudaMemcpyAsync(raw, queries, frames * static_cast<size_t>(width) * sizeof(float),
                                        cudaMemcpyDeviceToDevice, s));
@@ -479,6 +556,7 @@ extern "C" int vfr_retrieval_reserve(VfrIndex *index, size_t max_frames, char **
         require(max_frames <= static_cast<size_t>(INT32_MAX), "FAISS frame count exceeds CUDA grid limit");
         vfr::DeviceGuard guard(index->device);
         if (index->have_tc) vfr::reserve_tc(index, max_frames);
+        vfr::reserve_exact2d(index, max_frames);
     });
 }
 
@@ -500,14 +578,18 @@ extern "C" size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t 
                           "\"workspace_bytes\":%zu,\"empty_frames\":%llu,\"fallback_frames\":%llu,"
                           "\"candidate_frames\":%llu,\"timeouts\":%llu,\"max_row_norm\":%.9g,"
                           "\"max_row_residual\":%.9g,\"shared_handles\":%ld,\"last_plan\":{\"keep\":%d,"
-                          "\"segments\":%d,\"tiles_per_segment\":%d,\"layout\":\"%s\"}}",
+                          "\"segments\":%d,\"tiles_per_segment\":%d,\"layout\":\"%s\"},\"last_engine\":\"%s\"}",
                           engine, index->have_tc ? "true" : "false", index->candidates, index->d, index->nlist,
                           index->nprobe, static_cast<long long>(index->n), static_cast<long long>(index->label_base),
                           index->device, index->ws.frames, index->ws.bytes, c.empty_frames, c.fallback_frames,
                           c.candidate_frames, c.timeouts, index->max_row_norm, index->max_row_residual,
                           static_cast<long>(index->shared ? index->shared.use_count() : 0), index->last_keep,
                           index->last_segments, index->last_tiles_per_seg,
-                          index->last_layout < 0 ? "none" : index->last_layout == 0 ? "full" : "spread");
+                          index->last_layout < 0 ? "none" : index->last_layout == 0 ? "full" : "spread",
+                          index->last_engine == 1   ? "exact"
+                          : index->last_engine == 2 ? "tensor"
+                          : index->last_engine == 3 ? "exact2d"
+                                                    : "none");
     size_t need = m > 0 ? static_cast<size_t>(m) : 0;
     if (json && length) {
         size_t w = std::min(need, length - 1);

@@ -171,6 +171,14 @@ struct VfrIndex {
     // frames share its grid (ExactArgs::split_keys / split_done).
     unsigned long long *split_keys = nullptr;
     int32_t *split_done = nullptr;
+    // 2-D exact engine (exact2d.cu) for small IVF batches: the most rows a
+    // frame's probed lists can hold, and its scratch.
+    int64_t max_probed_rows = 0;
+    // Engine that served the last call (diagnostics): 0 none yet, 1 exact
+    // (one CTA per frame), 2 tensor cores, 3 the 2-D exact engine.
+    int32_t last_engine = 0;
+    void *x2_ws = nullptr;
+    size_t x2_bytes = 0;
     // Plan of the last tensor-core call on the host (diagnostics): candidate
     // list size per (work item, frame), database segments, tiles per
     // segment, and the A-tile layout (0 full, 1 spread, -1 no call yet).
