@@ -142,7 +142,12 @@ enum {
 enum {
     /* Loaders only: handles loaded from identical FAISS bytes on one device
      * (same engine class) share one copy of the device arrays; each handle
-     * keeps its own workspace and counters. */
+     * keeps its own workspace and counters.  "Identical" is decided by the
+     * 128-bit content hash (vfr_index_content_hash) and the byte length,
+     * without comparing the bytes: two different images collide by accident
+     * with probability about 2^-128, but the hash is not collision-resistant
+     * against crafted inputs, so enable sharing only for index files the
+     * caller trusts (its own voices), not for files supplied by others. */
     VFR_SHARE_STORAGE = 1
 };
 

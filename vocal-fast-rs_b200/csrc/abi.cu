@@ -149,7 +149,7 @@ int64_t max_probed_rows(const std::vector<int32_t> &offsets, int nprobe) {
 constexpr double kExact2dBytes = 400e6;
 
 size_t exact2d_frame_limit(const VfrIndex *ix) {
-    if (ix->nlist <= 1 || ix->engine != VFR_ENGINE_AUTO) return 0;
+    if (ix->nlist <= 1 || ix->engine != VFR_ENGINE_AUTO || ix->d > exact2d_max_width()) return 0;
     const double per_frame = static_cast<double>(ix->nlist + ix->max_probed_rows) * ix->d * 4.0;
     return static_cast<size_t>(std::min(65535.0, std::floor(kExact2dBytes / per_frame)));
 }

@@ -4,9 +4,10 @@
 // more than the arithmetic.  Three launches, the last two chained with
 // programmatic dependent launch:
 //
-//   1. coarse: CTA (slice, frame) computes the exact distances of 32
-//      centroids (one per octet, the reference's AVX2 order) and keeps its
-//      first nprobe keys (distance total order, list id);
+//   1. coarse: CTA (16-centroid slice, 8-frame group) stages both in shared
+//      memory once, computes the exact distances (the reference's AVX2
+//      order) and keeps each frame's first nprobe keys of the slice
+//      (distance total order, list id);
 //   2. fine: CTA (part, frame) merges the frame's slice lists into the
 //      first nprobe lists -- the reference's coarse sort,
 //      crates/vocal-cpu/src/retrieval.rs:45-51 -- and scans its 64 scan
@@ -91,24 +92,63 @@ __device__ __forceinline__ bool ratio_off(const ExactArgs &e) {
 }
 
 // ---------------------------------------------------------------- 1. coarse
-__global__ void __launch_bounds__(kT) exact2d_coarse_kernel(Exact2dArgs a) {
-    extern __shared__ float q[];
-    __shared__ unsigned long long keys[kOct];
+// CTA (slice, frame group): the slice's kSlice centroid rows and the group's
+// kGroup frames are staged in shared memory once; octet o computes centroid
+// o % kSlice against frames 4 (o / kSlice) .. +3 (the reference's AVX2 order;
+// (a - b)^2 == (b - a)^2 exactly, so the operand roles may swap), and warp f
+// keeps frame f's first nprobe keys (distance total order, list id).
+constexpr int kSlice = 16;                     // centroids per coarse CTA
+constexpr int kGroup = 8;                      // frames per coarse CTA
+constexpr int kFramesPerOctet = kGroup * kSlice / kOct;
+static_assert(kFramesPerOctet == 4 && kGroup == kT / 32, "one warp per frame of the group");
+constexpr int kExact2dMaxWidth = 2048;  // (kSlice + kGroup) rows of this width fit the opt-in shared memory
+
+__global__ void __launch_bounds__(kT) exact2d_coarse_kernel(Exact2dArgs a, long long frames) {
+    extern __shared__ float cs[];  // [kSlice][stride] centroids, then [kGroup][stride] frames
+    __shared__ unsigned long long keys[kGroup][kSlice];
     const ExactArgs &e = a.e;
     launch_dependents();
     if (ratio_off(e)) return;
-    const int tid = threadIdx.x, lane = tid & 31, octet = tid >> 3, j = tid & 7;
-    const long long frame = blockIdx.y;
-    const int d = e.d;
-    for (int i = tid; i < d; i += kT) q[i] = e.queries[frame * d + i];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
+    const int d = e.d, stride = (d + 3) & ~3;
+    const int c0 = static_cast<int>(blockIdx.x) * kSlice;
+    const long long f0 = static_cast<long long>(blockIdx.y) * kGroup;
+    float *cent = cs, *fr = cs + static_cast<size_t>(kSlice) * stride;
+    // rows staged whole (16-byte lanes when the width allows), zero past
+    // the last centroid or frame
+    const bool vec = (d & 3) == 0 && (reinterpret_cast<uintptr_t>(e.centroids) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(e.queries) & 15) == 0;
+    auto stage = [&](float *dst, const float *src, bool real) {
+        if (vec) {
+            const float4 *s4 = reinterpret_cast<const float4 *>(src);
+            float4 *d4 = reinterpret_cast<float4 *>(dst);
+            for (int k = tid; k < (d >> 2); k += kT) d4[k] = real ? __ldg(s4 + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            for (int k = tid; k < d; k += kT) dst[k] = real ? __ldg(src + k) : 0.f;
+        }
+    };
+#pragma unroll 1
+    for (int c = 0; c < kSlice; ++c)
+        stage(cent + c * stride, e.centroids + static_cast<size_t>(c0 + c < e.nlist ? c0 + c : 0) * d,
+              c0 + c < e.nlist);
+#pragma unroll 1
+    for (int g = 0; g < kGroup; ++g)
+        stage(fr + g * stride, e.queries + (f0 + g < frames ? f0 + g : 0) * d, f0 + g < frames);
     __syncthreads();
-    const int c = static_cast<int>(blockIdx.x) * kOct + octet;
-    const int cc = c < e.nlist ? c : e.nlist - 1;
-    const float dist = octet_l2(q, e.centroids + static_cast<size_t>(cc) * d, d, j, lane & ~7, kFullMask);
-    if (j == 0) keys[octet] = c < e.nlist ? make_key(dist, static_cast<uint32_t>(c)) : kEmptyKey;
+    const int c = octet % kSlice, g0 = (octet / kSlice) * kFramesPerOctet;
+    const float *xs[kFramesPerOctet];
+#pragma unroll
+    for (int k = 0; k < kFramesPerOctet; ++k) xs[k] = fr + (g0 + k) * stride;
+    float dist[kFramesPerOctet];
+    octet_l2n<kFramesPerOctet, false>(cent + c * stride, xs, d, j, lane & ~7, kFullMask, dist);
+    if (j == 0)
+#pragma unroll
+        for (int k = 0; k < kFramesPerOctet; ++k)
+            keys[g0 + k][c] = c0 + c < e.nlist ? make_key(dist[k], static_cast<uint32_t>(c0 + c)) : kEmptyKey;
     __syncthreads();
-    if (tid < 32) {
-        const unsigned long long v = sort32(keys[lane], lane);
+    const long long frame = f0 + warp;
+    if (frame < frames) {
+        const unsigned long long v = sort32(lane < kSlice ? keys[warp][lane] : kEmptyKey, lane);
         if (lane < a.probes) a.coarse_keys[(frame * a.slices + blockIdx.x) * a.probes + lane] = v;
     }
 }
@@ -272,10 +312,12 @@ __global__ void __launch_bounds__(kT) exact2d_finish_kernel(Exact2dArgs a) {
 
 }  // namespace
 
+int exact2d_max_width() { return kExact2dMaxWidth; }
+
 Exact2dLayout exact2d_layout(size_t frames, int nlist, int nprobe, int64_t max_probed) {
     Exact2dLayout l{};
     l.probes = std::min(nprobe, nlist);
-    l.slices = nlist > 1 ? (nlist + kOct - 1) / kOct : 0;
+    l.slices = nlist > 1 ? (nlist + kSlice - 1) / kSlice : 0;
     l.parts = static_cast<int>(std::max<int64_t>(1, (max_probed + kFinePart - 1) / kFinePart));
     size_t off = 0;
     auto take = [&](size_t &field, size_t bytes) {
@@ -309,7 +351,12 @@ void launch_exact2d(const ExactArgs &e, void *workspace, const Exact2dLayout &l,
     if (e.nlist > 1) {
         // not a programmatic launch: the frames (possibly blended in place by
         // the previous call) are read before any dependency wait
-        exact2d_coarse_kernel<<<dim3(static_cast<unsigned>(l.slices), f), kT, qbytes, s>>>(a);
+        const size_t cbytes = static_cast<size_t>(kSlice + kGroup) * ((e.d + 3) & ~3) * sizeof(float);
+        cudaError_t at = cudaFuncSetAttribute(exact2d_coarse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(cbytes));
+        if (at != cudaSuccess) throw std::runtime_error(std::string("exact2d coarse: ") + cudaGetErrorString(at));
+        exact2d_coarse_kernel<<<dim3(static_cast<unsigned>(l.slices), (f + kGroup - 1) / kGroup), kT, cbytes, s>>>(
+            a, frames);
         cudaError_t rc = cudaGetLastError();
         if (rc != cudaSuccess) throw std::runtime_error(std::string("exact2d coarse: ") + cudaGetErrorString(rc));
         rc = launch_pdl(exact2d_fine_kernel, dim3(static_cast<unsigned>(l.parts), f), dim3(kT), qbytes + heads, s, a);

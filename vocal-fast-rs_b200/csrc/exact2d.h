@@ -31,6 +31,9 @@ struct Exact2dLayout {
 };
 Exact2dLayout exact2d_layout(size_t frames, int nlist, int nprobe, int64_t max_probed);
 
+// Widest rows the engine takes (its coarse stage stages rows in shared memory).
+int exact2d_max_width();
+
 // Enqueues the three launches on `s` (workspace laid out by `l`).
 void launch_exact2d(const ExactArgs &e, void *workspace, const Exact2dLayout &l, long long frames, cudaStream_t s);
 

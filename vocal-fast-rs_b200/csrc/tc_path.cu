@@ -2105,6 +2105,7 @@ __global__ void gather_pairs_kernel(const __half *__restrict__ q16, int d_pad, c
 }
 
 struct IvfMergeArgs {
+    long long frames;
     int d;
     int nprobe;
     int pair_stride;
@@ -2290,6 +2291,356 @@ __global__ void __launch_bounds__(kMergeThreads, 3) ivf_merge_kernel(IvfMergeArg
     }
 }
 
+// ---------------------------------------------------------------- IVF merge, one warp per frame
+//
+// ivf_merge_warp_kernel: ivf_merge_kernel's result with one warp per frame
+// and no CTA-wide barrier, so a launch of many frames keeps a few dozen
+// frames in flight per SM instead of three.  Per frame: lane 2p + h loads the
+// candidate list (probe p, column half h; at most 16 keys, ascending) into
+// its warp's shared slots; U = the 8th smallest key of all lists (a warp
+// merge of the list heads); the re-rank set is every key whose lower bound
+// d~ + ||q||^2 - e does not exceed (U + ||q||^2 + e)(1 + 4 exact_rel) (the
+// narrowing test: a dropped row can neither enter nor tie the exact top 8;
+// rows the candidate stage never kept are covered by the lists' thresholds
+// in the certificate); the four octets compute the kept rows' exact
+// distances in the reference order, keyed by scan position (probe rank,
+// storage row); the top 8 by a warp merge; certificate; search output or
+// blend.
+constexpr int kIvfWarps = 8;
+
+__global__ void __launch_bounds__(32 * kIvfWarps, 3) ivf_merge_warp_kernel(IvfMergeArgs a) {
+    extern __shared__ __align__(16) float ivq[];  // [kIvfWarps][dq] frame rows
+    __shared__ unsigned long long lists[kIvfWarps][kIvfMaxProbe * kHalves * kItemKeep];
+    __shared__ unsigned long long sel[kIvfWarps][kRerankMax];
+    __shared__ unsigned long long ex[kIvfWarps][kRerankMax];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, octet = lane >> 3, j = lane & 7;
+    const long long frame = static_cast<long long>(blockIdx.x) * kIvfWarps + w;
+    if (frame >= a.frames || !a.probe_ok[frame]) return;  // r <= 0 (handled) or exact re-run
+    const int d = a.d, P = a.nprobe;
+    const int dq = (d + 3) & ~3;
+    float *q = ivq + static_cast<size_t>(w) * dq;
+    unsigned long long *lk = lists[w];
+    const size_t stride = static_cast<size_t>(a.pair_stride);
+    const float *src = a.queries + frame * d;
+    float *dst = a.out + frame * d;
+    const float inf = __int_as_float(0x7f800000);
+    const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
+    for (int i = lane; i < d; i += 32) q[i] = src[i];
+    // probe p's list on lane p: start, end and scan-position base
+    int32_t pstart = 0, pend = 0;
+    if (lane < P) {
+        const int32_t list = a.probes[frame * P + lane];
+        pstart = a.offsets[list];
+        pend = a.offsets[list + 1];
+    }
+    uint32_t incl = lane < P ? static_cast<uint32_t>(pend - pstart) : 0u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t up = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += up;
+    }
+    const uint32_t pbase = incl - (lane < P ? static_cast<uint32_t>(pend - pstart) : 0u);
+    // candidate list (probe lane / 2, half lane % 2) into the warp's slots
+    const int L = P * kHalves;
+    int cnt = 0;
+    float thr = inf;
+    if (lane < L) {
+        const int p = lane / kHalves, h = lane % kHalves;
+        const size_t pos = static_cast<size_t>(a.pair_slot[frame * P + p]);
+        cnt = a.counts[h * stride + pos];
+        thr = a.thr[h * stride + pos];
+        for (int i = 0; i < cnt; ++i) lk[lane * kItemKeep + i] = a.keys[(h * kItemKeep + i) * stride + pos];
+    }
+    float tmin = thr;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, o));
+    __syncwarp();
+    // U: the 8th smallest key of all lists
+    unsigned long long u8 = kEmptyKey;
+    {
+        int head = 0;
+#pragma unroll 1
+        for (int r = 0; r < 8; ++r) {
+            const unsigned long long c = head < cnt ? lk[lane * kItemKeep + head] : kEmptyKey;
+            const unsigned long long m = warp_min_u64(c);
+            if (c == m && m != kEmptyKey) ++head;
+            u8 = m;
+        }
+    }
+    const float4 qs = a.qstats[frame];
+    const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
+    const float limit = u8 == kEmptyKey ? inf : (key_dist(u8) + qs.x + e) * (1.f + 4.f * a.exact_rel) + 1e-30f;
+    // the re-rank set, compacted into sel (each lane scans one list)
+    int kept = 0;
+    for (int i = 0; i < cnt; ++i) kept += !(key_dist(lk[lane * kItemKeep + i]) + qs.x - e > limit);
+    uint32_t kincl = static_cast<uint32_t>(kept);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t up = __shfl_up_sync(kFullMask, kincl, o);
+        if (lane >= o) kincl += up;
+    }
+    const int total = __shfl_sync(kFullMask, static_cast<int>(kincl), 31);
+    {
+        int at = static_cast<int>(kincl) - kept;
+        for (int i = 0; i < cnt; ++i) {
+            const unsigned long long k = lk[lane * kItemKeep + i];
+            if (!(key_dist(k) + qs.x - e > limit)) {
+                if (at < kRerankMax) sel[w][at] = k;
+                ++at;
+            }
+        }
+    }
+    const bool too_many = total > kRerankMax;
+    const int m = min(total, kRerankMax);
+    __syncwarp();
+    // exact distances, two rows per octet per round, keyed by scan position
+    for (int c0 = 0; c0 < m; c0 += 8) {
+        uint32_t rows[2];
+        const float *xs[2];
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 4 * kk;
+            rows[kk] = key_pos(sel[w][c < m ? c : c0]);
+            xs[kk] = a.vectors + static_cast<size_t>(rows[kk]) * d;
+        }
+        float dist[2];
+        octet_l2n<2>(q, xs, d, j, lane & ~7, kFullMask, dist);
+        uint32_t sp[2] = {0u, 0u};
+        for (int pr = 0; pr < P; ++pr) {  // the probe holding each row (lists are disjoint row ranges)
+            const int32_t s = __shfl_sync(kFullMask, pstart, pr), t = __shfl_sync(kFullMask, pend, pr);
+            const uint32_t b = __shfl_sync(kFullMask, pbase, pr);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+                if (static_cast<int32_t>(rows[kk]) >= s && static_cast<int32_t>(rows[kk]) < t)
+                    sp[kk] = b + (rows[kk] - static_cast<uint32_t>(s));
+        }
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 4 * kk;
+            if (j == 0 && c < m) ex[w][c] = dist[kk] < inf ? make_key(dist[kk], sp[kk]) : kEmptyKey;
+        }
+    }
+    __syncwarp();
+    // the exact top 8: per lane the keys lane, lane + 32, ... (sorted), then 8 warp minima
+    unsigned long long best[8];
+    {
+        unsigned long long v[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) v[t] = lane + 32 * t < m ? ex[w][lane + 32 * t] : kEmptyKey;
+        key_cx(v[0], v[1]); key_cx(v[2], v[3]); key_cx(v[0], v[2]); key_cx(v[1], v[3]); key_cx(v[1], v[2]);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const unsigned long long mn = warp_min_u64(v[0]);
+            best[r] = mn;
+            if (v[0] == mn && mn != kEmptyKey) {
+                v[0] = v[1];
+                v[1] = v[2];
+                v[2] = v[3];
+                v[3] = kEmptyKey;
+            }
+        }
+    }
+    int count = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) count += best[i] != kEmptyKey;
+    const float d8 = count == 8 ? key_dist(best[7]) : inf;
+    const bool ok = !too_many && certify(tmin, d8, qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel,
+                                         a.norm_rel, a.exact_rel);
+    if (!ok) {
+        if (lane == 0) {
+            const int pos = atomicAdd(a.fallback_count, 1);
+            a.fallback_list[pos] = static_cast<int32_t>(frame);
+        }
+        return;
+    }
+    if (lane == 0 && a.counters) atomicAdd(&a.counters->candidate_frames, 1ull);
+    // lane k < 8: its neighbour's storage row (scan position -> probe -> row)
+    unsigned long long mine = kEmptyKey;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mine = lane == i ? best[i] : mine;
+    int32_t row = -1;
+    {
+        const uint32_t spos = key_pos(mine);
+        for (int pr = 0; pr < P; ++pr) {
+            const int32_t s = __shfl_sync(kFullMask, pstart, pr), t = __shfl_sync(kFullMask, pend, pr);
+            const uint32_t b = __shfl_sync(kFullMask, pbase, pr);
+            if (mine != kEmptyKey && spos >= b && spos < b + static_cast<uint32_t>(t - s))
+                row = s + static_cast<int32_t>(spos - b);
+        }
+    }
+    if (a.mode == kModeSearch) {
+        if (lane < a.k) {
+            const bool have = lane < count;
+            a.dist_out[frame * a.k + lane] = have ? key_dist(mine) : inf;
+            a.label_out[frame * a.k + lane] = have ? static_cast<int64_t>(a.ids[row]) + a.label_base : -1;
+        }
+        return;
+    }
+    if (count == 0) {
+        if (lane == 0 && a.counters) atomicAdd(&a.counters->empty_frames, 1ull);
+        if (dst != src)
+            for (int i = lane; i < d; i += 32) dst[i] = q[i];
+        return;
+    }
+    const double wk = lane < count ? reference_weight(key_dist(mine)) : 0.0;
+    double wv[8];
+    const float *vr[8];
+    double wsum = -0.0;  // the reference's order: S = w0 + w1 + ... (zeros past count)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        wv[k] = __shfl_sync(kFullMask, wk, k);
+        const int32_t rk = __shfl_sync(kFullMask, row, k);
+        vr[k] = a.vectors + static_cast<size_t>(rk >= 0 ? rk : 0) * d;
+        wsum = __dadd_rn(wsum, wv[k]);
+    }
+    const WeightDivisor sum = weight_divisor(wsum);
+    for (int i = lane; i < d; i += 32) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = k < count ? __ldg(vr[k] + i) : 0.f;
+        dst[i] = reference_blend_element<true>(q[i], v, wv, sum, count, ratio);
+    }
+}
+
+// coarse_select_warp_kernel: coarse_select_kernel's result with one warp per
+// frame, for launches whose frames have at most 32 coarse candidate lists
+// (one per lane; at most 16 keys each, ascending).  U = the nprobe-th
+// smallest key; every key whose lower bound can reach (U + ||q||^2 + e)(1 +
+// 4 exact_rel) is re-ranked with the exact centroid distance in the
+// reference order; the first nprobe by (distance total order, list id) --
+// crates/vocal-cpu/src/retrieval.rs:45-51 -- are certified against the
+// lists' thresholds, then recorded and counted per list.
+__global__ void __launch_bounds__(32 * kIvfWarps) coarse_select_warp_kernel(CoarseArgs a, long long frames) {
+    extern __shared__ __align__(16) float cq[];  // [kIvfWarps][dq]
+    __shared__ unsigned long long lists[kIvfWarps][32 * kItemKeep];
+    __shared__ unsigned long long sel[kIvfWarps][kRerankMax];
+    __shared__ unsigned long long ex[kIvfWarps][kRerankMax];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, octet = lane >> 3, j = lane & 7;
+    const long long frame = static_cast<long long>(blockIdx.x) * kIvfWarps + w;
+    if (frame >= frames) return;
+    const int d = a.d, P = a.nprobe;
+    const float *src = a.queries + frame * d;
+    const float inf = __int_as_float(0x7f800000);
+    if (a.mode == kModeBlend && !(load_ratio(a.index_rate) > 0.f)) {
+        // r <= 0: the frame is left as is (copied when out of place)
+        float *dst = a.out + frame * d;
+        if (dst != src)
+            for (int i = lane; i < d; i += 32) dst[i] = src[i];
+        if (lane == 0) a.probe_ok[frame] = 0;
+        return;
+    }
+    float *q = cq + static_cast<size_t>(w) * ((d + 3) & ~3);
+    unsigned long long *lk = lists[w];
+    for (int i = lane; i < d; i += 32) q[i] = src[i];
+    const unsigned long long *fk = a.keys + static_cast<size_t>(frame) * a.lists * kItemKeep;
+    int cnt = 0;
+    float thr = inf;
+    if (lane < a.lists) {
+        thr = a.thr[frame * a.thr_stride + lane];
+        for (int i = 0; i < kItemKeep; ++i) {  // slots past a list's count hold kEmptyKey
+            const unsigned long long k = fk[lane * kItemKeep + i];
+            lk[lane * kItemKeep + i] = k;
+            cnt += k != kEmptyKey;
+        }
+    }
+    float tmin = thr;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, o));
+    __syncwarp();
+    unsigned long long up = kEmptyKey;  // the P-th smallest approximate key
+    {
+        int head = 0;
+#pragma unroll 1
+        for (int r = 0; r < P; ++r) {
+            const unsigned long long c = head < cnt ? lk[lane * kItemKeep + head] : kEmptyKey;
+            const unsigned long long m = warp_min_u64(c);
+            if (c == m && m != kEmptyKey) ++head;
+            up = m;
+        }
+    }
+    const float4 qs = a.qstats[frame];
+    const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
+    const float limit = up == kEmptyKey ? inf : (key_dist(up) + qs.x + e) * (1.f + 4.f * a.exact_rel) + 1e-30f;
+    int kept = 0;
+    for (int i = 0; i < cnt; ++i) kept += !(key_dist(lk[lane * kItemKeep + i]) + qs.x - e > limit);
+    uint32_t kincl = static_cast<uint32_t>(kept);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t u = __shfl_up_sync(kFullMask, kincl, o);
+        if (lane >= o) kincl += u;
+    }
+    const int total = __shfl_sync(kFullMask, static_cast<int>(kincl), 31);
+    {
+        int at = static_cast<int>(kincl) - kept;
+        for (int i = 0; i < cnt; ++i) {
+            const unsigned long long k = lk[lane * kItemKeep + i];
+            if (!(key_dist(k) + qs.x - e > limit)) {
+                if (at < kRerankMax) sel[w][at] = k;
+                ++at;
+            }
+        }
+    }
+    const bool too_many = total > kRerankMax;
+    const int m = min(total, kRerankMax);
+    __syncwarp();
+    // exact centroid distances (every centroid takes part, as in the
+    // reference's sort: no +inf filter here)
+    for (int c0 = 0; c0 < m; c0 += 8) {
+        uint32_t ls[2];
+        const float *xs[2];
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 4 * kk;
+            ls[kk] = key_pos(sel[w][c < m ? c : c0]);
+            xs[kk] = a.centroids + static_cast<size_t>(ls[kk]) * d;
+        }
+        float dist[2];
+        octet_l2n<2>(q, xs, d, j, lane & ~7, kFullMask, dist);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 4 * kk;
+            if (j == 0 && c < m) ex[w][c] = make_key(dist[kk], ls[kk]);
+        }
+    }
+    __syncwarp();
+    // the first P exact keys: per lane keys lane, lane + 32, ... (sorted), P warp minima
+    unsigned long long top = kEmptyKey, pth = kEmptyKey;
+    {
+        unsigned long long v[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) v[t] = lane + 32 * t < m ? ex[w][lane + 32 * t] : kEmptyKey;
+        key_cx(v[0], v[1]); key_cx(v[2], v[3]); key_cx(v[0], v[2]); key_cx(v[1], v[3]); key_cx(v[1], v[2]);
+#pragma unroll 1
+        for (int r = 0; r < P; ++r) {
+            const unsigned long long mn = warp_min_u64(v[0]);
+            if (lane == r) top = mn;
+            pth = mn;
+            if (v[0] == mn && mn != kEmptyKey) {
+                v[0] = v[1];
+                v[1] = v[2];
+                v[2] = v[3];
+                v[3] = kEmptyKey;
+            }
+        }
+    }
+    bool ok = !too_many && m >= P && pth != kEmptyKey;
+    if (ok)
+        ok = certify(tmin, key_dist(pth), qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel,
+                     a.exact_rel);
+    if (lane == 0) {
+        a.probe_ok[frame] = ok ? 1 : 0;
+        if (!ok) {
+            const int pos = atomicAdd(a.fallback_count, 1);
+            a.fallback_list[pos] = static_cast<int32_t>(frame);
+        }
+    }
+    if (ok && lane < P) {
+        const int32_t list = static_cast<int32_t>(key_pos(top));
+        a.probes[frame * P + lane] = list;
+        atomicAdd(&a.list_count[list], 1);
+    }
+}
+
 struct IvfWs {
     size_t q16, qstats, ckeys, cthr, probes, probe_ok, list_count, list_cursor, list_start, items, item_count,
         pair_frame, pair_slot, qp, fkeys, fcounts, fthr, flist, fcount, total;
@@ -2459,6 +2810,13 @@ void build_tc(VfrIndex *ix) {
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, ix->merge_smem_max));
     }
     cuda_check(cudaFuncSetAttribute(coarse_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    if (ivf) {
+        // the warp-per-frame kernels: one frame row per warp in dynamic
+        // shared memory, beside their static per-warp key arrays
+        const int rows = kIvfWarps * ((ix->d + 3) & ~3) * static_cast<int>(sizeof(float));
+        cuda_check(cudaFuncSetAttribute(ivf_merge_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rows));
+        cuda_check(cudaFuncSetAttribute(coarse_select_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rows));
+    }
     {
         const char *env = std::getenv("VFR_SMALL_MERGE");
         ix->small_merge = !(env && env[0] == '0');
@@ -2609,8 +2967,13 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     cs.fallback_list = flist;
     cs.fallback_count = fcount;
     ix->prof.begin(kProfMerge, stream);
-    coarse_select_kernel<<<static_cast<unsigned>(frames), kMergeThreads,
-                           static_cast<size_t>(cs.slots) * 8 + static_cast<size_t>(ix->d) * 4, stream>>>(cs);
+    if (cs.lists <= 32)
+        coarse_select_warp_kernel<<<static_cast<unsigned>((frames + kIvfWarps - 1) / kIvfWarps), 32 * kIvfWarps,
+                                    static_cast<size_t>(kIvfWarps) * ((ix->d + 3) & ~3) * 4, stream>>>(
+            cs, static_cast<long long>(frames));
+    else
+        coarse_select_kernel<<<static_cast<unsigned>(frames), kMergeThreads,
+                               static_cast<size_t>(cs.slots) * 8 + static_cast<size_t>(ix->d) * 4, stream>>>(cs);
     cuda_check(cudaGetLastError());
     // 4. pairs bucketed by list, frames gathered into list order
     bucket_scan_kernel<<<1, 1024, 0, stream>>>(list_count, ix->list_order, ix->nlist, list_start, list_cursor, items,
@@ -2680,8 +3043,10 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     im.fallback_list = flist;
     im.fallback_count = fcount;
     im.counters = ix->counters;
+    im.frames = static_cast<long long>(frames);
     ix->prof.begin(kProfMerge, stream);
-    ivf_merge_kernel<<<static_cast<unsigned>(frames), kMergeThreads, static_cast<size_t>(ix->d) * 4, stream>>>(im);
+    ivf_merge_warp_kernel<<<static_cast<unsigned>((frames + kIvfWarps - 1) / kIvfWarps), 32 * kIvfWarps,
+                            static_cast<size_t>(kIvfWarps) * ((ix->d + 3) & ~3) * 4, stream>>>(im);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
 
