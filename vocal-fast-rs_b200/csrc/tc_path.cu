@@ -1893,14 +1893,16 @@ WsLayout ws_layout(size_t frames, int d_pad, int sms) {
 // ================================================================ IVF-Flat
 //
 // Coarse stage: cand_kernel<false> over the fp16 centroid shadow gives each
-// frame candidate lists of centroids; coarse_select_kernel re-ranks them with
+// frame candidate lists of centroids; coarse_select_warp_kernel (one warp
+// per frame; coarse_select_kernel, one CTA per frame, when a frame has more
+// than 32 candidate lists) re-ranks them with
 // exact fp32 distances in the reference order, keeps the first nprobe by
 // (distance total order, list id) -- crates/vocal-cpu/src/retrieval.rs:45-51 --
 // and certifies that no dropped centroid could enter them.  Fine stage: the
 // (frame, probe) pairs are bucketed by list, their fp16 frames gathered into
 // list order, cand_kernel<true> scans each list's rows for its pairs, and
-// ivf_merge_kernel re-ranks per frame with the scan position (probe rank,
-// storage row) as the tie order -- :52-64 -- then certifies and blends.
+// ivf_merge_warp_kernel re-ranks per frame with the scan position (probe
+// rank, storage row) as the tie order -- :52-64 -- then certifies and blends.
 // Frames left uncertified by either stage are re-run by the exact engine.
 
 constexpr int kIvfMaxProbe = 8;
@@ -2133,169 +2135,11 @@ struct IvfMergeArgs {
     DeviceCounters *counters;
 };
 
-__global__ void __launch_bounds__(kMergeThreads, 3) ivf_merge_kernel(IvfMergeArgs a) {
-    constexpr int kSlots = kIvfMaxProbe * kHalves * kItemKeep;
-    extern __shared__ __align__(16) float iq[];  // [d]
-    __shared__ unsigned long long keys[kSlots];
-    __shared__ SelectState sel;
-    __shared__ unsigned long long sel_keys[kRerankMax];
-    __shared__ unsigned long long octet_best[32 * 8];
-    __shared__ unsigned long long best[8];
-    __shared__ NarrowState narrow;
-    __shared__ int32_t pstart[kIvfMaxProbe], pend[kIvfMaxProbe];
-    __shared__ uint32_t pbase[kIvfMaxProbe + 1];
-    __shared__ int certified_s;
-    __shared__ int32_t best_row[8];
-    __shared__ double weights[8];
-    __shared__ double weight_sum;
-    const int tid = threadIdx.x, lane = tid & 31, octet = tid >> 3, j = tid & 7;
-    const long long frame = blockIdx.x;
-    if (!a.probe_ok[frame]) return;  // r <= 0 (handled) or exact re-run
-    const int d = a.d, P = a.nprobe;
-    const size_t stride = static_cast<size_t>(a.pair_stride);
-    const float *src = a.queries + frame * d;
-    float *dst = a.out + frame * d;
-    const float inf = __int_as_float(0x7f800000);
-    const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
-    for (int i = tid; i < d; i += kMergeThreads) iq[i] = src[i];
-    if (tid == 0) {
-        uint32_t acc = 0;
-        for (int p = 0; p < P; ++p) {
-            const int32_t list = a.probes[frame * P + p];
-            pstart[p] = a.offsets[list];
-            pend[p] = a.offsets[list + 1];
-            pbase[p] = acc;
-            acc += static_cast<uint32_t>(pend[p] - pstart[p]);
-        }
-        pbase[P] = acc;
-    }
-    float tmin = inf;
-    for (int i = tid; i < kSlots; i += kMergeThreads) {
-        const int p = i / (kHalves * kItemKeep), h = (i / kItemKeep) % kHalves, slot = i % kItemKeep;
-        unsigned long long key = kEmptyKey;
-        if (p < P) {
-            const size_t pos = static_cast<size_t>(a.pair_slot[frame * P + p]);
-            const int cnt = a.counts[h * stride + pos];
-            if (slot == 0) tmin = fminf(tmin, a.thr[h * stride + pos]);
-            if (slot < cnt) key = a.keys[(h * kItemKeep + slot) * stride + pos];
-        }
-        keys[i] = key;
-    }
-    const KeyStats ks = key_stats<kMergeThreads>(keys, kSlots, tmin, sel);
-    float cut;
-    bool too_many;
-    int m = select_rerank<kMergeThreads>(keys, kSlots, ks, sel_keys, sel, cut, too_many);
-    const float bound = fminf(ks.tmin, cut);
-    const float4 qs = a.qstats[frame];
-    m = narrow_rerank<kMergeThreads>(sel_keys, m, 8, qs.x,
-                                     approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel),
-                                     a.exact_rel, narrow);
-    // exact re-rank; the key's position is the reference's scan position
-    Top8 top;
-    top.init();
-    for (int c0 = 0; c0 < m; c0 += 64) {
-        uint32_t rows[2];
-        const float *xs[2];
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-            const int c = c0 + octet + 32 * kk;
-            rows[kk] = key_pos(sel_keys[c < m ? c : 0]);
-            xs[kk] = a.vectors + static_cast<size_t>(rows[kk]) * d;
-        }
-        float dist[2];
-        octet_l2n<2>(iq, xs, d, j, lane & ~7, kFullMask, dist);
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-            const uint32_t row = rows[kk];
-            if (c0 + octet + 32 * kk < m && dist[kk] < inf) {
-                int p = 0;
-                while (p + 1 < P && !(static_cast<int32_t>(row) >= pstart[p] && static_cast<int32_t>(row) < pend[p]))
-                    ++p;
-                top.insert(make_key(dist[kk], pbase[p] + (row - static_cast<uint32_t>(pstart[p]))));
-            }
-        }
-    }
-    if (j == 0)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) octet_best[octet * 8 + i] = top.k[i];
-    __syncthreads();
-    merge_octet_lists<32>(octet_best, best);
-    if (tid == 0) {
-        int count = 0;
-        while (count < 8 && best[count] != kEmptyKey) ++count;
-        const float d8 = count == 8 ? key_dist(best[7]) : inf;
-        const bool ok = !too_many && certify(bound, d8, qs, a.max_norm, a.max_hat, a.max_residual,
-                                             a.acc_rel, a.norm_rel, a.exact_rel);
-        certified_s = ok ? count + 1 : 0;
-    }
-    if (tid < 8) {
-        int32_t row = -1;
-        const unsigned long long key = best[tid];
-        if (key != kEmptyKey) {
-            const uint32_t pos = key_pos(key);
-            int p = 0;
-            while (p + 1 < P && pbase[p + 1] <= pos) ++p;
-            row = pstart[p] + static_cast<int32_t>(pos - pbase[p]);
-        }
-        best_row[tid] = row;
-    }
-    __syncthreads();
-    const int cert = certified_s;
-    if (cert == 0) {
-        if (tid == 0) {
-            const int pos = atomicAdd(a.fallback_count, 1);
-            a.fallback_list[pos] = static_cast<int32_t>(frame);
-        }
-        return;
-    }
-    const int count = cert - 1;
-    if (tid == 0 && a.counters) atomicAdd(&a.counters->candidate_frames, 1ull);
-    if (a.mode == kModeSearch) {
-        if (tid < a.k) {
-            const bool have = tid < count;
-            a.dist_out[frame * a.k + tid] = have ? key_dist(best[tid]) : inf;
-            a.label_out[frame * a.k + tid] = have ? static_cast<int64_t>(a.ids[best_row[tid]]) + a.label_base : -1;
-        }
-        return;
-    }
-    if (count == 0) {
-        if (tid == 0 && a.counters) atomicAdd(&a.counters->empty_frames, 1ull);
-        if (dst != src)
-            for (int i = tid; i < d; i += kMergeThreads) dst[i] = iq[i];
-        return;
-    }
-    if (tid == 0) {
-        float dist[8];
-        double w[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) dist[i] = key_dist(best[i]);
-        weight_sum = reference_weights(dist, count, w);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) weights[i] = w[i];
-    }
-    __syncthreads();
-    double w[8];
-    int32_t rows[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        w[i] = weights[i];
-        rows[i] = best_row[i];
-    }
-    const WeightDivisor sum = weight_divisor(weight_sum);
-    for (int i = tid; i < d; i += kMergeThreads) {
-        float v[8];
-#pragma unroll
-        for (int kq = 0; kq < 8; ++kq)
-            v[kq] = kq < count ? __ldg(a.vectors + static_cast<size_t>(rows[kq]) * d + i) : 0.f;
-        dst[i] = reference_blend_element(iq[i], v, w, sum, count, ratio);
-    }
-}
-
 // ---------------------------------------------------------------- IVF merge, one warp per frame
 //
-// ivf_merge_warp_kernel: ivf_merge_kernel's result with one warp per frame
-// and no CTA-wide barrier, so a launch of many frames keeps a few dozen
-// frames in flight per SM instead of three.  Per frame: lane 2p + h loads the
+// ivf_merge_warp_kernel: one warp per frame and no CTA-wide barrier, so a
+// launch of many frames keeps a few dozen frames in flight per SM (a CTA per
+// frame with CTA-wide selection passes kept three).  Per frame: lane 2p + h loads the
 // candidate list (probe p, column half h; at most 16 keys, ascending) into
 // its warp's shared slots; U = the 8th smallest key of all lists (a warp
 // merge of the list heads); the re-rank set is every key whose lower bound
