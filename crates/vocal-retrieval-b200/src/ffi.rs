@@ -373,6 +373,13 @@ unsafe extern "C" {
         error: *mut *mut c_char,
     ) -> i32;
     pub fn vfr_peer_rows_close(peers: *mut VfrPeerRows);
+    pub fn vfr_selftest_bounded_wait(
+        limit_ns: u64,
+        arrive: i32,
+        timed_out: *mut i32,
+        elapsed_ns: *mut u64,
+        error: *mut *mut c_char,
+    ) -> i32;
     pub fn vfr_blend_peer(
         peers: *mut VfrPeerRows,
         queries: *const f32,

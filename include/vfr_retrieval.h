@@ -375,6 +375,14 @@ VFR_API int vfr_blend_peer(VfrPeerRows *peers, const float *queries, float *out,
                            const int64_t *labels, size_t frames, int32_t width, const float *index_rate,
                            VfrStream *stream, char **error);
 
+/* Self-test of the bounded wait every mbarrier wait in the library's kernels
+ * uses (no counterpart in the reference): one thread waits on a barrier that
+ * only `arrive` != 0 completes, giving up after limit_ns (at most 2 s).
+ * *timed_out = 1 when the wait gave up, 0 when the phase completed;
+ * *elapsed_ns = the device time the wait took.  Synchronous; allocates. */
+VFR_API int vfr_selftest_bounded_wait(uint64_t limit_ns, int32_t arrive, int32_t *timed_out, uint64_t *elapsed_ns,
+                                      char **error);
+
 #ifdef __cplusplus
 }
 #endif

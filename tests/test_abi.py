@@ -72,3 +72,24 @@ def test_blend_argument_validation(native):
     native.vfr_free_error(ctypes.cast(err, ctypes.c_void_p))
     # diagnostics of a null handle is a no-op
     assert native.vfr_retrieval_diagnostics(None, None, 0) == 0
+
+
+@pytest.mark.gpu
+def test_bounded_wait_gives_up_and_reports(cuda):
+    """The bounded mbarrier wait every kernel of the library uses: waiting on
+    a barrier nothing completes returns a timeout status after the limit
+    (the context stays usable), and a completed phase returns at once."""
+    import ctypes
+
+    from vfr import lib
+
+    L = lib.load_library()
+    flag, ns = ctypes.c_int32(-1), ctypes.c_uint64(0)
+    lib.call(L.vfr_selftest_bounded_wait, 50_000_000, 0, ctypes.byref(flag), ctypes.byref(ns))
+    assert flag.value == 1
+    assert 50_000_000 <= ns.value < 1_000_000_000
+    lib.call(L.vfr_selftest_bounded_wait, 50_000_000, 1, ctypes.byref(flag), ctypes.byref(ns))
+    assert flag.value == 0 and ns.value < 50_000_000
+    # the device still runs work afterwards
+    t = cuda.arange(8, device="cuda", dtype=cuda.float32)
+    assert float(t.sum().item()) == 28.0

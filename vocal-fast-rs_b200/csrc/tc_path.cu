@@ -66,20 +66,21 @@ constexpr int kSmallBlock = 32;  // frame blocks up to this size use the spread 
 //
 // kFullLayout: 128 query rows per tile, 4 stages of (A 16 KB, B 32 KB).
 //
-// kSpreadLayout (blocks of at most 32 frames): the frames go to A rows
-// 0-7, 32-39, 64-71 and 96-103 (four TMA boxes of 8 rows), so all four lane
-// quarters, and all eight epilogue warps on four sub-partitions, share the
-// per-tile filtering that otherwise falls on two warps of one.  The 1 KB
-// A blocks of four stages interleave in one 16 KB pack (stage s at s KB,
-// quarter q at +4q KB); the MMA's other A rows read whatever lies there
-// (their TMEM lanes are never read).  Six stages: two packs (the second
-// pack's free 2 KB pieces hold the row-norm buffers) and six 32 KB B tiles,
-// 192 KB of database tiles in flight per SM.
+// kSpreadLayout (blocks of at most 32 frames): an M = 64 MMA whose A rows
+// 0-7, 16-23, 32-39 and 48-55 hold the frames (four TMA boxes of 8 rows);
+// those rows land on TMEM lanes 0-7, 32-39, 64-71 and 96-103, so all four
+// lane quarters, and all eight epilogue warps on four sub-partitions, share
+// the per-tile filtering that otherwise falls on two warps of one.  The 1 KB
+// A blocks of two stages interleave in one 8 KB pack (stage s at s KB,
+// quarter q at +2q KB); the MMA's other A rows read whatever lies there
+// (their TMEM lanes are never read).  Six stages: three packs, the row-norm
+// buffers, and six 32 KB B tiles, 192 KB of database tiles in flight per SM.
 enum { kFullLayout = 0, kSpreadLayout = 1 };
 template <int kLayout>
 struct Pipe;
 template <>
 struct Pipe<kFullLayout> {
+    static constexpr int kM = kTileM;
     static constexpr int kStages = 4;
     static constexpr int kBlocks = 1;            // A boxes per stage
     static constexpr int kBlockRows = kTileM;    // rows per A box
@@ -94,20 +95,26 @@ struct Pipe<kFullLayout> {
 };
 template <>
 struct Pipe<kSpreadLayout> {
+    // M = 64: the MMA's 64 A rows land on TMEM lanes 0-15, 32-47, 64-79 and
+    // 96-111 (16 per lane quarter), so frames at A rows 0-7, 16-23, 32-39 and
+    // 48-55 reach lanes 0-7, 32-39, 64-71 and 96-103, as the epilogue reads
+    // them; half the MMA work of M = 128 for the same 32 frames.
+    static constexpr int kM = 64;
     static constexpr int kStages = 6;
     static constexpr int kBlocks = 4;
     static constexpr int kBlockRows = 8;
     static constexpr int kRowsPerQuarter = 8;
     static constexpr uint32_t kTx = 4 * 1024 + kBBytes;
-    __host__ __device__ static constexpr uint32_t a_off(int s) { return (s / 4) * 16384u + (s % 4) * 1024u; }
-    __host__ __device__ static constexpr uint32_t a_block_off(int s, int q) { return a_off(s) + q * 4096u; }
+    // the 1 KB A blocks of two stages interleave in an 8 KB pack (stage s at
+    // s KB, quarter q at +2q KB); three packs, then the row-norm buffers
+    __host__ __device__ static constexpr uint32_t a_off(int s) { return (s / 2) * 8192u + (s % 2) * 1024u; }
+    __host__ __device__ static constexpr uint32_t a_block_off(int s, int q) { return a_off(s) + q * 2048u; }
     __host__ __device__ static constexpr uint32_t b_off(int s) { return 32768u + s * kBBytes; }
-    __host__ __device__ static constexpr uint32_t norm_off(int ew) {
-        return 16384u + (ew / 2) * 4096u + 2048u + (ew % 2) * 1024u;
-    }
+    __host__ __device__ static constexpr uint32_t norm_off(int ew) { return 24576u + ew * 1024u; }
     static constexpr uint32_t kBarOff = 32768u + kStages * kBBytes;
     static constexpr size_t kSmem = 1024 + kBarOff + 256;
 };
+static_assert((Pipe<kSpreadLayout>::kStages + 1) / 2 * 8192u <= 24576u, "A packs below the norm buffers");
 static_assert(Pipe<kFullLayout>::kSmem <= 232448 && Pipe<kSpreadLayout>::kSmem <= 232448, "cand_kernel shared memory");
 static_assert(kNormBytes == kEpiWarps * 1024, "one 1 KB row-norm double buffer per epilogue warp");
 constexpr uint32_t kTmemCols = 512;  // two 128 x 256 fp32 accumulators
@@ -142,6 +149,15 @@ struct CandArgs {
     const int32_t *list_start;    // pair offsets [nlist + 1] (lists in size order, not id order)
     const int32_t *list_count;    // pairs per list [nlist]
     int pair_stride;              // output stride: pairs capacity
+    // Flat only (null: off): a per-frame filter bound shared by every CTA
+    // (total-order bits of an approximate distance d~, +inf at call start).
+    // A list whose 8 best so far have d~ <= u publishes u + 2e + slack: no
+    // row at or above it can enter or tie the frame's exact top 8, so every
+    // CTA may drop such rows; the list's reported threshold then becomes
+    // min(its K-th best, the bound it used), which keeps the certificate.
+    unsigned int *gbound;
+    const float4 *qstats;  // (||q||^2, ||q^||, ||q - q^||) per frame
+    float max_norm, max_hat, max_residual, acc_rel, norm_rel, exact_rel;
 };
 
 // One work item: A rows [a_row0, a_row0 + a_rows) against database rows
@@ -272,6 +288,18 @@ struct TopList {
     }
 };
 
+// The frame's exactness certificate: every dropped candidate has an
+// approximate distance >= bound; qs = (||q||^2, ||q^||, ||q - q^||); the
+// database bounds are max ||x||, max ||x^||, max ||x - x^||.  True when no
+// dropped candidate can reach (or tie) the `rank`-th exact distance dk.
+// The bound e on |(d~ + ||q||^2) - true distance| for an approximate key
+// distance d~ of this frame (the certificate's error model).
+__device__ __forceinline__ float approx_error(float4 qs, float max_norm, float max_hat, float max_residual,
+                                              float acc_rel, float norm_rel) {
+    return 2.f * (qs.y * max_residual + qs.z * max_norm) + 2.f * acc_rel * qs.y * max_hat +
+           norm_rel * (max_norm * max_norm + qs.x) + 6e-8f * (max_norm * max_norm + 2.f * qs.y * max_hat);
+}
+
 // Four consecutive row norms.  Flat segments start on tile boundaries, so the
 // address is 16-byte aligned; IVF lists start anywhere.
 template <bool kIvf>
@@ -397,7 +425,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer (one thread)
-            const uint32_t idesc = tc::idesc_f16(kTileM, kTileN, kFormatF16);
+            const uint32_t idesc = tc::idesc_f16(P::kM, kTileN, kFormatF16);
             int stage = 0;
             uint32_t phase = 0;
             uint32_t acc_count = 0;
@@ -460,6 +488,20 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             TopList<K> top;
             top.init();
             bool aborted = false;
+            // the frame's shared filter bound (flat, when enabled): read at
+            // every tile, published when this list's 8th best improves
+            unsigned int *gp = nullptr;
+            float g = inf, qe = 0.f, two_e = 0.f, published = inf;
+            if constexpr (!kIvf) {
+                if (a.gbound != nullptr && lane_real && r < it.a_rows) {
+                    const long long fr = static_cast<long long>(it.a_row0) + r;
+                    const float4 qs = a.qstats[fr];
+                    const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
+                    gp = a.gbound + fr;
+                    qe = qs.x + e;
+                    two_e = 2.f * e;
+                }
+            }
             // This warp's copy of the row norms, one tile ahead: lane l holds
             // norms [4l, 4l+4) of the next tile's half in registers until the
             // current tile is done, then stores them into the other buffer.
@@ -473,6 +515,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 const uint32_t tile_row = static_cast<uint32_t>(row0 + static_cast<int64_t>(t) * kTileN);
                 float4 pre0 = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (t + 1 < tiles) pre0 = load_norms4<kIvf>(a.row_norms + tile_row + kTileN + half * kHalfCols + lane * 4);
+                if (gp != nullptr) g = from_total_order_bits(__ldcg(gp));
                 // every lane polls; the outcome is made warp-uniform before the
                 // .sync.aligned TMEM loads
                 const bool ready = tc::mbar_wait(&acc_full[b], (acc_count >> 1) & 1, kWaitLimitNs);
@@ -506,10 +549,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                         __syncwarp();
                         tc::tmem_ld16_nowait(tcol + (c + 1) * 16, v[cur ^ 1]);
                     }
-                    // branch-free filter against the threshold at chunk start
+                    // filter against the threshold at chunk start: the chunk's
+                    // minimum first, and the survivor mask only when some lane
+                    // of the warp has a survivor (in steady state most chunks
+                    // have none, and the vote is warp-uniform)
                     float dd[16];
                     uint32_t mask = 0;
-                    const float thr = top.dist[K - 1];
+                    const float thr = fminf(top.dist[K - 1], g);
                     // IVF: rows past the list's end belong to the next list
                     const int64_t lim = kIvf ? it.b_end - (static_cast<int64_t>(col_row) + c * 16) : 16;
 #pragma unroll
@@ -521,14 +567,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                             const int e = e4 * 4 + u;
                             dd[e] = fmaf(a.coef, v[cur][e], nv[u]);
                             if constexpr (kIvf) dd[e] = e < lim ? dd[e] : inf;
-                            mask |= (dd[e] < thr ? 1u : 0u) << e;
                         }
                     }
-                    if (!lane_real) mask = 0u;  // no frame in this lane: its values are not distances
+                    float lo8[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) lo8[e] = fminf(dd[e], dd[e + 8]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) lo8[e] = fminf(lo8[e], lo8[e + 4]);
+                    const float cmin = fminf(fminf(lo8[0], lo8[2]), fminf(lo8[1], lo8[3]));
+                    // lanes with no frame hold no distances (spread layout)
+                    const bool survive = __any_sync(kFullMask, lane_real && cmin < thr);  // warp-uniform
+                    if (survive) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) mask |= (dd[e] < thr ? 1u : 0u) << e;
+                        if (!lane_real) mask = 0u;
+                    }
                     // many survivors (the start of an item): one bulk merge for
                     // the warp; otherwise insert the few survivors one by one
                     // (re-checked, the threshold drops as they go in)
-                    if (__reduce_max_sync(kFullMask, static_cast<unsigned>(__popc(mask))) >= 6u) {
+                    if (survive && __reduce_max_sync(kFullMask, static_cast<unsigned>(__popc(mask))) >= 6u) {
                         uint32_t cr[16];
 #pragma unroll
                         for (int e = 0; e < 16; ++e) cr[e] = col_row + c * 16 + e;
@@ -549,6 +606,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
                 ++acc_count;
+                if (gp != nullptr && top.dist[7] < published) {
+                    // the list's 8 best bound the frame's 8th best from above:
+                    // u + 2e + slack is a d~ no row of the exact top 8 reaches
+                    const float u = top.dist[7];
+                    published = u;
+                    const float bound = u + two_e + (8.f * a.exact_rel * fabsf(u + qe) + 1e-6f * (fabsf(u) + fabsf(qe)) + 1e-30f);
+                    atomicMin(gp, total_order_bits(bound));
+                }
                 if (t + 1 < tiles) {
                     reinterpret_cast<float4 *>(nbuf + ((t + 1) & 1) * kHalfCols)[lane] = pre0;
                     __syncwarp();
@@ -578,7 +643,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 for (int i = 0; i < K; i += 2)
                     dk[i / 2] = make_ulonglong2(i < cnt ? make_key(top.dist[i], top.row[i]) : kEmptyKey,
                                                 i + 1 < cnt ? make_key(top.dist[i + 1], top.row[i + 1]) : kEmptyKey);
-                a.out_thr[frame * a.thr_stride + list] = cnt == K ? top.dist[K - 1] : inf;
+                // rows this list dropped have d~ >= min(its K-th best, the
+                // smallest shared bound it filtered with: the last one read)
+                a.out_thr[frame * a.thr_stride + list] = fminf(cnt == K ? top.dist[K - 1] : inf, g);
             }
         }
     }
@@ -592,7 +659,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
 // ---------------------------------------------------------------- queries
 __global__ void prep_queries_kernel(const float *__restrict__ q, __half *__restrict__ qh, float4 *__restrict__ stats,
-                                    long long frames, int d, int d_pad, float scale, int32_t *zero) {
+                                    long long frames, int d, int d_pad, float scale, int32_t *zero,
+                                    unsigned int *gbound) {
     launch_dependents();  // the candidate kernel may start its prologue and database loads now
     if (blockIdx.x == 0 && threadIdx.x == 0 && zero) *zero = 0;  // the call's fallback frame count
     const long long f = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -618,7 +686,10 @@ __global__ void prep_queries_kernel(const float *__restrict__ q, __half *__restr
         hat2 += __shfl_xor_sync(kFullMask, hat2, s);
         res2 += __shfl_xor_sync(kFullMask, res2, s);
     }
-    if (lane == 0) stats[f] = make_float4(qn2, sqrtf(hat2) * 1.00001f, sqrtf(res2) * 1.00001f, 0.f);
+    if (lane == 0) {
+        stats[f] = make_float4(qn2, sqrtf(hat2) * 1.00001f, sqrtf(res2) * 1.00001f, 0.f);
+        if (gbound) gbound[f] = total_order_bits(__int_as_float(0x7f800000));
+    }
 }
 
 // ---------------------------------------------------------------- merge
@@ -961,18 +1032,6 @@ __device__ __forceinline__ void merge_octet_lists(const unsigned long long *octe
         }
     }
     __syncthreads();
-}
-
-// The frame's exactness certificate: every dropped candidate has an
-// approximate distance >= bound; qs = (||q||^2, ||q^||, ||q - q^||); the
-// database bounds are max ||x||, max ||x^||, max ||x - x^||.  True when no
-// dropped candidate can reach (or tie) the `rank`-th exact distance dk.
-// The bound e on |(d~ + ||q||^2) - true distance| for an approximate key
-// distance d~ of this frame (the certificate's error model).
-__device__ __forceinline__ float approx_error(float4 qs, float max_norm, float max_hat, float max_residual,
-                                              float acc_rel, float norm_rel) {
-    return 2.f * (qs.y * max_residual + qs.z * max_norm) + 2.f * acc_rel * qs.y * max_hat +
-           norm_rel * (max_norm * max_norm + qs.x) + 6e-8f * (max_norm * max_norm + 2.f * qs.y * max_hat);
 }
 
 __device__ __forceinline__ bool certify(float bound, float dk, float4 qs, float max_norm, float max_hat,
@@ -1456,7 +1515,7 @@ constexpr int kSmallStageMin = 16;  // fewer stage rows than this: merge_kernel 
 constexpr int kSmallStageMax = 64;
 
 template <int kT>
-__global__ void __launch_bounds__(kT, 1) merge_small_kernel(MergeArgs a) {
+__global__ void __launch_bounds__(kT, kT == kMergeThreadsMax ? 1 : 2) merge_small_kernel(MergeArgs a) {
     constexpr int kOct = kT / 8;
     constexpr int kWarps = kT / 32;
     extern __shared__ __align__(16) uint8_t msm[];
@@ -1607,7 +1666,7 @@ __global__ void __launch_bounds__(kT, 1) merge_small_kernel(MergeArgs a) {
     // memory, any others from global memory (flat scan position == row)
     // (a warp whose four octets have no staged row skips the pass: the
     // chains are long and issue-bound, so idle octets would slow the rest)
-    static_assert(kSmallStageMax <= kOct, "one staged row per octet");
+    // (stage_rows never exceeds the octets: the host caps it at kOct)
     if (warp * 4 < staged)
         stage_distances<1, kOct>(q, stage, stride, staged, 0, d, octet, j, lane, sel_keys, exact_keys);
     if (staged < m) global_distances<kOct>(a, q, staged, m, sel_keys, exact_keys);
@@ -1777,13 +1836,26 @@ void launch_merge(VfrIndex *ix, MergeArgs &ma, size_t frames, cudaStream_t strea
     const bool few = ix->d % 4 == 0 && reinterpret_cast<uintptr_t>(ix->vectors) % 16 == 0 &&
                      frames <= static_cast<size_t>(ix->sm_count) * 2;
     if (few && ix->small_merge) {
-        // merge_small_kernel, with as many stage rows as fit (at least kSmallStageMin)
-        for (int rows = kSmallStageMax; rows >= kSmallStageMin; --rows) {
+        // merge_small_kernel, with as many stage rows as fit (at least
+        // kSmallStageMin): 512 threads (one CTA per SM) when every frame
+        // has an SM of its own, else 256 threads and half the shared
+        // memory each, so two CTAs per SM take the launch in one wave
+        const bool one_wave = frames <= static_cast<size_t>(ix->sm_count);
+        const int max_rows = one_wave ? kSmallStageMax : kMergeThreads / 8;
+        // two CTAs: half the SM's shared memory each, less the per-CTA
+        // reservation and static arrays (4 KB covers both)
+        const size_t budget = one_wave ? static_cast<size_t>(ix->merge_smem_max)
+                                       : static_cast<size_t>(ix->merge_smem_max) / 2 - 4096;
+        for (int rows = max_rows; rows >= kSmallStageMin; --rows) {
             const size_t need = small_smem(ma.sort_size, ma.thr_stride, ix->d, rows).total;
-            if (need <= static_cast<size_t>(ix->merge_smem_max)) {
+            if (need <= budget) {
                 ma.stage_rows = rows;
-                cuda_check(launch_pdl(merge_small_kernel<kMergeThreadsMax>, dim3(static_cast<unsigned>(frames)),
-                                      dim3(kMergeThreadsMax), need, stream, ma));
+                if (one_wave)
+                    cuda_check(launch_pdl(merge_small_kernel<kMergeThreadsMax>, dim3(static_cast<unsigned>(frames)),
+                                          dim3(kMergeThreadsMax), need, stream, ma));
+                else
+                    cuda_check(launch_pdl(merge_small_kernel<kMergeThreads>, dim3(static_cast<unsigned>(frames)),
+                                          dim3(kMergeThreads), need, stream, ma));
                 return;
             }
         }
@@ -1825,6 +1897,19 @@ void launch_cand_flat(const Plan &p, int grid, const void *q16, int d_pad, const
     cuda_check(launch_pdl(kernel, dim3(grid), dim3(kThreadsTC), smem, stream, tmap_q, tmap_x, ca));
 }
 
+// The shared filter bound of a flat call: per-frame bounds, the frames'
+// stats and the index's certificate constants.
+void set_shared_bound(CandArgs &ca, const VfrIndex *ix, unsigned int *gbound, const float4 *qstats) {
+    ca.gbound = gbound;
+    ca.qstats = qstats;
+    ca.max_norm = ix->max_row_norm;
+    ca.max_hat = ix->max_row_hat;
+    ca.max_residual = ix->max_row_residual;
+    ca.acc_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -22);
+    ca.norm_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -23);
+    ca.exact_rel = static_cast<float>(ix->d / 8 + 9) * std::ldexp(1.0f, -24);
+}
+
 Plan make_plan(size_t frames, int64_t n, int sms) {
     Plan p{};
     p.n_qtiles = static_cast<int>((frames + kTileM - 1) / kTileM);
@@ -1864,7 +1949,7 @@ int64_t items_cap(size_t frames, int sms) {
 }
 
 struct WsLayout {
-    size_t q16, qstats, keys, thr, flist, fcount, total;
+    size_t q16, qstats, keys, thr, flist, fcount, gbound, total;
 };
 
 WsLayout ws_layout(size_t frames, int d_pad, int sms) {
@@ -1886,6 +1971,8 @@ WsLayout ws_layout(size_t frames, int d_pad, int sms) {
     off = align256(off + fr * sizeof(int32_t));
     l.fcount = off;
     off = align256(off + 16);
+    l.gbound = off;
+    off = align256(off + fr * sizeof(unsigned int));
     l.total = off;
     return l;
 }
@@ -2640,17 +2727,20 @@ void build_tc(VfrIndex *ix) {
     {
         int optin = 0;
         cuda_check(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ix->device));
-        cudaFuncAttributes fa{}, fb{}, fc{};
+        cudaFuncAttributes fa{}, fb{}, fc{}, fd{};
         cuda_check(cudaFuncGetAttributes(&fa, merge_kernel<kMergeThreads>));
         cuda_check(cudaFuncGetAttributes(&fb, merge_kernel<kMergeThreadsMax>));
         cuda_check(cudaFuncGetAttributes(&fc, merge_small_kernel<kMergeThreadsMax>));
-        ix->merge_smem_max =
-            optin - static_cast<int>(std::max({fa.sharedSizeBytes, fb.sharedSizeBytes, fc.sharedSizeBytes}));
+        cuda_check(cudaFuncGetAttributes(&fd, merge_small_kernel<kMergeThreads>));
+        ix->merge_smem_max = optin - static_cast<int>(std::max(
+                                         {fa.sharedSizeBytes, fb.sharedSizeBytes, fc.sharedSizeBytes, fd.sharedSizeBytes}));
         cuda_check(cudaFuncSetAttribute(merge_kernel<kMergeThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         ix->merge_smem_max));
         cuda_check(cudaFuncSetAttribute(merge_kernel<kMergeThreadsMax>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         ix->merge_smem_max));
         cuda_check(cudaFuncSetAttribute(merge_small_kernel<kMergeThreadsMax>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, ix->merge_smem_max));
+        cuda_check(cudaFuncSetAttribute(merge_small_kernel<kMergeThreads>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, ix->merge_smem_max));
     }
     cuda_check(cudaFuncSetAttribute(coarse_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
@@ -2749,7 +2839,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     const long long lanes = static_cast<long long>(frames) * 32;
     ix->prof.begin(kProfPrep, stream);
     prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
-        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount);
+        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount, nullptr);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
     cuda_check(cudaMemsetAsync(list_count, 0, static_cast<size_t>(ix->nlist) * sizeof(int32_t), stream));
@@ -2950,12 +3040,13 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     float *thr = reinterpret_cast<float *>(ws + l.thr);
     int32_t *flist = reinterpret_cast<int32_t *>(ws + l.flist);
     int32_t *fcount = reinterpret_cast<int32_t *>(ws + l.fcount);
+    unsigned int *gbound = reinterpret_cast<unsigned int *>(ws + l.gbound);
 
     const Plan p = make_plan(frames, ix->n, ix->sm_count);
     const long long lanes = static_cast<long long>(frames) * 32;
     ix->prof.begin(kProfPrep, stream);
     prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
-        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount);
+        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount, gbound);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
 
@@ -2974,6 +3065,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ca.lists = p.segments * kHalves;
     ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
+    set_shared_bound(ca, ix, gbound, qstats);
     const int items = p.segments * p.n_qtiles;
     const int grid = std::min(items, ix->sm_count);
     note_plan(ix, p, frames);
@@ -3070,7 +3162,8 @@ constexpr size_t kNoAllocLists = static_cast<size_t>(kNoAllocMaxItems) * kHalves
 constexpr size_t kNoAllocThr = kNoAllocKeys + kNoAllocLists * kItemKeep * kTileM * sizeof(unsigned long long);
 constexpr size_t kNoAllocList = kNoAllocThr + (kNoAllocLists * kTileM + kNoAllocMaxFrames * 4) * sizeof(float);
 constexpr size_t kNoAllocCount = kNoAllocList + kNoAllocMaxFrames * sizeof(int32_t);
-constexpr size_t kNoAllocBytes = kNoAllocCount + 256;
+constexpr size_t kNoAllocBound = kNoAllocCount + 256;
+constexpr size_t kNoAllocBytes = kNoAllocBound + kNoAllocMaxFrames * sizeof(unsigned int);
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
@@ -3121,12 +3214,13 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     float *thr = reinterpret_cast<float *>(ws + kNoAllocThr);
     int32_t *flist = reinterpret_cast<int32_t *>(ws + kNoAllocList);
     int32_t *fcount = reinterpret_cast<int32_t *>(ws + kNoAllocCount);
+    unsigned int *gbound = reinterpret_cast<unsigned int *>(ws + kNoAllocBound);
 
     const Plan p = make_plan_noalloc(frames, ix->n, ix->sm_count);
     require(p.segments > 0, "no-allocation scratch cannot hold this plan");
     const long long lanes = static_cast<long long>(frames) * 32;
     prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
-        features, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount);
+        features, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount, gbound);
     cuda_check(cudaGetLastError());
 
     CandArgs ca{};
@@ -3144,6 +3238,7 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ca.lists = p.segments * kHalves;
     ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
+    set_shared_bound(ca, ix, gbound, qstats);
     const int items = p.segments * p.n_qtiles;
     note_plan(ix, p, frames);
     launch_cand_flat(p, std::min(items, ix->sm_count), q16, ix->d_pad, ix->tmap_vectors, ca, stream);

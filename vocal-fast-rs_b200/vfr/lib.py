@@ -118,6 +118,7 @@ def load_library(path: str | None = None):
         "vfr_peer_rows_open": ([vp, i32, P(IpcRows), i32, P(vp), err], ctypes.c_int),
         "vfr_peer_rows_close": ([vp], None),
         "vfr_blend_peer": ([vp, vp, vp, vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
+        "vfr_selftest_bounded_wait": ([ctypes.c_uint64, i32, P(i32), P(ctypes.c_uint64), err], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
