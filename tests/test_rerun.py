@@ -3,7 +3,7 @@ engine).  Frames whose candidate set cannot be certified -- here more than
 kRerankMax rows at exactly the same distance -- are re-run exactly; when at
 most 64 frames fall back, each frame's probed rows are split across many
 CTAs and the slices' top-8 lists merged (exact_split), otherwise one CTA
-scans each frame.  Both must give the reference's results bit for bit:
+scans each frame.  400 frames put the merge on its one-warp-per-frame form.  Both must give the reference's results bit for bit:
 search (distances, scan-order ties, labels) and blend against the oracle
 (crates/vocal-cpu/src/retrieval.rs:27-83), flat and IVF.
 """
@@ -32,7 +32,7 @@ def tie_heavy(n, d, nlist, seed, copies=150, clusters=3):
 
 
 @pytest.mark.parametrize("nlist,nprobe", [(1, 1), (16, 4), (16, 8), (16, 16)])
-@pytest.mark.parametrize("frames,tied_frames", [(40, 10), (70, 70), (12, 1)])
+@pytest.mark.parametrize("frames,tied_frames", [(40, 10), (70, 70), (12, 1), (400, 100)])
 def test_rerun_matches_oracle(cuda, oracle, nlist, nprobe, frames, tied_frames):
     from vfr import GpuRetrievalIndex, lib
 

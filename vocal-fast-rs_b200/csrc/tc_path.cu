@@ -1161,8 +1161,11 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreads ? 3 : 1) merge_kernel(
     const float inf = __int_as_float(0x7f800000);
     const int real_slots = a.lists * a.keep;
 
-    // no early trigger: the exact kernel behind launches as these CTAs exit,
-    // so its CTAs never hold SM slots that merge CTAs still need
+    // the exact kernel behind launches once every CTA of this grid has
+    // started (so it takes no SM slot a merge CTA still needs) and waits for
+    // this grid's completion before it reads anything: its launch latency
+    // overlaps the merge
+    launch_dependents();
     if (tid == 0) {
         tc::mbar_init(&gather_bar, 1);
         tc::mbar_init(&stage_bar, 1);
@@ -1545,6 +1548,7 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreadsMax ? 1 : 2) merge_smal
     const float inf = __int_as_float(0x7f800000);
     const int real_slots = a.lists * a.keep;
     const int stride = stage_stride(d);
+    launch_dependents();  // as in merge_kernel: the exact kernel's launch overlaps this one
 
     if (tid == 0) {
         tc::mbar_init(&gather_bar, 1);
@@ -1734,6 +1738,182 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreadsMax ? 1 : 2) merge_smal
     }
 }
 
+// ---------------------------------------------------------------- flat merge, one warp per frame
+//
+// merge_warp_kernel: the flat merge of launches with more than two frames
+// per SM, one warp per frame and no CTA-wide barrier (8 frames per CTA).
+// The frame's candidate block (lists x keep keys; each list ascending,
+// kEmptyKey past its count) is read from global memory (L2: the candidate
+// kernel has just written it), once to find U, the 8th smallest key (each
+// lane keeps the 8 smallest of its slots in registers, then a warp merge),
+// and once to collect every key whose lower bound d~ + ||q||^2 - e does not
+// exceed (U + ||q||^2 + e)(1 + 4 exact_rel) -- the rows that may still
+// enter the exact top 8.  Octets compute their exact distances two rows at
+// a time in the reference's order (the flat scan position is the row), a
+// warp merge gives the top 8, and the lists' thresholds certify the rows the
+// candidate stage dropped, as in merge_kernel.
+constexpr int kMergeWarps = 8;
+
+__global__ void __launch_bounds__(32 * kMergeWarps, 3) merge_warp_kernel(MergeArgs a, long long frames) {
+    extern __shared__ __align__(16) float mwq[];  // [kMergeWarps][d rounded up to 4] frame rows
+    __shared__ unsigned long long sel[kMergeWarps][kRerankMax];
+    __shared__ unsigned long long ex[kMergeWarps][kRerankMax];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, octet = lane >> 3, j = lane & 7;
+    const long long frame = static_cast<long long>(blockIdx.x) * kMergeWarps + w;
+    launch_dependents();  // as in merge_kernel: the exact kernel's launch overlaps this one
+    if (frame >= frames) return;
+    const int d = a.d;
+    float *q = mwq + static_cast<size_t>(w) * ((d + 3) & ~3);
+    const float *src = a.queries + frame * d;
+    float *dst = a.out + frame * d;
+    const float inf = __int_as_float(0x7f800000);
+    // the caller's inputs first, while the candidate kernel may still run
+    const float ratio = a.mode == kModeBlend ? load_ratio(a.index_rate) : 1.f;
+    float *raw_row = a.raw_out ? a.raw_out + frame * d : nullptr;
+    for (int i = lane; i < d; i += 32) {
+        const float v = src[i];
+        q[i] = v;
+        if (raw_row) raw_row[i] = v;
+    }
+    __syncwarp();
+    grid_dependency_wait();
+    if (a.mode == kModeBlend && !(ratio > 0.f)) {
+        if (dst != src)
+            for (int i = lane; i < d; i += 32) dst[i] = q[i];
+        return;
+    }
+    const int slots = a.lists * a.keep;
+    const unsigned long long *fk = a.keys + static_cast<size_t>(frame) * slots;
+    float tmin = inf;
+    for (int l = lane; l < a.lists; l += 32) tmin = fminf(tmin, __ldcg(a.thr + frame * a.thr_stride + l));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, o));
+    // U: each lane's 8 smallest slots (sorted insertion), then 8 warp pops
+    unsigned long long v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = kEmptyKey;
+#pragma unroll 4
+    for (int i = lane; i < slots; i += 32) {
+        const unsigned long long k = __ldcg(fk + i);
+        if (k < v[7]) {
+            v[7] = k;
+#pragma unroll
+            for (int e = 6; e >= 0; --e) key_cx(v[e], v[e + 1]);
+        }
+    }
+    unsigned long long u8 = kEmptyKey;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const unsigned long long mn = warp_min_u64(v[0]);
+        u8 = mn;
+        if (v[0] == mn && mn != kEmptyKey) {
+#pragma unroll
+            for (int e = 0; e < 7; ++e) v[e] = v[e + 1];
+            v[7] = kEmptyKey;
+        }
+    }
+    const float4 qs = a.qstats[frame];
+    const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
+    const float limit = u8 == kEmptyKey ? inf : (key_dist(u8) + qs.x + e) * (1.f + 4.f * a.exact_rel) + 1e-30f;
+    // the re-rank set, in slot order
+    int total = 0;
+    for (int base = 0; base < slots; base += 32) {
+        const int i = base + lane;
+        const unsigned long long k = i < slots ? __ldcg(fk + i) : kEmptyKey;
+        const bool kept = k != kEmptyKey && !(key_dist(k) + qs.x - e > limit);
+        const unsigned ball = __ballot_sync(kFullMask, kept);
+        if (kept) {
+            const int pos = total + __popc(ball & ((1u << lane) - 1u));
+            if (pos < kRerankMax) sel[w][pos] = k;
+        }
+        total += __popc(ball);
+    }
+    const int m = min(total, kRerankMax);
+    __syncwarp();
+    for (int c0 = 0; c0 < m; c0 += 8) {
+        uint32_t rows[2];
+        const float *xs[2];
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 4 * kk;
+            rows[kk] = key_pos(sel[w][c < m ? c : c0]);
+            xs[kk] = a.vectors + static_cast<size_t>(rows[kk]) * d;
+        }
+        float dist[2];
+        octet_l2n<2>(q, xs, d, j, lane & ~7, kFullMask, dist);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int c = c0 + octet + 4 * kk;
+            if (j == 0 && c < m) ex[w][c] = dist[kk] < inf ? make_key(dist[kk], rows[kk]) : kEmptyKey;
+        }
+    }
+    __syncwarp();
+    // the exact top 8 (m <= 128: four keys a lane, sorted, then 8 pops)
+    unsigned long long best[8];
+    {
+        unsigned long long t[4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) t[s] = lane + 32 * s < m ? ex[w][lane + 32 * s] : kEmptyKey;
+        key_cx(t[0], t[1]); key_cx(t[2], t[3]); key_cx(t[0], t[2]); key_cx(t[1], t[3]); key_cx(t[1], t[2]);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const unsigned long long mn = warp_min_u64(t[0]);
+            best[r] = mn;
+            if (t[0] == mn && mn != kEmptyKey) {
+                t[0] = t[1];
+                t[1] = t[2];
+                t[2] = t[3];
+                t[3] = kEmptyKey;
+            }
+        }
+    }
+    int count = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) count += best[i] != kEmptyKey;
+    const float d8 = count == 8 ? key_dist(best[7]) : inf;
+    if (total > kRerankMax || !certify(tmin, d8, qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel,
+                                       a.exact_rel)) {
+        if (lane == 0) a.fallback_list[atomicAdd(a.fallback_count, 1)] = static_cast<int32_t>(frame);
+        return;
+    }
+    if (lane == 0 && a.counters) atomicAdd(&a.counters->candidate_frames, 1ull);
+    unsigned long long mine = kEmptyKey;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mine = lane == i ? best[i] : mine;
+    if (a.mode == kModeSearch) {
+        if (lane < a.k) {
+            const bool have = lane < count;
+            a.dist_out[frame * a.k + lane] = have ? key_dist(mine) : inf;
+            a.label_out[frame * a.k + lane] = have ? static_cast<int64_t>(a.ids[key_pos(mine)]) + a.label_base : -1;
+        }
+        return;
+    }
+    if (count == 0) {
+        if (lane == 0 && a.counters) atomicAdd(&a.counters->empty_frames, 1ull);
+        if (dst != src)
+            for (int i = lane; i < d; i += 32) dst[i] = q[i];
+        return;
+    }
+    const double wk = lane < count ? reference_weight(key_dist(mine)) : 0.0;
+    double wv[8];
+    const float *vr[8];
+    double wsum = -0.0;  // the reference's order: S = w0 + w1 + ... (zeros past count)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        wv[k] = __shfl_sync(kFullMask, wk, k);
+        const uint32_t rk = key_pos(__shfl_sync(kFullMask, mine, k));
+        vr[k] = a.vectors + static_cast<size_t>(k < count ? rk : 0u) * d;
+        wsum = __dadd_rn(wsum, wv[k]);
+    }
+    const WeightDivisor sum = weight_divisor(wsum);
+    for (int i = lane; i < d; i += 32) {
+        float x[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = k < count ? __ldg(vr[k] + i) : 0.f;
+        dst[i] = reference_blend_element<true>(q[i], x, wv, sum, count, ratio);
+    }
+}
+
 // ---------------------------------------------------------------- index build
 __global__ void max_abs_kernel(const float *__restrict__ x, size_t count, unsigned int *out) {
     float m = 0.f;
@@ -1859,6 +2039,13 @@ void launch_merge(VfrIndex *ix, MergeArgs &ma, size_t frames, cudaStream_t strea
                 return;
             }
         }
+    }
+    if (!few && ix->small_merge) {
+        // many frames: one warp per frame
+        const size_t smem = static_cast<size_t>(kMergeWarps) * ((ix->d + 3) & ~3) * sizeof(float);
+        cuda_check(launch_pdl(merge_warp_kernel, dim3(static_cast<unsigned>((frames + kMergeWarps - 1) / kMergeWarps)),
+                              dim3(32 * kMergeWarps), smem, stream, ma, static_cast<long long>(frames)));
+        return;
     }
     if (few) {
         // as many rows as fit, up to kRerankStop (the usual re-rank set); at
@@ -2246,6 +2433,7 @@ __global__ void __launch_bounds__(32 * kIvfWarps, 3) ivf_merge_warp_kernel(IvfMe
     __shared__ unsigned long long ex[kIvfWarps][kRerankMax];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, octet = lane >> 3, j = lane & 7;
     const long long frame = static_cast<long long>(blockIdx.x) * kIvfWarps + w;
+    launch_dependents();  // as in merge_kernel: the exact kernel's launch overlaps this one
     if (frame >= a.frames || !a.probe_ok[frame]) return;  // r <= 0 (handled) or exact re-run
     const int d = a.d, P = a.nprobe;
     const int dq = (d + 3) & ~3;
@@ -2742,6 +2930,10 @@ void build_tc(VfrIndex *ix) {
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, ix->merge_smem_max));
         cuda_check(cudaFuncSetAttribute(merge_small_kernel<kMergeThreads>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, ix->merge_smem_max));
+        // merge_warp_kernel: one frame row per warp (d <= 4096: at most
+        // 128 KB beside its 16 KB of static key arrays)
+        cuda_check(cudaFuncSetAttribute(merge_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        kMergeWarps * ((ix->d + 3) & ~3) * static_cast<int>(sizeof(float))));
     }
     cuda_check(cudaFuncSetAttribute(coarse_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
     if (ivf) {
@@ -3009,7 +3201,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     ea.probes = probes;
     ea.probe_ok = probe_ok;
     ix->prof.begin(kProfExact, stream);
-    launch_exact(ea, static_cast<long long>(frames), stream);
+    launch_exact(ea, static_cast<long long>(frames), stream, true);
     ix->prof.end(stream);
 }
 
