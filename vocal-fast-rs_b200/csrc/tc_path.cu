@@ -300,6 +300,15 @@ __device__ __forceinline__ float approx_error(float4 qs, float max_norm, float m
            norm_rel * (max_norm * max_norm + qs.x) + 6e-8f * (max_norm * max_norm + 2.f * qs.y * max_hat);
 }
 
+// A list's own filter bound from its 8th best approximate distance u (the
+// frame's qe = ||q||^2 + e and 2e): the 8 rows at or below u have exact
+// distances within (u + qe)(1 + exact_rel), so no row whose d~ exceeds
+// u + 2e + slack reaches or ties the frame's exact 8th best (+inf while the
+// list holds fewer than 8).
+__device__ __forceinline__ float own_bound(float u, float qe, float two_e, float exact_rel) {
+    return u + two_e + (8.f * exact_rel * fabsf(u + qe) + 1e-6f * (fabsf(u) + fabsf(qe)) + 1e-30f);
+}
+
 // Four consecutive row norms.  Flat segments start on tile boundaries, so the
 // address is 16-byte aligned; IVF lists start anywhere.
 template <bool kIvf>
@@ -489,9 +498,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             top.init();
             bool aborted = false;
             // the frame's shared filter bound (flat, when enabled): read at
-            // every tile, published when this list's 8th best improves
+            // every tile, published when this list's 8th best improves.  The
+            // list's own bound (its 8th best u plus 2e and rounding slack, a
+            // d~ no row of the frame's exact top 8 reaches) filters at once.
             unsigned int *gp = nullptr;
-            float g = inf, qe = 0.f, two_e = 0.f, published = inf;
+            float g = inf, qe = 0.f, two_e = 0.f, published = inf, own = inf;
             if constexpr (!kIvf) {
                 if (a.gbound != nullptr && lane_real && r < it.a_rows) {
                     const long long fr = static_cast<long long>(it.a_row0) + r;
@@ -555,7 +566,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     // have none, and the vote is warp-uniform)
                     float dd[16];
                     uint32_t mask = 0;
-                    const float thr = fminf(top.dist[K - 1], g);
+                    const float thr = fminf(fminf(top.dist[K - 1], g), own);
                     // IVF: rows past the list's end belong to the next list
                     const int64_t lim = kIvf ? it.b_end - (static_cast<int64_t>(col_row) + c * 16) : 16;
 #pragma unroll
@@ -590,6 +601,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
                         for (int e = 0; e < 16; ++e) cr[e] = col_row + c * 16 + e;
                         top.merge16(dd, cr);
+                        if (gp != nullptr) own = own_bound(top.dist[7], qe, two_e, a.exact_rel);
                         mask = 0;
                     }
                     while (mask) {
@@ -598,7 +610,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                         float x = dd[0];
 #pragma unroll
                         for (int i = 1; i < 16; ++i) x = e == i ? dd[i] : x;
-                        if (x < top.dist[K - 1]) top.insert(x, col_row + c * 16 + e);
+                        if (x < fminf(top.dist[K - 1], own)) {
+                            top.insert(x, col_row + c * 16 + e);
+                            if (gp != nullptr) own = own_bound(top.dist[7], qe, two_e, a.exact_rel);
+                        }
                     }
                     if (c + 1 < kHalfCols / 16) tc::tmem_wait_ld(v[cur ^ 1]);
                 }
@@ -607,12 +622,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
                 ++acc_count;
                 if (gp != nullptr && top.dist[7] < published) {
-                    // the list's 8 best bound the frame's 8th best from above:
-                    // u + 2e + slack is a d~ no row of the exact top 8 reaches
-                    const float u = top.dist[7];
-                    published = u;
-                    const float bound = u + two_e + (8.f * a.exact_rel * fabsf(u + qe) + 1e-6f * (fabsf(u) + fabsf(qe)) + 1e-30f);
-                    atomicMin(gp, total_order_bits(bound));
+                    published = top.dist[7];
+                    atomicMin(gp, total_order_bits(own));
                 }
                 if (t + 1 < tiles) {
                     reinterpret_cast<float4 *>(nbuf + ((t + 1) & 1) * kHalfCols)[lane] = pre0;
@@ -644,8 +655,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     dk[i / 2] = make_ulonglong2(i < cnt ? make_key(top.dist[i], top.row[i]) : kEmptyKey,
                                                 i + 1 < cnt ? make_key(top.dist[i + 1], top.row[i + 1]) : kEmptyKey);
                 // rows this list dropped have d~ >= min(its K-th best, the
-                // smallest shared bound it filtered with: the last one read)
-                a.out_thr[frame * a.thr_stride + list] = fminf(cnt == K ? top.dist[K - 1] : inf, g);
+                // smallest shared bound it filtered with (the last one read),
+                // its own final bound); all three only ever decrease
+                a.out_thr[frame * a.thr_stride + list] = fminf(fminf(cnt == K ? top.dist[K - 1] : inf, g), own);
             }
         }
     }
@@ -1753,6 +1765,7 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreadsMax ? 1 : 2) merge_smal
 // warp merge gives the top 8, and the lists' thresholds certify the rows the
 // candidate stage dropped, as in merge_kernel.
 constexpr int kMergeWarps = 8;
+constexpr int kMergeBatch = 8;  // key loads in flight per lane
 
 __global__ void __launch_bounds__(32 * kMergeWarps, 3) merge_warp_kernel(MergeArgs a, long long frames) {
     extern __shared__ __align__(16) float mwq[];  // [kMergeWarps][d rounded up to 4] frame rows
@@ -1788,17 +1801,26 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 3) merge_warp_kernel(MergeAr
     for (int l = lane; l < a.lists; l += 32) tmin = fminf(tmin, __ldcg(a.thr + frame * a.thr_stride + l));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, o));
-    // U: each lane's 8 smallest slots (sorted insertion), then 8 warp pops
+    // U: each lane's 8 smallest slots (sorted insertion), then 8 warp pops.
+    // The slots are read kMergeBatch at a time, all loads of a batch issued
+    // before any is used (the key block sits in L2: one round trip a batch).
     unsigned long long v[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = kEmptyKey;
-#pragma unroll 4
-    for (int i = lane; i < slots; i += 32) {
-        const unsigned long long k = __ldcg(fk + i);
-        if (k < v[7]) {
-            v[7] = k;
+    for (int base = 0; base < slots; base += 32 * kMergeBatch) {
+        unsigned long long kb[kMergeBatch];
 #pragma unroll
-            for (int e = 6; e >= 0; --e) key_cx(v[e], v[e + 1]);
+        for (int t = 0; t < kMergeBatch; ++t) {
+            const int i = base + 32 * t + lane;
+            kb[t] = i < slots ? __ldcg(fk + i) : kEmptyKey;
+        }
+#pragma unroll
+        for (int t = 0; t < kMergeBatch; ++t) {
+            if (kb[t] < v[7]) {
+                v[7] = kb[t];
+#pragma unroll
+                for (int e = 6; e >= 0; --e) key_cx(v[e], v[e + 1]);
+            }
         }
     }
     unsigned long long u8 = kEmptyKey;
@@ -1815,18 +1837,25 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 3) merge_warp_kernel(MergeAr
     const float4 qs = a.qstats[frame];
     const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
     const float limit = u8 == kEmptyKey ? inf : (key_dist(u8) + qs.x + e) * (1.f + 4.f * a.exact_rel) + 1e-30f;
-    // the re-rank set, in slot order
+    // the re-rank set, in slot order (batched loads, as above)
     int total = 0;
-    for (int base = 0; base < slots; base += 32) {
-        const int i = base + lane;
-        const unsigned long long k = i < slots ? __ldcg(fk + i) : kEmptyKey;
-        const bool kept = k != kEmptyKey && !(key_dist(k) + qs.x - e > limit);
-        const unsigned ball = __ballot_sync(kFullMask, kept);
-        if (kept) {
-            const int pos = total + __popc(ball & ((1u << lane) - 1u));
-            if (pos < kRerankMax) sel[w][pos] = k;
+    for (int base = 0; base < slots; base += 32 * kMergeBatch) {
+        unsigned long long kb[kMergeBatch];
+#pragma unroll
+        for (int t = 0; t < kMergeBatch; ++t) {
+            const int i = base + 32 * t + lane;
+            kb[t] = i < slots ? __ldcg(fk + i) : kEmptyKey;
         }
-        total += __popc(ball);
+#pragma unroll
+        for (int t = 0; t < kMergeBatch; ++t) {
+            const bool kept = kb[t] != kEmptyKey && !(key_dist(kb[t]) + qs.x - e > limit);
+            const unsigned ball = __ballot_sync(kFullMask, kept);
+            if (kept) {
+                const int pos = total + __popc(ball & ((1u << lane) - 1u));
+                if (pos < kRerankMax) sel[w][pos] = kb[t];
+            }
+            total += __popc(ball);
+        }
     }
     const int m = min(total, kRerankMax);
     __syncwarp();
