@@ -118,6 +118,11 @@ static_assert((Pipe<kSpreadLayout>::kStages + 1) / 2 * 8192u <= 24576u, "A packs
 static_assert(Pipe<kFullLayout>::kSmem <= 232448 && Pipe<kSpreadLayout>::kSmem <= 232448, "cand_kernel shared memory");
 static_assert(kNormBytes == kEpiWarps * 1024, "one 1 KB row-norm double buffer per epilogue warp");
 constexpr uint32_t kTmemCols = 512;  // two 128 x 256 fp32 accumulators
+// Per-frame bound words of a flat call: [0] the shared filter bound, [8, 16)
+// the group slots (one 32-byte aligned pair of 16-byte loads)
+constexpr int kBoundWords = 16;
+constexpr int kBoundSlotWord = 8;
+constexpr int kBoundSlots = 8;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kFormatF16 = 0;
 
@@ -309,6 +314,16 @@ __device__ __forceinline__ float own_bound(float u, float qe, float two_e, float
     return u + two_e + (8.f * exact_rel * fabsf(u + qe) + 1e-6f * (fabsf(u) + fabsf(qe)) + 1e-30f);
 }
 
+// A frame's bound from its bound words (kBoundWords layout): the smaller of
+// the shared word and the own bound of the group slots' maximum.
+__device__ __forceinline__ float frame_bound(const unsigned int *w, float qe, float two_e, float exact_rel) {
+    const uint4 s0 = __ldcg(reinterpret_cast<const uint4 *>(w + kBoundSlotWord));
+    const uint4 s1 = __ldcg(reinterpret_cast<const uint4 *>(w + kBoundSlotWord + 4));
+    // total-order bits: the largest word is the largest value
+    const uint32_t umax = max(max(max(s0.x, s0.y), max(s0.z, s0.w)), max(max(s1.x, s1.y), max(s1.z, s1.w)));
+    return fminf(from_total_order_bits(__ldcg(w)), own_bound(from_total_order_bits(umax), qe, two_e, exact_rel));
+}
+
 // Four consecutive row norms.  Flat segments start on tile boundaries, so the
 // address is 16-byte aligned; IVF lists start anywhere.
 template <bool kIvf>
@@ -478,7 +493,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         __syncwarp();  // converged at the CTA barrier, as the producer warp
     } else {
         // ---------------- epilogue: one thread per frame of the tile; the two
-        // warps of a TMEM lane quarter split each tile's columns in halves
+        // warps of a TMEM lane quarter split each tile's columns in halves.
+        // The frames' statistics and bound words come from the preparation
+        // kernel: wait for it (flat; the IVF kernel waited at its start).
+        if constexpr (!kIvf) grid_dependency_wait();
         const int ew = warp - 2;
         const int quarter = warp & 3;  // TMEM lanes this warp may access
         const int half = ew >> 2;
@@ -497,18 +515,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             TopList<K> top;
             top.init();
             bool aborted = false;
-            // the frame's shared filter bound (flat, when enabled): read at
-            // every tile, published when this list's 8th best improves.  The
-            // list's own bound (its 8th best u plus 2e and rounding slack, a
-            // d~ no row of the frame's exact top 8 reaches) filters at once.
+            // The frame's bound words (flat, when enabled; kBoundWords per
+            // frame): word 0 is the shared filter bound, the minimum of every
+            // list's published own bound; words 8-15 are group slots, slot j
+            // the smallest best d~ of the lists whose index is j mod 8.  Rows
+            // of different slots come from disjoint lists, so the 8 slots name
+            // 8 distinct rows and their maximum bounds the frame's 8th best as
+            // a list's own 8th best does.  Both are read at every tile start
+            // and published after every tile that improved them.  The list's
+            // own bound (its 8th best u plus 2e and rounding slack, a d~ no
+            // row of the frame's exact top 8 reaches) filters at once.
             unsigned int *gp = nullptr;
-            float g = inf, qe = 0.f, two_e = 0.f, published = inf, own = inf;
+            float g = inf, qe = 0.f, two_e = 0.f, published = inf, own = inf, best_published = inf;
+            const int slot = (it.seg * kHalves + half) & (kBoundSlots - 1);
             if constexpr (!kIvf) {
                 if (a.gbound != nullptr && lane_real && r < it.a_rows) {
                     const long long fr = static_cast<long long>(it.a_row0) + r;
                     const float4 qs = a.qstats[fr];
                     const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
-                    gp = a.gbound + fr;
+                    gp = a.gbound + fr * kBoundWords;
                     qe = qs.x + e;
                     two_e = 2.f * e;
                 }
@@ -526,7 +551,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 const uint32_t tile_row = static_cast<uint32_t>(row0 + static_cast<int64_t>(t) * kTileN);
                 float4 pre0 = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (t + 1 < tiles) pre0 = load_norms4<kIvf>(a.row_norms + tile_row + kTileN + half * kHalfCols + lane * 4);
-                if (gp != nullptr) g = from_total_order_bits(__ldcg(gp));
+                if (gp != nullptr) g = frame_bound(gp, qe, two_e, a.exact_rel);
                 // every lane polls; the outcome is made warp-uniform before the
                 // .sync.aligned TMEM loads
                 const bool ready = tc::mbar_wait(&acc_full[b], (acc_count >> 1) & 1, kWaitLimitNs);
@@ -615,6 +640,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                             if (gp != nullptr) own = own_bound(top.dist[7], qe, two_e, a.exact_rel);
                         }
                     }
+
                     if (c + 1 < kHalfCols / 16) tc::tmem_wait_ld(v[cur ^ 1]);
                 }
                 tc::tc_fence_before();
@@ -624,6 +650,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 if (gp != nullptr && top.dist[7] < published) {
                     published = top.dist[7];
                     atomicMin(gp, total_order_bits(own));
+                }
+                if (gp != nullptr && top.dist[0] < best_published) {
+                    best_published = top.dist[0];
+                    atomicMin(gp + kBoundSlotWord + slot, total_order_bits(best_published));
                 }
                 if (t + 1 < tiles) {
                     reinterpret_cast<float4 *>(nbuf + ((t + 1) & 1) * kHalfCols)[lane] = pre0;
@@ -700,8 +730,9 @@ __global__ void prep_queries_kernel(const float *__restrict__ q, __half *__restr
     }
     if (lane == 0) {
         stats[f] = make_float4(qn2, sqrtf(hat2) * 1.00001f, sqrtf(res2) * 1.00001f, 0.f);
-        if (gbound) gbound[f] = total_order_bits(__int_as_float(0x7f800000));
     }
+    if (gbound && lane < kBoundWords)
+        gbound[f * kBoundWords + lane] = total_order_bits(__int_as_float(0x7f800000));
 }
 
 // ---------------------------------------------------------------- merge
@@ -733,6 +764,7 @@ struct MergeArgs {
     DeviceCounters *counters;
     int stage_rows;  // re-rank rows staged in shared memory per chunk (0: read them from global memory)
     float *raw_out;  // optional: the frames before the blend (RetrievalProtection::save_raw)
+    const unsigned int *gbound;  // flat: the call's per-frame bound words (kBoundWords each), or null
 };
 
 constexpr int kMergeThreads = 256;     // per frame, when many frames share the GPU
@@ -1548,7 +1580,7 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreadsMax ? 1 : 2) merge_smal
     __shared__ float warp_tmin[kWarps];
     __shared__ unsigned long long u8_s;
     __shared__ float tmin_s;
-    __shared__ int count_s, certified_s;
+    __shared__ int count_s, bound_count_s, certified_s;
     __shared__ __align__(8) uint64_t gather_bar;
     __shared__ __align__(8) uint64_t stage_bar;
 
@@ -1567,6 +1599,7 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreadsMax ? 1 : 2) merge_smal
         tc::mbar_init(&stage_bar, 1);
         tc::fence_mbarrier_init();
         count_s = 0;
+        bound_count_s = 0;
     }
     if (tid < 8) best[tid] = kEmptyKey;
     // the caller's inputs first, while the candidate kernel may still run
@@ -1602,13 +1635,41 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreadsMax ? 1 : 2) merge_smal
             for (int i = tid; i < d; i += kT) dst[i] = q[i];
         return;
     }
-    // per warp: the smallest list threshold and the 8 smallest keys of its
-    // slice of the key slots; then warp 0 reduces them
+    // The re-rank set is every key whose lower bound d~ + ||q||^2 - e does
+    // not exceed `limit`.  First choice: the candidate stage's final frame
+    // bound G (no row above it reaches or ties the exact top 8), when at most
+    // a stage's worth of keys lie at or below it; else the narrowing limit
+    // from U, the 8th smallest key (per warp, the 8 smallest of its slice of
+    // the key slots, then warp 0 reduces them).
+    const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
     {
         float tmin = inf;
         for (int s = tid; s < a.lists; s += kT) tmin = fminf(tmin, thr[s]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, o));
+        if (lane == 0) warp_tmin[warp] = tmin;
+    }
+    float limit = inf;
+    bool by_bound = false;
+    // (the 512-thread form: its stage holds up to 64 rows; with the 256-thread
+    // form's 32 the bound's set often does not fit, and the count is wasted)
+    if (kT == kMergeThreadsMax && a.gbound != nullptr) {
+        limit = frame_bound(a.gbound + frame * kBoundWords, qs.x + e, 2.f * e, a.exact_rel) + qs.x - e;
+        int n = 0;
+        for (int i = tid; i < a.sort_size; i += kT) {
+            const unsigned long long k = keys[i];
+            n += k != kEmptyKey && !(key_dist(k) + qs.x - e > limit);
+        }
+        if (n) atomicAdd(&bound_count_s, n);
+        __syncthreads();
+        by_bound = bound_count_s <= a.stage_rows;  // CTA-uniform
+        if (tid == 0) {
+            float t = inf;
+            for (int w = 0; w < kWarps; ++w) t = fminf(t, warp_tmin[w]);
+            tmin_s = t;
+        }
+    }
+    if (!by_bound) {
         const int chunk = (a.sort_size + kWarps - 1) / kWarps;
         const int lo = warp * chunk;
         const int n = max(0, min(chunk, a.sort_size - lo));
@@ -1618,29 +1679,25 @@ __global__ void __launch_bounds__(kT, kT == kMergeThreadsMax ? 1 : 2) merge_smal
         else
             warp_smallest8(keys + lo, n, top);
         if (lane == 0) {
-            warp_tmin[warp] = tmin;
 #pragma unroll
             for (int r = 0; r < 8; ++r) warp_top[warp * 8 + r] = top[r];
         }
-    }
-    __syncthreads();
-    if (warp == 0) {
-        static_assert(kWarps * 8 <= 256, "one register list per lane");
-        unsigned long long top[8];
-        warp_smallest8_reg(warp_top, kWarps * 8, top);
-        float tmin = lane < kWarps ? warp_tmin[lane] : inf;
+        __syncthreads();
+        if (warp == 0) {
+            static_assert(kWarps * 8 <= 256, "one register list per lane");
+            warp_smallest8_reg(warp_top, kWarps * 8, top);
+            float tmin = lane < kWarps ? warp_tmin[lane] : inf;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, o));
-        if (lane == 0) {
-            u8_s = top[7];
-            tmin_s = tmin;
+            for (int o = 16; o > 0; o >>= 1) tmin = fminf(tmin, __shfl_xor_sync(kFullMask, tmin, o));
+            if (lane == 0) {
+                u8_s = top[7];
+                tmin_s = tmin;
+            }
         }
+        __syncthreads();
+        const unsigned long long u8 = u8_s;
+        limit = u8 == kEmptyKey ? inf : (key_dist(u8) + qs.x + e) * (1.f + 4.f * a.exact_rel) + 1e-30f;
     }
-    __syncthreads();
-    // the re-rank set: every key that can still reach or tie the exact top 8
-    const unsigned long long u8 = u8_s;
-    const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
-    const float limit = u8 == kEmptyKey ? inf : (key_dist(u8) + qs.x + e) * (1.f + 4.f * a.exact_rel) + 1e-30f;
     for (int base = 0; base < a.sort_size; base += kT) {  // sort_size and kT are multiples of 32
         const int i = base + tid;
         const unsigned long long k = i < a.sort_size ? keys[i] : kEmptyKey;
@@ -2188,7 +2245,7 @@ WsLayout ws_layout(size_t frames, int d_pad, int sms) {
     l.fcount = off;
     off = align256(off + 16);
     l.gbound = off;
-    off = align256(off + fr * sizeof(unsigned int));
+    off = align256(off + fr * kBoundWords * sizeof(unsigned int));
     l.total = off;
     return l;
 }
@@ -3323,6 +3380,7 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ma.raw_out = raw;
     ma.fallback_count = fcount;
     ma.counters = ix->counters;
+    ma.gbound = gbound;
     ix->prof.begin(kProfMerge, stream);
     launch_merge(ix, ma, frames, stream);
     ix->prof.end(stream);
@@ -3384,7 +3442,7 @@ constexpr size_t kNoAllocThr = kNoAllocKeys + kNoAllocLists * kItemKeep * kTileM
 constexpr size_t kNoAllocList = kNoAllocThr + (kNoAllocLists * kTileM + kNoAllocMaxFrames * 4) * sizeof(float);
 constexpr size_t kNoAllocCount = kNoAllocList + kNoAllocMaxFrames * sizeof(int32_t);
 constexpr size_t kNoAllocBound = kNoAllocCount + 256;
-constexpr size_t kNoAllocBytes = kNoAllocBound + kNoAllocMaxFrames * sizeof(unsigned int);
+constexpr size_t kNoAllocBytes = kNoAllocBound + kNoAllocMaxFrames * kBoundWords * sizeof(unsigned int);
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
@@ -3490,6 +3548,7 @@ void run_tc_noalloc(VfrIndex *ix, float *features, const float *rate, size_t fra
     ma.fallback_list = flist;
     ma.fallback_count = fcount;
     ma.counters = ix->counters;
+    ma.gbound = gbound;
     launch_merge(ix, ma, frames, stream);
 
     ExactArgs ea{};
