@@ -154,14 +154,17 @@ struct CandArgs {
     const int32_t *list_start;    // pair offsets [nlist + 1] (lists in size order, not id order)
     const int32_t *list_count;    // pairs per list [nlist]
     int pair_stride;              // output stride: pairs capacity
-    // Flat only (null: off): a per-frame filter bound shared by every CTA
-    // (total-order bits of an approximate distance d~, +inf at call start).
-    // A list whose 8 best so far have d~ <= u publishes u + 2e + slack: no
-    // row at or above it can enter or tie the frame's exact top 8, so every
-    // CTA may drop such rows; the list's reported threshold then becomes
-    // min(its K-th best, the bound it used), which keeps the certificate.
+    // Per-frame bound words shared by every CTA (null: off; flat, and the
+    // IVF fine stage): kBoundWords per frame, total-order bits of approximate
+    // distances d~, +inf at call start.  Word 0: a list whose 8 best so far
+    // have d~ <= u publishes u + 2e + slack, a d~ no row of the frame's exact
+    // top 8 reaches or ties.  Words 8-15: group slots, the smallest best d~
+    // of the lists in each group (disjoint rows).  Every CTA may drop rows
+    // above the bounds; a list's reported threshold is then min(its K-th
+    // best, the bounds it used), which keeps the certificate.
     unsigned int *gbound;
-    const float4 *qstats;  // (||q||^2, ||q^||, ||q - q^||) per frame
+    const float4 *qstats;          // (||q||^2, ||q^||, ||q - q^||) per frame
+    const int32_t *pair_frame;     // IVF fine stage: the frame of each A row (pair)
     float max_norm, max_hat, max_residual, acc_rel, norm_rel, exact_rel;
 };
 
@@ -197,7 +200,7 @@ __device__ __forceinline__ Item item_at(const CandArgs &a, int item, int total) 
         it.a_rows = min(kTileM, a.list_start[e.x] + a.list_count[e.x] - it.a_row0);
         it.b_row0 = a.list_offsets[e.x];
         it.b_end = a.list_offsets[e.x + 1];
-        it.seg = 0;
+        it.seg = e.x;  // the list (its group slot in the frames' bound words)
     } else {
         const int qtile = item % a.n_qtiles;
         it.seg = item / a.n_qtiles;
@@ -528,9 +531,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             unsigned int *gp = nullptr;
             float g = inf, qe = 0.f, two_e = 0.f, published = inf, own = inf, best_published = inf;
             const int slot = (it.seg * kHalves + half) & (kBoundSlots - 1);
-            if constexpr (!kIvf) {
+            {
                 if (a.gbound != nullptr && lane_real && r < it.a_rows) {
-                    const long long fr = static_cast<long long>(it.a_row0) + r;
+                    const long long fr = kIvf ? static_cast<long long>(a.pair_frame[it.a_row0 + r])
+                                              : static_cast<long long>(it.a_row0) + r;
                     const float4 qs = a.qstats[fr];
                     const float e = approx_error(qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel, a.norm_rel);
                     gp = a.gbound + fr * kBoundWords;
@@ -672,7 +676,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     for (int i = 0; i < K; ++i)
                         if (i < cnt) a.out_keys[(half * K + i) * stride + pos] = make_key(top.dist[i], top.row[i]);
                     a.out_count[half * stride + pos] = cnt;
-                    a.out_thr[half * stride + pos] = cnt == K ? top.dist[K - 1] : inf;
+                    // as flat lists: min(K-th best, the last shared bound read, own bound)
+                    a.out_thr[half * stride + pos] = fminf(fminf(cnt == K ? top.dist[K - 1] : inf, g), own);
                 }
             } else if (lane_real && r < it.a_rows) {
                 // every slot is written (kEmptyKey past cnt), so the merge
@@ -2848,7 +2853,7 @@ __global__ void __launch_bounds__(32 * kIvfWarps) coarse_select_warp_kernel(Coar
 
 struct IvfWs {
     size_t q16, qstats, ckeys, cthr, probes, probe_ok, list_count, list_cursor, list_start, items, item_count,
-        pair_frame, pair_slot, qp, fkeys, fcounts, fthr, flist, fcount, total;
+        pair_frame, pair_slot, qp, fkeys, fcounts, fthr, flist, fcount, gbound, total;
 };
 
 IvfWs ivf_ws_layout(size_t frames, int d_pad, int nlist, int nprobe, int sms) {
@@ -2881,6 +2886,7 @@ IvfWs ivf_ws_layout(size_t frames, int d_pad, int nlist, int nprobe, int sms) {
     take(l.fthr, kHalves * pairs * sizeof(float));
     take(l.flist, fr * sizeof(int32_t));
     take(l.fcount, 16);
+    take(l.gbound, fr * kBoundWords * sizeof(unsigned int));
     l.total = off;
     return l;
 }
@@ -3107,6 +3113,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     float *fthr = reinterpret_cast<float *>(ws + l.fthr);
     int32_t *flist = reinterpret_cast<int32_t *>(ws + l.flist);
     int32_t *fcount = reinterpret_cast<int32_t *>(ws + l.fcount);
+    unsigned int *gbound = reinterpret_cast<unsigned int *>(ws + l.gbound);
     const size_t pair_cap = ix->ws.frames * static_cast<size_t>(P);
     const float coef = -2.0f / (ix->tc_scale * ix->tc_scale);
     const float acc_rel = static_cast<float>(ix->d_pad) * std::ldexp(1.0f, -22);
@@ -3117,7 +3124,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     const long long lanes = static_cast<long long>(frames) * 32;
     ix->prof.begin(kProfPrep, stream);
     prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
-        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount, nullptr);
+        queries, q16, qstats, static_cast<long long>(frames), ix->d, ix->d_pad, ix->tc_scale, fcount, gbound);
     cuda_check(cudaGetLastError());
     ix->prof.end(stream);
     cuda_check(cudaMemsetAsync(list_count, 0, static_cast<size_t>(ix->nlist) * sizeof(int32_t), stream));
@@ -3218,6 +3225,8 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     cf.list_start = list_start;
     cf.list_count = list_count;
     cf.pair_stride = static_cast<int>(pair_cap);
+    cf.pair_frame = pair_frame;
+    set_shared_bound(cf, ix, gbound, qstats);
     ix->prof.begin(kProfCand, stream);
     cand_kernel<true, kIvfKeep><<<ix->sm_count, kThreadsTC, Pipe<kFullLayout>::kSmem, stream>>>(tmap_qp, ix->tmap_vectors, cf);
     cuda_check(cudaGetLastError());
