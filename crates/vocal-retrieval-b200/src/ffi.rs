@@ -27,6 +27,12 @@ pub struct VfrPeerRows {
     _private: [u8; 0],
 }
 
+/// Opaque single-process multi-GPU index (vfr_retrieval_*_sharded).
+#[repr(C)]
+pub struct VfrShardedIndex {
+    _private: [u8; 0],
+}
+
 /// Stream handle with the layout of vocal::Stream (bridge.h:54).
 #[repr(C)]
 pub struct Stream {
@@ -37,6 +43,8 @@ pub const VFR_ENGINE_AUTO: i32 = 0;
 pub const VFR_ENGINE_EXACT: i32 = 1;
 pub const VFR_ENGINE_TENSOR: i32 = 2;
 pub const VFR_SHARE_STORAGE: i32 = 1;
+pub const VFR_SHARD_ROWS: i32 = 0;
+pub const VFR_SHARD_QUERIES: i32 = 1;
 
 #[repr(C)]
 #[derive(Clone, Copy, Debug)]
@@ -386,6 +394,48 @@ unsafe extern "C" {
         out: *mut f32,
         dist: *const f32,
         labels: *const i64,
+        frames: usize,
+        width: i32,
+        index_rate: *const f32,
+        stream: *mut Stream,
+        error: *mut *mut c_char,
+    ) -> i32;
+    pub fn vfr_retrieval_create_sharded(
+        device_count: i32,
+        devices: *const i32,
+        mode: i32,
+        dimensions: i32,
+        nlist: i32,
+        nprobe: i32,
+        vector_count: usize,
+        centroids: *const f32,
+        centroid_count: usize,
+        offsets: *const i32,
+        offset_count: usize,
+        vectors: *const f32,
+        vector_value_count: usize,
+        ids: *const i32,
+        id_count: usize,
+        options: *const VfrOptions,
+        out: *mut *mut VfrShardedIndex,
+        error: *mut *mut c_char,
+    ) -> i32;
+    pub fn vfr_retrieval_destroy_sharded(index: *mut VfrShardedIndex);
+    pub fn vfr_retrieval_search_sharded(
+        index: *mut VfrShardedIndex,
+        queries: *const f32,
+        frames: usize,
+        width: i32,
+        k: i32,
+        distances: *mut f32,
+        labels: *mut i64,
+        stream: *mut Stream,
+        error: *mut *mut c_char,
+    ) -> i32;
+    pub fn vfr_retrieval_blend_sharded(
+        index: *mut VfrShardedIndex,
+        queries: *const f32,
+        out: *mut f32,
         frames: usize,
         width: i32,
         index_rate: *const f32,

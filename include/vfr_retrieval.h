@@ -375,6 +375,40 @@ VFR_API int vfr_blend_peer(VfrPeerRows *peers, const float *queries, float *out,
                            const int64_t *labels, size_t frames, int32_t width, const float *index_rate,
                            VfrStream *stream, char **error);
 
+/* Single-process multi-GPU index: one handle over several devices of a node
+ * (the reference is single-GPU; this is the C entry its Rust runtime would
+ * call to drive several GPUs from one process).  devices[0] is the home
+ * device: queries, outputs, index_rate and `stream` belong to it, and every
+ * call is ordered on that stream.
+ *
+ * VFR_SHARD_ROWS (flat indexes): device s holds rows [s n / G, (s + 1) n / G);
+ *   every shard searches all frames, the lists are merged by (distance,
+ *   global row) -- the single-index scan order -- and the blend reads each
+ *   winner's row from the device that owns it over NVLink.  Results equal a
+ *   single index's bit for bit.
+ * VFR_SHARD_QUERIES: every device holds a replica and serves a contiguous
+ *   share of the frames (any index kind).
+ * Peer access between the home device and every other device is enabled at
+ * create (an error when the hardware has none).  Scratch grows on demand
+ * outside stream capture (VfrOptions.max_frames pre-sizes it and the
+ * shards' workspaces); calls on one handle are serialised on the host. */
+typedef struct VfrShardedIndex VfrShardedIndex;
+enum { VFR_SHARD_ROWS = 0, VFR_SHARD_QUERIES = 1 };
+VFR_API int vfr_retrieval_create_sharded(int32_t device_count, const int32_t *devices, int32_t mode,
+                                         int32_t dimensions, int32_t nlist, int32_t nprobe, size_t vector_count,
+                                         const float *centroids, size_t centroid_count, const int32_t *offsets,
+                                         size_t offset_count, const float *vectors, size_t vector_value_count,
+                                         const int32_t *ids, size_t id_count, const VfrOptions *options,
+                                         VfrShardedIndex **out, char **error);
+VFR_API void vfr_retrieval_destroy_sharded(VfrShardedIndex *index);
+/* k in 1..8; distances [frames][k], labels [frames][k] (FAISS ids, -1 past a frame's count). */
+VFR_API int vfr_retrieval_search_sharded(VfrShardedIndex *index, const float *queries, size_t frames,
+                                         int32_t width, int32_t k, float *distances, int64_t *labels,
+                                         VfrStream *stream, char **error);
+/* Out-of-place blend (out may alias queries), as vfr_retrieval_blend_from. */
+VFR_API int vfr_retrieval_blend_sharded(VfrShardedIndex *index, const float *queries, float *out, size_t frames,
+                                        int32_t width, const float *index_rate, VfrStream *stream, char **error);
+
 /* Self-test of the bounded wait every mbarrier wait in the library's kernels
  * uses (no counterpart in the reference): one thread waits on a barrier that
  * only `arrive` != 0 completes, giving up after limit_ns (at most 2 s).

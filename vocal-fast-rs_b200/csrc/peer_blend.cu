@@ -21,21 +21,13 @@
 
 #include "exact_common.cuh"
 #include "index_build.h"
+#include "peer_table.h"
 #include "vfr_common.h"
 
 namespace vfr {
 namespace {
 
-constexpr int kMaxPeerShards = 64;
 constexpr int kPeerWarps = 8;  // frames per CTA (one warp each)
-
-struct PeerTable {
-    int shards;
-    int d;
-    const float *rows[kMaxPeerShards];   // [rows of shard][d], this process's mapping
-    const int32_t *row_of_id[kMaxPeerShards];  // null: identity (labels are storage rows)
-    int64_t bounds[kMaxPeerShards + 1];  // global label bounds of the shards
-};
 
 __device__ __forceinline__ const float *winner_row(const PeerTable &t, int64_t label) {
     if (label < t.bounds[0] || label >= t.bounds[t.shards]) return nullptr;
@@ -133,6 +125,22 @@ __global__ void __launch_bounds__(32 * kPeerWarps) blend_peer_kernel(const __gri
 }
 
 }  // namespace
+
+void launch_blend_peer(const PeerTable &t, const float *queries, float *out, const float *dist,
+                       const int64_t *labels, long long frames, const float *index_rate, cudaStream_t s) {
+    require(frames <= static_cast<long long>(INT32_MAX) * kPeerWarps, "frame count exceeds CUDA grid limit");
+    if (frames <= 0) return;
+    bool vec4 = t.d % 4 == 0 && reinterpret_cast<uintptr_t>(queries) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(out) % 16 == 0;
+    for (int k = 0; k < t.shards; ++k) vec4 = vec4 && reinterpret_cast<uintptr_t>(t.rows[k]) % 16 == 0;
+    const unsigned grid = static_cast<unsigned>((frames + kPeerWarps - 1) / kPeerWarps);
+    if (vec4)
+        blend_peer_kernel<true><<<grid, 32 * kPeerWarps, 0, s>>>(t, queries, out, dist, labels, frames, index_rate);
+    else
+        blend_peer_kernel<false><<<grid, 32 * kPeerWarps, 0, s>>>(t, queries, out, dist, labels, frames, index_rate);
+    cuda_check(cudaGetLastError());
+}
+
 }  // namespace vfr
 
 // ---------------------------------------------------------------- host side
@@ -250,20 +258,10 @@ extern "C" int vfr_blend_peer(VfrPeerRows *peers, const float *queries, float *o
     return vfr::guarded(error, [&] {
         vfr::require(peers && queries && out && dist && labels && index_rate, "invalid blend arguments");
         vfr::require(width == peers->table.d, "FAISS feature width mismatch");
-        vfr::require(frames <= static_cast<size_t>(INT32_MAX) * vfr::kPeerWarps, "frame count exceeds CUDA grid limit");
+        vfr::require(frames <= static_cast<size_t>(INT32_MAX), "frame count exceeds CUDA grid limit");
         if (frames == 0) return;
         vfr::DeviceGuard guard(peers->device);
-        cudaStream_t s = vfr::call_stream(stream);
-        bool vec4 = width % 4 == 0 && reinterpret_cast<uintptr_t>(queries) % 16 == 0 &&
-                    reinterpret_cast<uintptr_t>(out) % 16 == 0;
-        for (int k = 0; k < peers->table.shards; ++k) vec4 = vec4 && reinterpret_cast<uintptr_t>(peers->table.rows[k]) % 16 == 0;
-        const unsigned grid = static_cast<unsigned>((frames + vfr::kPeerWarps - 1) / vfr::kPeerWarps);
-        if (vec4)
-            vfr::blend_peer_kernel<true><<<grid, 32 * vfr::kPeerWarps, 0, s>>>(
-                peers->table, queries, out, dist, labels, static_cast<long long>(frames), index_rate);
-        else
-            vfr::blend_peer_kernel<false><<<grid, 32 * vfr::kPeerWarps, 0, s>>>(
-                peers->table, queries, out, dist, labels, static_cast<long long>(frames), index_rate);
-        vfr::cuda_check(cudaGetLastError());
+        vfr::launch_blend_peer(peers->table, queries, out, dist, labels, static_cast<long long>(frames), index_rate,
+                               vfr::call_stream(stream));
     });
 }

@@ -300,3 +300,71 @@ def blend_gathered_rows(queries, out, dist, rows, slot_rows, index_rate, stream=
     s = stream_struct(stream)
     call(L.vfr_blend_gathered_rows, _ptr(queries), _ptr(out), _ptr(dist), _ptr(rows) if rows.numel() else 0,
          rows.shape[0], _ptr(slot_rows), queries.shape[0], queries.shape[1], _ptr(index_rate), ctypes.byref(s))
+
+
+class ShardedRetrievalIndex:
+    """One handle over several GPUs of this process (vfr_retrieval_*_sharded):
+    `mode` SHARD_ROWS splits a flat index's rows across `devices` (results
+    equal a single index's bit for bit), SHARD_QUERIES gives every device a
+    replica and a share of the frames.  Frames, outputs, the ratio and the
+    stream belong to devices[0]."""
+
+    def __init__(self, handle: int, d: int, devices, mode: int):
+        self._h = ctypes.c_void_p(handle)
+        self.d = d
+        self.devices = list(devices)
+        self.mode = mode
+
+    @classmethod
+    def from_arrays(cls, devices, mode, centroids, offsets, vectors, ids, nprobe: int, engine: int = _l.ENGINE_AUTO,
+                    max_frames: int = 0):
+        L = load_library()
+        keep = []
+
+        def host(a, dtype):
+            if hasattr(a, "data_ptr"):
+                a = a.detach().cpu().numpy()
+            a = np.ascontiguousarray(a, dtype)
+            keep.append(a)
+            return a
+
+        c = host(centroids, np.float32)
+        o = host(offsets, np.int32)
+        v = host(vectors, np.float32)
+        i = host(ids, np.int32)
+        dev = (ctypes.c_int32 * len(devices))(*devices)
+        d = c.shape[-1] if c.ndim == 2 else int(v.shape[-1])
+        out = ctypes.c_void_p()
+        opt = _l.Options(ctypes.sizeof(_l.Options), engine, 0, 0, 0, max_frames)
+        call(L.vfr_retrieval_create_sharded, len(devices), dev, int(mode), int(d), int(o.size - 1), int(nprobe),
+             i.size, c.ctypes.data, c.size, o.ctypes.data, o.size, v.ctypes.data, v.size, i.ctypes.data, i.size,
+             ctypes.byref(opt), ctypes.byref(out))
+        return cls(out.value, int(d), devices, mode)
+
+    def __del__(self):
+        self.close()
+
+    def close(self):
+        if getattr(self, "_h", None) and self._h.value and _l._lib is not None:
+            _l._lib.vfr_retrieval_destroy_sharded(self._h)
+            self._h = ctypes.c_void_p()
+
+    def search(self, queries, k: int = 8, stream=None):
+        """(distances [Q,k] f32, labels [Q,k] i64) on devices[0]."""
+        import torch
+
+        frames = queries.shape[0]
+        dist = torch.empty((frames, k), dtype=torch.float32, device=queries.device)
+        labels = torch.empty((frames, k), dtype=torch.int64, device=queries.device)
+        if frames:
+            s = stream_struct(stream)
+            call(load_library().vfr_retrieval_search_sharded, self._h, _ptr(queries), frames, self.d, int(k),
+                 _ptr(dist), _ptr(labels), ctypes.byref(s))
+        return dist, labels
+
+    def blend_from(self, queries, out, index_rate, stream=None) -> None:
+        frames = queries.shape[0]
+        if frames:
+            s = stream_struct(stream)
+            call(load_library().vfr_retrieval_blend_sharded, self._h, _ptr(queries), _ptr(out), frames, self.d,
+                 _ptr(index_rate), ctypes.byref(s))

@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(PKG, "libvfr_retrieval.so")
 HEADER = os.path.join(PKG, "..", "include", "vfr_retrieval.h")
 
 ENGINE_AUTO, ENGINE_EXACT, ENGINE_TENSOR = 0, 1, 2
+SHARD_ROWS, SHARD_QUERIES = 0, 1
 SHARE_STORAGE = 1  # VfrOptions.flags: VFR_SHARE_STORAGE
 
 _lib = None
@@ -119,6 +120,11 @@ def load_library(path: str | None = None):
         "vfr_peer_rows_close": ([vp], None),
         "vfr_blend_peer": ([vp, vp, vp, vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
         "vfr_selftest_bounded_wait": ([ctypes.c_uint64, i32, P(i32), P(ctypes.c_uint64), err], ctypes.c_int),
+        "vfr_retrieval_create_sharded": ([i32, P(i32), i32, i32, i32, i32, sz, vp, sz, vp, sz, vp, sz, vp, sz,
+                                          P(Options), P(vp), err], ctypes.c_int),
+        "vfr_retrieval_destroy_sharded": ([vp], None),
+        "vfr_retrieval_search_sharded": ([vp, vp, sz, i32, i32, vp, vp, P(Stream), err], ctypes.c_int),
+        "vfr_retrieval_blend_sharded": ([vp, vp, vp, sz, i32, vp, P(Stream), err], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
