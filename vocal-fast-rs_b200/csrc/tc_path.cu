@@ -2559,7 +2559,15 @@ __global__ void __launch_bounds__(32 * kIvfWarps, 3) ivf_merge_warp_kernel(IvfMe
         const size_t pos = static_cast<size_t>(a.pair_slot[frame * P + p]);
         cnt = a.counts[h * stride + pos];
         thr = a.thr[h * stride + pos];
-        for (int i = 0; i < cnt; ++i) lk[lane * kItemKeep + i] = a.keys[(h * kItemKeep + i) * stride + pos];
+        // all of the list's loads in flight at once, beside the count's (the
+        // keys of one pair are kItemKeep strided words apart; every slot of
+        // the [half][K][pair] array exists, those past the count are unused)
+        unsigned long long kv[kItemKeep];
+#pragma unroll
+        for (int i = 0; i < kItemKeep; ++i) kv[i] = __ldg(a.keys + (h * kItemKeep + i) * stride + pos);
+#pragma unroll
+        for (int i = 0; i < kItemKeep; ++i)
+            if (i < cnt) lk[lane * kItemKeep + i] = kv[i];
     }
     float tmin = thr;
 #pragma unroll
@@ -2747,10 +2755,16 @@ __global__ void __launch_bounds__(32 * kIvfWarps) coarse_select_warp_kernel(Coar
     float thr = inf;
     if (lane < a.lists) {
         thr = a.thr[frame * a.thr_stride + lane];
-        for (int i = 0; i < kItemKeep; ++i) {  // slots past a list's count hold kEmptyKey
-            const unsigned long long k = fk[lane * kItemKeep + i];
-            lk[lane * kItemKeep + i] = k;
-            cnt += k != kEmptyKey;
+        // the list's 16 keys (slots past its count hold kEmptyKey): every
+        // load in flight before the first store
+        ulonglong2 kv[kItemKeep / 2];
+#pragma unroll
+        for (int i = 0; i < kItemKeep / 2; ++i) kv[i] = __ldg(reinterpret_cast<const ulonglong2 *>(fk + lane * kItemKeep) + i);
+#pragma unroll
+        for (int i = 0; i < kItemKeep / 2; ++i) {
+            lk[lane * kItemKeep + 2 * i] = kv[i].x;
+            lk[lane * kItemKeep + 2 * i + 1] = kv[i].y;
+            cnt += (kv[i].x != kEmptyKey) + (kv[i].y != kEmptyKey);
         }
     }
     float tmin = thr;
