@@ -204,9 +204,16 @@ def cpu_baseline(vectors, queries, ratio, n):
     t0 = time.perf_counter()
     orc.blend(queries[:sample], ratio, threads=cores)
     dt = time.perf_counter() - t0
+    # the reference's own loop is serial (crates/vocal-cpu/src/pipeline.rs:295-299): one thread, two frames
+    t1 = time.perf_counter()
+    orc.blend(queries[:2], ratio, threads=1)
+    dt1 = time.perf_counter() - t1
     return {"value": sample / dt, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"first {sample} frames against all {n} rows ({dt:.1f} s), AVX2-order C restatement, "
-                      f"{cores} threads"}
+                      f"{cores} threads",
+            "single_core": {"value": 2 / dt1, "unit": UNIT, "cores": 1,
+                            "sample": f"first 2 frames against all {n} rows ({dt1:.2f} s), one thread, the "
+                                      "reference's serial loop"}}
 
 
 PARITY_FRAMES = 64
