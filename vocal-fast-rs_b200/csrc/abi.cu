@@ -585,7 +585,7 @@ extern "C" size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t 
                           c.candidate_frames, c.timeouts, index->max_row_norm, index->max_row_residual,
                           static_cast<long>(index->shared ? index->shared.use_count() : 0), index->last_keep,
                           index->last_segments, index->last_tiles_per_seg,
-                          index->last_layout < 0 ? "none" : index->last_layout == 0 ? "full" : "spread",
+                          index->last_layout < 0 ? "none" : index->last_layout == 0 ? "full" : index->last_layout == 1 ? "spread" : "pair",
                           index->last_engine == 1   ? "exact"
                           : index->last_engine == 2 ? "tensor"
                           : index->last_engine == 3 ? "exact2d"

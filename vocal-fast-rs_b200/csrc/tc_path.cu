@@ -58,6 +58,7 @@ constexpr int kThreadsTC = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, warp
 constexpr uint32_t kBBytes = kTileN * kTileK * 2;
 constexpr uint32_t kNormBytes = kEpiWarps * 2 * (kTileN / kHalves) * sizeof(float);  // per warp, double buffered
 constexpr int kSmallBlock = 32;  // frame blocks up to this size use the spread layout
+constexpr int kPairMinFrames = 4096;  // with VFR_PAIR=1, launches from this size use CTA pairs when their items are long
 
 // Shared-memory layouts of cand_kernel.  The MMA is always M = 128: query
 // row m of the A tile feeds TMEM lane m, and an epilogue warp can read only
@@ -75,7 +76,7 @@ constexpr int kSmallBlock = 32;  // frame blocks up to this size use the spread 
 // quarter q at +2q KB); the MMA's other A rows read whatever lies there
 // (their TMEM lanes are never read).  Six stages: three packs, the row-norm
 // buffers, and six 32 KB B tiles, 192 KB of database tiles in flight per SM.
-enum { kFullLayout = 0, kSpreadLayout = 1 };
+enum { kFullLayout = 0, kSpreadLayout = 1, kPairLayout = 2 };
 template <int kLayout>
 struct Pipe;
 template <>
@@ -114,6 +115,30 @@ struct Pipe<kSpreadLayout> {
     static constexpr uint32_t kBarOff = 32768u + kStages * kBBytes;
     static constexpr size_t kSmem = 1024 + kBarOff + 256;
 };
+// kPairLayout (large flat launches): a cluster of two CTAs runs one M = 256,
+// N = 256 MMA (cta_group::2).  CTA r holds the 128 frames of its query tile
+// (A) and database rows [128 r, 128 r + 128) of each tile (B, half of N) at
+// the same offsets as the other CTA, and its TMEM receives its frames' 128 x
+// 256 block of D, so the epilogue is the full layout's.  Per stage and CTA:
+// A 16 KB + B 16 KB, six stages (twice the full layout's bytes in flight per
+// MMA, a third less L2 traffic per FLOP).
+template <>
+struct Pipe<kPairLayout> {
+    static constexpr int kM = 2 * kTileM;  // the pair's MMA
+    static constexpr int kStages = 6;
+    static constexpr int kBlocks = 1;
+    static constexpr int kBlockRows = kTileM;
+    static constexpr int kRowsPerQuarter = 32;
+    static constexpr uint32_t kBHalf = kBBytes / 2;
+    static constexpr uint32_t kTx = 2 * (kTileM * kTileK * 2 + kBHalf);  // both CTAs' loads of a stage
+    __host__ __device__ static constexpr uint32_t a_off(int s) { return s * (16384u + kBHalf); }
+    __host__ __device__ static constexpr uint32_t a_block_off(int s, int) { return a_off(s); }
+    __host__ __device__ static constexpr uint32_t b_off(int s) { return a_off(s) + 16384u; }
+    __host__ __device__ static constexpr uint32_t norm_off(int ew) { return kStages * (16384u + kBHalf) + ew * 1024u; }
+    static constexpr uint32_t kBarOff = kStages * (16384u + kBHalf) + kNormBytes;
+    static constexpr size_t kSmem = 1024 + kBarOff + 256;
+};
+static_assert(Pipe<kPairLayout>::kSmem <= 232448, "cand_kernel shared memory (pair layout)");
 static_assert((Pipe<kSpreadLayout>::kStages + 1) / 2 * 8192u <= 24576u, "A packs below the norm buffers");
 static_assert(Pipe<kFullLayout>::kSmem <= 232448 && Pipe<kSpreadLayout>::kSmem <= 232448, "cand_kernel shared memory");
 static_assert(kNormBytes == kEpiWarps * 1024, "one 1 KB row-norm double buffer per epilogue warp");
@@ -154,6 +179,7 @@ struct CandArgs {
     const int32_t *list_start;    // pair offsets [nlist + 1] (lists in size order, not id order)
     const int32_t *list_count;    // pairs per list [nlist]
     int pair_stride;              // output stride: pairs capacity
+    int pair_layout;              // flat, kPairLayout: items are (query-tile pair, segment)
     // Per-frame bound words shared by every CTA (null: off; flat, and the
     // IVF fine stage): kBoundWords per frame, total-order bits of approximate
     // distances d~, +inf at call start.  Word 0: a list whose 8 best so far
@@ -182,14 +208,14 @@ struct Item {
 template <bool kIvf>
 __device__ __forceinline__ int item_total(const CandArgs &a) {
     if constexpr (kIvf) return *a.item_count;
-    else return a.segments * a.n_qtiles;
+    else return a.segments * (a.pair_layout ? (a.n_qtiles + 1) / 2 : a.n_qtiles);
 }
 
 // IVF items come largest first (the item table follows the lists in
 // descending size); CTA g takes items g, g + G, ... of a "snake" order that
 // reverses every other round of G, so each CTA's load evens out.
 template <bool kIvf>
-__device__ __forceinline__ Item item_at(const CandArgs &a, int item, int total) {
+__device__ __forceinline__ Item item_at(const CandArgs &a, int item, int total, int rank = 0) {
     Item it{};
     if constexpr (kIvf) {
         const int g = static_cast<int>(gridDim.x);
@@ -202,10 +228,13 @@ __device__ __forceinline__ Item item_at(const CandArgs &a, int item, int total) 
         it.b_end = a.list_offsets[e.x + 1];
         it.seg = e.x;  // the list (its group slot in the frames' bound words)
     } else {
-        const int qtile = item % a.n_qtiles;
-        it.seg = item / a.n_qtiles;
+        // pair layout: CTA `rank` of the pair takes query tile 2 p + rank
+        // (the second tile of an odd count is padding: no frames)
+        const int per_seg = a.pair_layout ? (a.n_qtiles + 1) / 2 : a.n_qtiles;
+        const int qtile = a.pair_layout ? 2 * (item % per_seg) + rank : item % per_seg;
+        it.seg = item / per_seg;
         it.a_row0 = qtile * kTileM;
-        it.a_rows = min(kTileM, a.frames - it.a_row0);
+        it.a_rows = max(0, min(kTileM, a.frames - it.a_row0));
         it.b_row0 = it.seg * a.seg_rows;
         it.b_end = min(it.b_row0 + a.seg_rows, a.n);
     }
@@ -340,6 +369,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     cand_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_x, CandArgs a) {
     using P = Pipe<kLayout>;
     constexpr int kStages = P::kStages;
+    constexpr bool kPair = kLayout == kPairLayout;
     static_assert(!kIvf || kLayout == kFullLayout, "IVF work items use the full layout");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -358,6 +388,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     // flat producer waits for the query tiles only (below)
     if constexpr (kIvf) grid_dependency_wait();
     const int items = item_total<kIvf>(a);
+    // pair layout: the cluster is the unit of work; CTA rank 0 (the leader)
+    // issues the MMA and owns the stage barriers both CTAs' loads complete
+    const int rank = kPair ? static_cast<int>(tc::cluster_rank()) : 0;
+    const int first_item = kPair ? static_cast<int>(tc::cluster_id()) : static_cast<int>(blockIdx.x);
+    const int item_step = kPair ? static_cast<int>(tc::cluster_count()) : static_cast<int>(gridDim.x);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -366,7 +401,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&acc_full[b], 1);
-            tc::mbar_init(&acc_empty[b], kEpiWarps);
+            tc::mbar_init(&acc_empty[b], kPair ? 2 * kEpiWarps : kEpiWarps);
         }
         *abort_flag = 0;
         tc::fence_mbarrier_init();
@@ -376,11 +411,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         tc::tma_prefetch(&tmap_x);
     }
     if (warp == 1) {
-        tc::tmem_alloc(tmem_slot, kTmemCols);
-        tc::tmem_relinquish();
+        if constexpr (kPair) {
+            tc::tmem_alloc_pair(tmem_slot, kTmemCols);
+            tc::tmem_relinquish_pair();
+        } else {
+            tc::tmem_alloc(tmem_slot, kTmemCols);
+            tc::tmem_relinquish();
+        }
     }
     tc::tc_fence_before();
-    __syncthreads();
+    if constexpr (kPair) tc::cluster_sync();  // the leader's barriers exist before the other CTA's loads
+    else __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -395,16 +436,27 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             // Flat: the database tiles of the first stages do not depend on
             // the query preparation, so they are requested before waiting
             // for it; those stages then only add their query tile.
+            // pair layout: this CTA's database rows are its half of each
+            // tile; every load completes on the leader's stage barrier,
+            // whose expected bytes (both CTAs' loads) the leader sets
+            const int32_t b_half = kPair ? rank * (kTileN / 2) : 0;
+            auto stage_bar = [&](int st) -> uint32_t {
+                return kPair ? tc::map_to_rank(&full[st], 0) : tc::smem_u32(&full[st]);
+            };
+            auto load = [&](void *dst, const CUtensorMap *map, int st, int32_t x, int32_t y) {
+                if constexpr (kPair) tc::tma_load_2d_pair(dst, map, stage_bar(st), x, y);
+                else tc::tma_load_2d(dst, map, &full[st], x, y);
+            };
             int early = 0;
             if constexpr (!kIvf) {
-                if (static_cast<int>(blockIdx.x) < items) {
-                    const Item it0 = item_at<kIvf>(a, blockIdx.x, items);
+                if (first_item < items) {
+                    const Item it0 = item_at<kIvf>(a, first_item, items, rank);
                     early = min(kStages, it0.tiles * a.ksteps);
                     for (int s = 0; s < early; ++s) {
                         const int t = s / a.ksteps, k = s % a.ksteps;
-                        tc::mbar_arrive_expect_tx(&full[s], P::kTx);
-                        tc::tma_load_2d(smem + P::b_off(s), &tmap_x, &full[s], k * kTileK,
-                                        static_cast<int32_t>(it0.b_row0 + t * kTileN));
+                        if (rank == 0) tc::mbar_arrive_expect_tx(&full[s], P::kTx);
+                        load(smem + P::b_off(s), &tmap_x, s, k * kTileK,
+                             static_cast<int32_t>(it0.b_row0 + t * kTileN) + b_half);
                     }
                 }
                 grid_dependency_wait();
@@ -412,8 +464,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             int stage = 0;
             uint32_t phase = 0;
             int issued = 0;
-            for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
-                const Item it = item_at<kIvf>(a, item, items);
+            for (int item = first_item; item < items && !*abort_flag; item += item_step) {
+                const Item it = item_at<kIvf>(a, item, items, rank);
                 for (int t = 0; t < it.tiles && !*abort_flag; ++t) {
                     for (int k = 0; k < a.ksteps; ++k, ++issued) {
                         if (!tc::mbar_wait(&empty[stage], phase ^ 1, kWaitLimitNs)) {
@@ -421,14 +473,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                             break;
                         }
                         if (issued >= early) {  // else the database tile is already requested
-                            tc::mbar_arrive_expect_tx(&full[stage], P::kTx);
-                            tc::tma_load_2d(smem + P::b_off(stage), &tmap_x, &full[stage], k * kTileK,
-                                            static_cast<int32_t>(it.b_row0 + t * kTileN));
+                            if (rank == 0) tc::mbar_arrive_expect_tx(&full[stage], P::kTx);
+                            load(smem + P::b_off(stage), &tmap_x, stage, k * kTileK,
+                                 static_cast<int32_t>(it.b_row0 + t * kTileN) + b_half);
                         }
 #pragma unroll
                         for (int qb = 0; qb < P::kBlocks; ++qb)
-                            tc::tma_load_2d(smem + P::a_block_off(stage, qb), &tmap_q, &full[stage], k * kTileK,
-                                            it.a_row0 + qb * P::kBlockRows);
+                            load(smem + P::a_block_off(stage, qb), &tmap_q, stage, k * kTileK,
+                                 it.a_row0 + qb * P::kBlockRows);
                         if (++stage == kStages) {
                             stage = 0;
                             phase ^= 1;
@@ -450,14 +502,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         // for the whole kernel resumed microseconds after it released.
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer (one thread)
+        if (lane == 0 && rank == 0) {
+            // ---------------- MMA issuer (one thread; the pair's leader)
             const uint32_t idesc = tc::idesc_f16(P::kM, kTileN, kFormatF16);
             int stage = 0;
             uint32_t phase = 0;
             uint32_t acc_count = 0;
-            for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
-                const Item it = item_at<kIvf>(a, item, items);
+            for (int item = first_item; item < items && !*abort_flag; item += item_step) {
+                const Item it = item_at<kIvf>(a, item, items, rank);
                 for (int t = 0; t < it.tiles && !*abort_flag; ++t) {
                     const uint32_t b = acc_count & 1;
                     if (!tc::mbar_wait(&acc_empty[b], ((acc_count >> 1) & 1) ^ 1, kWaitLimitNs)) {
@@ -478,17 +530,23 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                         const uint32_t sb = tc::smem_u32(smem + P::b_off(stage));
 #pragma unroll
                         for (int kk = 0; kk < kTileK / 16; ++kk) {
-                            tc::mma_f16(d_tmem, tc::smem_desc_sw128(sa + kk * 32), tc::smem_desc_sw128(sb + kk * 32),
-                                        idesc, (k | kk) != 0);
+                            if constexpr (kPair)
+                                tc::mma_f16_pair(d_tmem, tc::smem_desc_sw128(sa + kk * 32),
+                                                 tc::smem_desc_sw128(sb + kk * 32), idesc, (k | kk) != 0);
+                            else
+                                tc::mma_f16(d_tmem, tc::smem_desc_sw128(sa + kk * 32),
+                                            tc::smem_desc_sw128(sb + kk * 32), idesc, (k | kk) != 0);
                         }
-                        tc::mma_commit(&empty[stage]);
+                        if constexpr (kPair) tc::mma_commit_pair(&empty[stage]);  // both CTAs' stage
+                        else tc::mma_commit(&empty[stage]);
                         if (++stage == kStages) {
                             stage = 0;
                             phase ^= 1;
                         }
                     }
                     if (!ok) break;
-                    tc::mma_commit(&acc_full[b]);
+                    if constexpr (kPair) tc::mma_commit_pair(&acc_full[b]);  // both CTAs' epilogues
+                    else tc::mma_commit(&acc_full[b]);
                     ++acc_count;
                 }
             }
@@ -511,8 +569,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         uint32_t acc_count = 0;
         const float inf = __int_as_float(0x7f800000);
-        for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
-            const Item it = item_at<kIvf>(a, item, items);
+        // pair layout: the accumulator is the leader's to reuse; both CTAs'
+        // epilogue warps release it on the leader's barrier
+        auto release_acc = [&](uint32_t buf) {
+            if (kPair && rank != 0) tc::mbar_arrive_cluster(tc::map_to_rank(&acc_empty[buf], 0));
+            else tc::mbar_arrive(&acc_empty[buf]);
+        };
+        for (int item = first_item; item < items && !*abort_flag; item += item_step) {
+            const Item it = item_at<kIvf>(a, item, items, rank);
             const int64_t row0 = it.b_row0;
             const int tiles = it.tiles;
             TopList<K> top;
@@ -570,7 +634,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                     // frame tile: release the accumulator without reading it
                     tc::tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
+                    if (lane == 0) release_acc(b);
                     ++acc_count;
                     continue;
                 }
@@ -649,7 +713,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                 }
                 tc::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&acc_empty[b]);
+                if (lane == 0) release_acc(b);
                 ++acc_count;
                 if (gp != nullptr && top.dist[7] < published) {
                     published = top.dist[7];
@@ -697,10 +761,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         }
     }
     tc::tc_fence_before();
-    __syncthreads();
+    if constexpr (kPair) tc::cluster_sync();  // neither CTA leaves while the other may use its memory
+    else __syncthreads();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, kTmemCols);
+        if constexpr (kPair) tc::tmem_dealloc_pair(tmem, kTmemCols);
+        else tc::tmem_dealloc(tmem, kTmemCols);
     }
 }
 
@@ -2175,6 +2241,29 @@ void launch_cand_flat(const Plan &p, int grid, const void *q16, int d_pad, const
     cuda_check(launch_pdl(kernel, dim3(grid), dim3(kThreadsTC), smem, stream, tmap_q, tmap_x, ca));
 }
 
+// Launches the CTA-pair candidate kernel (clusters of two CTAs, cta_group::2
+// MMA) behind prep_queries_kernel; `tmap_x_half` boxes 128 database rows.
+void launch_cand_pair(int clusters, const void *q16, int d_pad, const CUtensorMap &tmap_x_half, const CandArgs &ca,
+                      cudaStream_t stream) {
+    CUtensorMap tmap_q;
+    encode_rows(&tmap_q, q16, d_pad, ca.frames, Pipe<kPairLayout>::kBlockRows);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
+    cfg.blockDim = dim3(kThreadsTC);
+    cfg.dynamicSmemBytes = Pipe<kPairLayout>::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cuda_check(cudaLaunchKernelEx(&cfg, cand_kernel<false, kIvfKeep, kPairLayout>, tmap_q, tmap_x_half, ca));
+}
+
 // The shared filter bound of a flat call: per-frame bounds, the frames'
 // stats and the index's certificate constants.
 void set_shared_bound(CandArgs &ca, const VfrIndex *ix, unsigned int *gbound, const float4 *qstats) {
@@ -2203,6 +2292,33 @@ Plan make_plan(size_t frames, int64_t n, int sms) {
         const int64_t waves = (seg * p.n_qtiles + sms - 1) / sms;
         // each item restarts its per-frame top list (a burst of insertions
         // worth ~2 tiles of epilogue work) and adds keys to the merge
+        const double cost = static_cast<double>(waves * (tps + 2)) + 0.02 * static_cast<double>(seg);
+        if (cost < best - 1e-9) {
+            best = cost;
+            p.segments = static_cast<int>(seg);
+            p.tiles_per_seg = static_cast<int>(tps);
+        }
+    }
+    return p;
+}
+
+// make_plan for the CTA-pair layout: work items are (query-tile pair,
+// segment) and `clusters` pairs run at once; the candidate lists per frame
+// (segments x kHalves) stay within the same workspace bound.
+Plan make_plan_pair(size_t frames, int64_t n, int sms, int clusters) {
+    Plan p{};
+    p.n_qtiles = static_cast<int>((frames + kTileM - 1) / kTileM);
+    const int64_t pairs = (p.n_qtiles + 1) / 2;
+    const int64_t ntiles = (n + kTileN - 1) / kTileN;
+    const int64_t cap = std::max<int64_t>(static_cast<int64_t>(p.n_qtiles) * 16, static_cast<int64_t>(sms) * 8);
+    double best = 1e300;
+    p.segments = 1;
+    p.tiles_per_seg = static_cast<int>(ntiles);
+    for (int64_t s = 1; s <= std::min<int64_t>(kMaxSegments, ntiles); ++s) {
+        const int64_t tps = (ntiles + s - 1) / s;
+        const int64_t seg = (ntiles + tps - 1) / tps;
+        if (seg * p.n_qtiles > cap) break;
+        const int64_t waves = (seg * pairs + clusters - 1) / clusters;
         const double cost = static_cast<double>(waves * (tps + 2)) + 0.02 * static_cast<double>(seg);
         if (cost < best - 1e-9) {
             best = cost;
@@ -2998,6 +3114,7 @@ void build_tc(VfrIndex *ix) {
         return;
     }
     encode_rows(&ix->tmap_vectors, ix->vectors_h, ix->d_pad, ix->n_pad, kTileN);
+    encode_rows(&ix->tmap_vectors_half, ix->vectors_h, ix->d_pad, ix->n_pad, kTileN / 2);
     if (ivf) {
         encode_rows(&ix->tmap_centroids, ix->centroids_h, ix->d_pad, ix->nlist_pad, kTileN);
         // lists by descending size (ties by id): the fine stage's item table
@@ -3018,6 +3135,34 @@ void build_tc(VfrIndex *ix) {
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kSmall));
     cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep, kSpreadLayout>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kSmall));
+    ix->pair_clusters = 0;
+    if (!ivf) {
+        // CTA pairs (clusters of two) that can be resident at once
+        constexpr int kPairSmem = static_cast<int>(Pipe<kPairLayout>::kSmem);
+        cuda_check(cudaFuncSetAttribute(cand_kernel<false, kIvfKeep, kPairLayout>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem));
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(static_cast<unsigned>(2 * (ix->sm_count / 2)));
+        cfg.blockDim = dim3(kThreadsTC);
+        cfg.dynamicSmemBytes = kPairSmem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        // opt-in (VFR_PAIR=1): measured on c5 it runs at the one-CTA
+        // layout's rate per clock, so the one-CTA layout stays the default
+        const char *env = std::getenv("VFR_PAIR");
+        if (env && env[0] == '1') {
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, cand_kernel<false, kIvfKeep, kPairLayout>, &cfg) ==
+                cudaSuccess)
+                ix->pair_clusters = clusters;
+            cudaGetLastError();  // a device without the query keeps the one-CTA layouts
+        }
+    }
     {
         int optin = 0;
         cuda_check(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ix->device));
@@ -3343,7 +3488,16 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     int32_t *fcount = reinterpret_cast<int32_t *>(ws + l.fcount);
     unsigned int *gbound = reinterpret_cast<unsigned int *>(ws + l.gbound);
 
-    const Plan p = make_plan(frames, ix->n, ix->sm_count);
+    Plan p = make_plan(frames, ix->n, ix->sm_count);
+    // large launches with long work items run on CTA pairs
+    bool pair = false;
+    if (ix->pair_clusters > 0 && frames >= static_cast<size_t>(kPairMinFrames)) {
+        const Plan pp = make_plan_pair(frames, ix->n, ix->sm_count, ix->pair_clusters);
+        if (pp.tiles_per_seg > kShortItemTiles) {
+            p = pp;
+            pair = true;
+        }
+    }
     const long long lanes = static_cast<long long>(frames) * 32;
     ix->prof.begin(kProfPrep, stream);
     prep_queries_kernel<<<static_cast<unsigned>((lanes + 255) / 256), 256, 0, stream>>>(
@@ -3367,11 +3521,17 @@ void run_tc(VfrIndex *ix, const float *queries, float *out, const float *rate, i
     ca.thr_stride = (ca.lists + 3) & ~3;
     ca.counters = ix->counters;
     set_shared_bound(ca, ix, gbound, qstats);
-    const int items = p.segments * p.n_qtiles;
-    const int grid = std::min(items, ix->sm_count);
+    ca.pair_layout = pair ? 1 : 0;
     note_plan(ix, p, frames);
+    if (pair) ix->last_layout = kPairLayout;
     ix->prof.begin(kProfCand, stream);
-    launch_cand_flat(p, grid, q16, ix->d_pad, ix->tmap_vectors, ca, stream);
+    if (pair) {
+        const int items = p.segments * ((p.n_qtiles + 1) / 2);
+        launch_cand_pair(std::min(items, ix->pair_clusters), q16, ix->d_pad, ix->tmap_vectors_half, ca, stream);
+    } else {
+        const int items = p.segments * p.n_qtiles;
+        launch_cand_flat(p, std::min(items, ix->sm_count), q16, ix->d_pad, ix->tmap_vectors, ca, stream);
+    }
     ix->prof.end(stream);
 
     MergeArgs ma{};

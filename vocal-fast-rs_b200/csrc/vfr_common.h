@@ -160,6 +160,8 @@ struct VfrIndex {
     int32_t *list_order = nullptr;  // [nlist] list ids by descending size (IVF fine-stage order)
     alignas(64) CUtensorMap tmap_centroids;
     alignas(64) CUtensorMap tmap_vectors;  // fp16 rows, box [256 rows][64]
+    alignas(64) CUtensorMap tmap_vectors_half;  // fp16 rows, box [128 rows][64] (CTA-pair tiles)
+    int pair_clusters = 0;  // CTA pairs that fit at once (0: no pair layout)
     bool have_tc = false;
     vfr::Workspace ws;
     vfr::Profiler prof;
