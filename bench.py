@@ -65,6 +65,7 @@ def args_parse():
     ap.add_argument("--no-training", action="store_true", help="skip the IVF training timing")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of rank 0's first frames")
     ap.add_argument("--no-configs", action="store_true", help="skip the c1/c2/published-shape timings")
+    ap.add_argument("--no-cublas", action="store_true", help="skip the same-box cuBLAS reference")
     return ap.parse_args()
 
 
@@ -126,6 +127,36 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
                 "power_w_max": max(power) if power else None, "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def cublas_same_box(device):
+    """torch.matmul bf16 8192^3 (cuBLAS) back to back for about 2 s on this
+    GPU with the SM clock sampled: the same-box reference for the candidate
+    kernel's tensor rate (the measured peaks come from another box, and the
+    clock under the power cap differs between boxes)."""
+    import torch
+
+    a = torch.randn(8192, 8192, dtype=torch.bfloat16, device=device)
+    b = torch.randn_like(a)
+    c = torch.empty_like(a)
+    for _ in range(20):
+        torch.matmul(a, b, out=c)
+    torch.cuda.synchronize()
+    sampler = ClockSampler()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 2500
+    e0.record()
+    for _ in range(reps):
+        torch.matmul(a, b, out=c)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop({torch.cuda.current_device()})
+    ms = e0.elapsed_time(e1) / reps
+    del a, b, c
+    torch.cuda.empty_cache()
+    return {"tflops": 2 * 8192 ** 3 / ms / 1e9, "ms_per_gemm": ms, "clocks": clocks,
+            "what": "torch.matmul bf16 8192^3, 2,500 back to back on this GPU after the timed steps"}
 
 
 def dist_setup(gpus):
@@ -921,6 +952,13 @@ def main():
         extra["c1"] = flat_config(device, "c1")
         extra["c2"] = flat_config(device, "c2")
         extra["published_shape"] = published_shape(device)
+    if rank == 0 and world == 1 and not a.no_cublas and roofline and roofline.get("unit") == "TFLOP/s":
+        ref = cublas_same_box(device)
+        extra["cublas_same_box"] = ref
+        mhz, ref_mhz = (clocks or {}).get("sm_mhz"), ref["clocks"].get("sm_mhz")
+        if roofline.get("achieved") and mhz and ref_mhz:
+            # per clock: the kernel's TFLOP/s per MHz over cuBLAS's on this box
+            roofline["per_clock_vs_cublas_same_box"] = (roofline["achieved"] / mhz) / (ref["tflops"] / ref_mhz)
     cpu = None
     if rank == 0 and world == 1 and full_host is not None and not a.no_cpu_baseline:
         cpu = cpu_baseline(full_host, queries.cpu().numpy(), w.ratio, n)
