@@ -323,7 +323,7 @@ __device__ void exact_split(const ExactArgs &a, long long frame, int i, int s, i
 // tensor-core engine could not certify), a fixed grid over it: with at most
 // kSplitFrames listed frames (and split scratch), every frame gets
 // gridDim.x / count CTAs, each scanning a slice; otherwise one CTA per frame.
-__global__ void __launch_bounds__(kThreads, 1) exact_kernel(ExactArgs a) {
+__global__ void __launch_bounds__(kThreads, 3) exact_kernel(ExactArgs a) {
     extern __shared__ float q[];  // [d] copy of the frame
     __shared__ FrameSmem sm;
     grid_dependency_wait();  // the frame list and the outputs belong to the kernel before
