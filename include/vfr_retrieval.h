@@ -281,7 +281,7 @@ VFR_API int vfr_retrieval_blend_save_raw(VfrIndex *index, float *features, float
                                          int32_t width, const float *index_rate, VfrStream *stream, char **error);
 
 /* JSON diagnostics (engine, candidate width, empty-frame count, fallback
- * count, layout).  Returns the length needed (excluding NUL); writes at most
+ * count, rows the exact re-runs scanned, layout).  Returns the length needed (excluding NUL); writes at most
  * length bytes including NUL.  Synchronises the index's device. */
 VFR_API size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t length);
 

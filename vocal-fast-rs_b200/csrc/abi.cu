@@ -58,6 +58,7 @@ void free_index(VfrIndex *ix) noexcept {
     if (ix->x2_ws) cudaFree(ix->x2_ws);
     if (ix->split_keys) cudaFree(ix->split_keys);
     if (ix->split_done) cudaFree(ix->split_done);
+    if (ix->rerun_hints) cudaFree(ix->rerun_hints);
     ix->shared.reset();
     cudaSetDevice(previous);
     delete ix;
@@ -184,6 +185,8 @@ void finish_index(VfrIndex *ix, const VfrOptions &o) {
     cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->split_keys), kSplitKeyBytes), "cudaMalloc re-run scratch");
     cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->split_done), kSplitFrames * sizeof(int32_t)));
     cuda_check(cudaMemset(ix->split_done, 0, kSplitFrames * sizeof(int32_t)));
+    cuda_check(cudaMalloc(reinterpret_cast<void **>(&ix->rerun_hints), kSplitFrames * sizeof(RerunHint)));
+    cuda_check(cudaMemset(ix->rerun_hints, 0xff, kSplitFrames * sizeof(RerunHint)));  // frame = -1
     cuda_check(cudaDeviceSynchronize());
 }
 
@@ -254,6 +257,7 @@ void publish_shared(VfrIndex *ix, const ShareKey &key) {
     rows->proto.counters = nullptr;
     rows->proto.split_keys = nullptr;
     rows->proto.split_done = nullptr;
+    rows->proto.rerun_hints = nullptr;
     rows->proto.ws = Workspace{};
     rows->proto.prof.pool.clear();
     rows->proto.prof.marks.clear();
@@ -576,13 +580,13 @@ extern "C" size_t vfr_retrieval_diagnostics(VfrIndex *index, char *json, size_t 
                           "{\"engine\":\"%s\",\"tensor_cores\":%s,\"candidates\":%d,\"dimensions\":%d,\"nlist\":%d,"
                           "\"nprobe\":%d,\"vectors\":%lld,\"label_base\":%lld,\"device\":%d,\"workspace_frames\":%zu,"
                           "\"workspace_bytes\":%zu,\"empty_frames\":%llu,\"fallback_frames\":%llu,"
-                          "\"candidate_frames\":%llu,\"timeouts\":%llu,\"max_row_norm\":%.9g,"
+                          "\"candidate_frames\":%llu,\"rerun_rows\":%llu,\"timeouts\":%llu,\"max_row_norm\":%.9g,"
                           "\"max_row_residual\":%.9g,\"shared_handles\":%ld,\"last_plan\":{\"keep\":%d,"
                           "\"segments\":%d,\"tiles_per_segment\":%d,\"layout\":\"%s\"},\"last_engine\":\"%s\"}",
                           engine, index->have_tc ? "true" : "false", index->candidates, index->d, index->nlist,
                           index->nprobe, static_cast<long long>(index->n), static_cast<long long>(index->label_base),
                           index->device, index->ws.frames, index->ws.bytes, c.empty_frames, c.fallback_frames,
-                          c.candidate_frames, c.timeouts, index->max_row_norm, index->max_row_residual,
+                          c.candidate_frames, c.rerun_rows, c.timeouts, index->max_row_norm, index->max_row_residual,
                           static_cast<long>(index->shared ? index->shared.use_count() : 0), index->last_keep,
                           index->last_segments, index->last_tiles_per_seg,
                           index->last_layout < 0 ? "none" : index->last_layout == 0 ? "full" : index->last_layout == 1 ? "spread" : "pair",

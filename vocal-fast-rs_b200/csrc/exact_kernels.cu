@@ -59,6 +59,7 @@ struct FrameSmem {
     unsigned long long wave_keys[kOctets];
     int probe_list[kMaxProbe];
     uint32_t probe_base[kMaxProbe + 1];
+    uint32_t scan_base[kMaxProbe + 1];  // probe_base over the probes being scanned only
     unsigned long long octet_best[kOctets * 8];
     unsigned long long best[8];
     unsigned long long red[kThreads / 32];
@@ -69,9 +70,11 @@ struct FrameSmem {
 };
 
 // The coarse stage: the first nprobe lists in (distance, list id) order and
-// the scan position where each starts (probe_base[probes] = rows scanned).
-// Returns the number of probed lists.  Called by every thread.
-__device__ int coarse_stage(const ExactArgs &a, long long frame, const float *q, FrameSmem &sm) {
+// the scan position where each starts (probe_base[probes] = rows scanned);
+// scan_base is the same over the probes in scan_mask only (the rows this
+// call scans).  Returns the number of probed lists.  Called by every thread.
+__device__ int coarse_stage(const ExactArgs &a, long long frame, const float *q, FrameSmem &sm,
+                            uint32_t scan_mask = ~0u) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
     const int octet_base = lane & ~7;
     const int d = a.d;
@@ -114,33 +117,134 @@ __device__ int coarse_stage(const ExactArgs &a, long long frame, const float *q,
     }
     __syncthreads();
     if (tid == 0) {
-        uint32_t acc = 0;
+        uint32_t acc = 0, scanned = 0;
         for (int r = 0; r < probes; ++r) {
+            const uint32_t len = static_cast<uint32_t>(a.offsets[sm.probe_list[r] + 1] - a.offsets[sm.probe_list[r]]);
             sm.probe_base[r] = acc;
-            acc += static_cast<uint32_t>(a.offsets[sm.probe_list[r] + 1] - a.offsets[sm.probe_list[r]]);
+            sm.scan_base[r] = scanned;
+            acc += len;
+            if ((scan_mask >> r) & 1u) scanned += len;
         }
         sm.probe_base[probes] = acc;
+        sm.scan_base[probes] = scanned;
     }
     __syncthreads();
     return probes;
 }
 
-// Scans scan positions [p0, p1) of the probed lists (list r covers
-// positions probe_base[r] .. probe_base[r + 1], rows in storage order) and
-// leaves the CTA's top 8 keys (distance, scan position) in sm.best.
+// Squared L2 distance in the AVX2 order from a pair of threads (lanes 2p
+// and 2p+1, h = lane & 1): thread h owns lanes 4h..4h+3 of the eight and
+// reads its half of every 8-float block as one float4, so a thread keeps
+// eight 16-byte row loads in flight where an octet thread keeps 4-byte ones.
+// Each lane's sum still runs over the blocks in order from +0, and the eight
+// lane sums are added in lane order from -0 before the tail, so the value is
+// octet_l2's bit for bit.  Needs d % 4 == 0 and 16-byte aligned q and rows;
+// both threads of the pair return it.
+__device__ __forceinline__ float pair_l2(const float *__restrict__ q, const float *__restrict__ x, int d, int h) {
+    const int blocks = d >> 3;
+    float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
+    const float4 *xv = reinterpret_cast<const float4 *>(x) + h;
+    const float4 *qv = reinterpret_cast<const float4 *>(q) + h;
+#pragma unroll 8
+    for (int b = 0; b < blocks; ++b) {
+        const float4 xx = __ldg(xv + 2 * b);
+        const float4 qq = qv[2 * b];
+        const float t0 = __fsub_rn(qq.x, xx.x), t1 = __fsub_rn(qq.y, xx.y);
+        const float t2 = __fsub_rn(qq.z, xx.z), t3 = __fsub_rn(qq.w, xx.w);
+        c0 = __fadd_rn(c0, __fmul_rn(t0, t0));
+        c1 = __fadd_rn(c1, __fmul_rn(t1, t1));
+        c2 = __fadd_rn(c2, __fmul_rn(t2, t2));
+        c3 = __fadd_rn(c3, __fmul_rn(t3, t3));
+    }
+    const float o0 = __shfl_xor_sync(kFullMask, c0, 1), o1 = __shfl_xor_sync(kFullMask, c1, 1);
+    const float o2 = __shfl_xor_sync(kFullMask, c2, 1), o3 = __shfl_xor_sync(kFullMask, c3, 1);
+    const float l[8] = {h ? o0 : c0, h ? o1 : c1, h ? o2 : c2, h ? o3 : c3,
+                        h ? c0 : o0, h ? c1 : o1, h ? c2 : o2, h ? c3 : o3};
+    float s = -0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s = __fadd_rn(s, l[i]);
+    float tail = -0.0f;
+    for (int i = blocks * 8; i < d; ++i) {
+        const float t = __fsub_rn(q[i], __ldg(x + i));
+        tail = __fadd_rn(tail, __fmul_rn(t, t));
+    }
+    return __fadd_rn(s, tail);
+}
+
+// scan_range with pair_l2: 128 rows per pass (one per thread pair), each
+// pair keeping its own top 8; the pairs' lists are merged per warp in
+// registers, then across the warps.
+__device__ void scan_range_pairs(const ExactArgs &a, const float *q, FrameSmem &sm, int probes, uint32_t p0,
+                                 uint32_t p1) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, pair = tid >> 1, h = tid & 1;
+    const int d = a.d;
+    Top8 top;
+    top.init();
+    for (int r = 0; r < probes; ++r) {
+        // [p0, p1) counts the scanned probes' rows only; keys carry the
+        // full scan position lb + (row - first)
+        const uint32_t lb = sm.probe_base[r], cb = sm.scan_base[r], ce = sm.scan_base[r + 1];
+        const uint32_t from = cb > p0 ? cb : p0, to = ce < p1 ? ce : p1;
+        if (from >= to) continue;
+        const int first = a.offsets[sm.probe_list[r]];
+        const int begin = first + static_cast<int>(from - cb);
+        const int end = first + static_cast<int>(to - cb);
+        for (int row0 = begin; row0 < end; row0 += kThreads / 2) {
+            const int row = row0 + pair;
+            const float dist = pair_l2(q, a.vectors + static_cast<size_t>(row < end ? row : begin) * d, d, h);
+            // the reference never admits +inf (best starts at +inf, `>=` rejects)
+            if (row < end && dist < __int_as_float(0x7f800000))
+                top.insert(make_key(dist, lb + static_cast<uint32_t>(row - first)));
+        }
+    }
+    // the warp's 16 lists (even lanes): eight rounds of a warp minimum, the
+    // owner of each minimum advancing its head (keys are distinct)
+    int head = 0;
+    for (int i = 0; i < 8; ++i) {
+        unsigned long long mine = kEmptyKey;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mine = (h == 0 && e == head) ? top.k[e] : mine;
+        const unsigned long long m = warp_min_u64(mine);
+        if (mine == m && m != kEmptyKey) ++head;
+        if (lane == 0) sm.octet_best[warp * 8 + i] = m;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        head = 0;
+        for (int i = 0; i < 8; ++i) {
+            const unsigned long long mine =
+                lane < kThreads / 32 && head < 8 ? sm.octet_best[lane * 8 + head] : kEmptyKey;
+            const unsigned long long m = warp_min_u64(mine);
+            if (mine == m && m != kEmptyKey) ++head;
+            if (lane == 0) sm.best[i] = m;
+        }
+    }
+    __syncthreads();
+}
+
+// Scans positions [p0, p1) of the scanned probes' rows (probe r covers
+// scan_base[r] .. scan_base[r + 1], rows in storage order; with every probe
+// scanned these are the scan positions) and leaves the CTA's top 8 keys
+// (distance, scan position probe_base[r] + row offset) in sm.best.
 __device__ void scan_range(const ExactArgs &a, const float *q, FrameSmem &sm, int probes, uint32_t p0, uint32_t p1) {
+    if ((a.d & 3) == 0 && (reinterpret_cast<uintptr_t>(a.vectors) & 15) == 0) {
+        scan_range_pairs(a, q, sm, probes, p0, p1);
+        return;
+    }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, octet = tid >> 3, j = tid & 7;
     const int octet_base = lane & ~7;
     const int d = a.d;
     Top8 top;
     top.init();
     for (int r = 0; r < probes; ++r) {
-        const uint32_t lb = sm.probe_base[r], le = sm.probe_base[r + 1];
-        const uint32_t from = lb > p0 ? lb : p0, to = le < p1 ? le : p1;
+        // [p0, p1) counts the scanned probes' rows only; keys carry the
+        // full scan position lb + (row - first)
+        const uint32_t lb = sm.probe_base[r], cb = sm.scan_base[r], ce = sm.scan_base[r + 1];
+        const uint32_t from = cb > p0 ? cb : p0, to = ce < p1 ? ce : p1;
         if (from >= to) continue;
         const int first = a.offsets[sm.probe_list[r]];
-        const int begin = first + static_cast<int>(from - lb);
-        const int end = first + static_cast<int>(to - lb);
+        const int begin = first + static_cast<int>(from - cb);
+        const int end = first + static_cast<int>(to - cb);
         for (int row0 = begin; row0 < end; row0 += 4 * kOctets) {
             const float *xs[4];
 #pragma unroll
@@ -266,6 +370,8 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame, float *q,
     float ratio;
     if (!frame_prologue(a, frame, q, ratio, true)) return;
     const int probes = coarse_stage(a, frame, q, sm);
+    if (threadIdx.x == 0 && a.frame_list && a.counters)
+        atomicAdd(&a.counters->rerun_rows, static_cast<unsigned long long>(sm.scan_base[probes]));
     scan_range(a, q, sm, probes, 0u, sm.probe_base[probes]);
     finish_frame(a, frame, q, ratio, sm, probes);
 }
@@ -279,10 +385,18 @@ __device__ void exact_split(const ExactArgs &a, long long frame, int i, int s, i
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float ratio;
     if (!frame_prologue(a, frame, q, ratio, s == 0)) return;
-    const int probes = coarse_stage(a, frame, q, sm);
-    const uint64_t total = sm.probe_base[probes];
+    // the fine stage's hint (IVF): scan only the probes it marks; every CTA
+    // of the frame reads it before the frame's counter below, and the last
+    // one clears it after use
+    const RerunHint *hint = nullptr;
+    if (a.hints != nullptr && i < kSplitFrames && a.probe_ok != nullptr && a.probe_ok[frame] &&
+        __ldcg(&a.hints[i].frame) == static_cast<int32_t>(frame))
+        hint = a.hints + i;
+    const int probes = coarse_stage(a, frame, q, sm, hint ? __ldcg(&hint->scan_mask) : ~0u);
+    const uint64_t total = sm.scan_base[probes];
     const uint32_t p0 = static_cast<uint32_t>(total * s / nsplit);
     const uint32_t p1 = static_cast<uint32_t>(total * (s + 1) / nsplit);
+    if (tid == 0 && a.counters && p1 > p0) atomicAdd(&a.counters->rerun_rows, static_cast<unsigned long long>(p1 - p0));
     scan_range(a, q, sm, probes, p0, p1);
     unsigned long long *slot = a.split_keys + (static_cast<size_t>(i) * kExactSplitGrid + s) * 8;
     if (tid < 8) slot[tid] = sm.best[tid];
@@ -294,6 +408,7 @@ __device__ void exact_split(const ExactArgs &a, long long frame, int i, int s, i
     __threadfence();
     if (tid == 0) {
         a.split_done[i] = 0;  // ready for the next call
+        if (hint != nullptr) a.hints[i].frame = -1;
         if (a.counters) atomicAdd(&a.counters->fallback_frames, 1ull);
     }
     // the slices' lists, merged: each thread keeps the top 8 of a strided
@@ -302,6 +417,7 @@ __device__ void exact_split(const ExactArgs &a, long long frame, int i, int s, i
     mine.init();
     const unsigned long long *all = a.split_keys + static_cast<size_t>(i) * kExactSplitGrid * 8;
     for (int e = tid; e < nsplit * 8; e += kThreads) mine.insert(__ldcg(all + e));
+    if (hint != nullptr && tid < 8) mine.insert(__ldcg(&hint->keys[tid]));  // the other probes' top 8
     int head = 0;
     for (int r = 0; r < 8; ++r) {
         unsigned long long cand = kEmptyKey;
@@ -324,7 +440,7 @@ __device__ void exact_split(const ExactArgs &a, long long frame, int i, int s, i
 // kSplitFrames listed frames (and split scratch), every frame gets
 // gridDim.x / count CTAs, each scanning a slice; otherwise one CTA per frame.
 __global__ void __launch_bounds__(kThreads, 3) exact_kernel(ExactArgs a) {
-    extern __shared__ float q[];  // [d] copy of the frame
+    extern __shared__ __align__(16) float q[];  // [d] copy of the frame
     __shared__ FrameSmem sm;
     grid_dependency_wait();  // the frame list and the outputs belong to the kernel before
     if (a.frame_list) {
@@ -335,6 +451,8 @@ __global__ void __launch_bounds__(kThreads, 3) exact_kernel(ExactArgs a) {
             if (s < nsplit) exact_split(a, a.frame_list[i], i, s, nsplit, q, sm);
         } else {
             for (int i = blockIdx.x; i < count; i += gridDim.x) {
+                // full scans: a hint of this entry is not needed
+                if (a.hints != nullptr && i < kSplitFrames && threadIdx.x == 0) a.hints[i].frame = -1;
                 exact_frame(a, a.frame_list[i], q, sm);
                 __syncthreads();
             }

@@ -16,6 +16,7 @@ struct DeviceCounters {
     unsigned long long fallback_frames;   // frames re-run by the exact scan
     unsigned long long timeouts;          // bounded waits that gave up
     unsigned long long candidate_frames;  // frames served by the tensor-core path
+    unsigned long long rerun_rows;        // rows the exact re-runs scanned
 };
 
 enum { kModeBlend = 0, kModeSearch = 1 };
@@ -49,10 +50,27 @@ struct ExactArgs {
     // coarse order) and whether they are set; reused instead of recomputed
     const int32_t *probes;
     const int32_t *probe_ok;
+    // optional (IVF, with split scratch): the fine stage's hints for the
+    // first kSplitFrames listed frames (RerunHint, below); null = full scans
+    struct RerunHint *hints;
 };
 constexpr int kSplitFrames = 64;       // listed frames that share the grid
 constexpr int kExactSplitGrid = 1184;  // CTAs of a frame-list launch at most
 constexpr size_t kSplitKeyBytes = static_cast<size_t>(kSplitFrames) * kExactSplitGrid * 8 * 8;
+// What the IVF merge hands the exact re-run about a frame it could not
+// certify (entry i of the hint array belongs to entry i of the frame list):
+// bit p of scan_mask marks probe p (coarse order) whose candidate lists
+// could not certify the frame, and keys[] holds the exact top 8 (distance,
+// scan position) of the re-ranked rows of the other probes.  Rows of those
+// other probes outside keys[] cannot enter the frame's exact top 8 (their
+// lists' thresholds or the narrowing limit exclude them), so the re-run
+// scans only the marked probes and merges keys[] in.  frame = -1 when the
+// entry holds nothing; the re-run clears it after use.
+struct RerunHint {
+    unsigned long long keys[8];
+    int32_t frame;
+    uint32_t scan_mask;
+};
 // frames: the frame count, or with a frame list the largest possible length.
 // after_kernel: launched behind another kernel of the same call, which it may
 // overlap until its own dependency wait (programmatic dependent launch).

@@ -2613,6 +2613,7 @@ struct IvfMergeArgs {
     float max_norm, max_hat, max_residual, acc_rel, norm_rel, exact_rel;
     int32_t *fallback_list;
     int32_t *fallback_count;
+    RerunHint *hints;  // [kSplitFrames] or null: what the exact re-run needs to rescan
     DeviceCounters *counters;
 };
 
@@ -2781,9 +2782,61 @@ __global__ void __launch_bounds__(32 * kIvfWarps, 3) ivf_merge_warp_kernel(IvfMe
     const bool ok = !too_many && certify(tmin, d8, qs, a.max_norm, a.max_hat, a.max_residual, a.acc_rel,
                                          a.norm_rel, a.exact_rel);
     if (!ok) {
+        int pos = 0;
         if (lane == 0) {
-            const int pos = atomicAdd(a.fallback_count, 1);
+            pos = atomicAdd(a.fallback_count, 1);
             a.fallback_list[pos] = static_cast<int32_t>(frame);
+        }
+        pos = __shfl_sync(kFullMask, pos, 0);
+        if (a.hints != nullptr && pos < kSplitFrames) {
+            // The probes the re-run must rescan: those with a list whose
+            // threshold cannot certify d8 (every probe when the re-rank set
+            // overflowed or holds fewer than 8 rows).  A list that certifies
+            // d8 dropped only rows that can neither reach nor tie the frame's
+            // exact 8th best (d8 bounds it from above); rows outside the
+            // re-rank set are beaten by the 8 rows at or below U.  So the
+            // other probes contribute at most their re-ranked rows, of which
+            // the exact top 8 is handed over.
+            uint32_t scan_mask = ~0u;
+            if (!too_many && count == 8) {
+                const bool fails = lane < L && !certify(thr, d8, qs, a.max_norm, a.max_hat, a.max_residual,
+                                                        a.acc_rel, a.norm_rel, a.exact_rel);
+                const uint32_t fb = __ballot_sync(kFullMask, fails);
+                scan_mask = 0u;
+                for (int p = 0; p < P; ++p)
+                    if ((fb >> (p * kHalves)) & ((1u << kHalves) - 1u)) scan_mask |= 1u << p;
+                if (scan_mask == 0u) scan_mask = ~0u;
+            }
+            unsigned long long v[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const unsigned long long key = lane + 32 * t < m ? ex[w][lane + 32 * t] : kEmptyKey;
+                const uint32_t spos = key_pos(key);
+                bool rescanned = true;
+                for (int pr = 0; pr < P; ++pr) {
+                    const int32_t s = __shfl_sync(kFullMask, pstart, pr), t2 = __shfl_sync(kFullMask, pend, pr);
+                    const uint32_t b = __shfl_sync(kFullMask, pbase, pr);
+                    if (spos >= b && spos < b + static_cast<uint32_t>(t2 - s)) rescanned = (scan_mask >> pr) & 1u;
+                }
+                v[t] = key != kEmptyKey && !rescanned ? key : kEmptyKey;
+            }
+            key_cx(v[0], v[1]); key_cx(v[2], v[3]); key_cx(v[0], v[2]); key_cx(v[1], v[3]); key_cx(v[1], v[2]);
+            RerunHint *h = a.hints + pos;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const unsigned long long mn = warp_min_u64(v[0]);
+                if (lane == 0) h->keys[r] = mn;
+                if (v[0] == mn && mn != kEmptyKey) {
+                    v[0] = v[1];
+                    v[1] = v[2];
+                    v[2] = v[3];
+                    v[3] = kEmptyKey;
+                }
+            }
+            if (lane == 0) {
+                h->scan_mask = scan_mask;
+                h->frame = static_cast<int32_t>(frame);
+            }
         }
         return;
     }
@@ -3421,6 +3474,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     im.norm_rel = norm_rel;
     im.exact_rel = exact_rel;
     im.fallback_list = flist;
+    im.hints = ix->rerun_hints;
     im.fallback_count = fcount;
     im.counters = ix->counters;
     im.frames = static_cast<long long>(frames);
@@ -3454,6 +3508,7 @@ void run_ivf(VfrIndex *ix, const float *queries, float *out, const float *rate, 
     ea.split_done = ix->split_done;
     ea.probes = probes;
     ea.probe_ok = probe_ok;
+    ea.hints = ix->rerun_hints;
     ix->prof.begin(kProfExact, stream);
     launch_exact(ea, static_cast<long long>(frames), stream, true);
     ix->prof.end(stream);

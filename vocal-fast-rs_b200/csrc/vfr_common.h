@@ -173,6 +173,7 @@ struct VfrIndex {
     // frames share its grid (ExactArgs::split_keys / split_done).
     unsigned long long *split_keys = nullptr;
     int32_t *split_done = nullptr;
+    vfr::RerunHint *rerun_hints = nullptr;  // [kSplitFrames], frame = -1 between calls
     // 2-D exact engine (exact2d.cu) for small IVF batches: the most rows a
     // frame's probed lists can hold, and its scratch.
     int64_t max_probed_rows = 0;
