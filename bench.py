@@ -721,6 +721,7 @@ def ivf(device):
         diag = idx.diagnostics()
         out[f"nprobe{nprobe}"] = {"ms_per_30k_frames": ms, "frames_per_s": queries.shape[0] / (ms / 1000.0),
                                   "exact_rerun_frames": diag["fallback_frames"] // 6,
+                                  "exact_rerun_rows": diag["rerun_rows"] // 6,
                                   "certified_frames": diag["candidate_frames"] // 6}
         idx.close()
         peaks, peak_kind = measured_peaks()
