@@ -27,6 +27,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kOctets = kThreads / 8;
+constexpr uint64_t kSplitRows = 128;  // rows per slice at least: one pass of the scan
 
 __device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long v) {
 #pragma unroll
@@ -376,7 +377,8 @@ __device__ void exact_frame(const ExactArgs &a, const long long frame, float *q,
     finish_frame(a, frame, q, ratio, sm, probes);
 }
 
-// Slice `s` of `nsplit` of fallback frame `i` (of at most kSplitFrames): the
+// Slice `s` of fallback frame `i` (of at most kSplitFrames), which has up to
+// `nsplit` CTAs and uses as many as its scan has passes of rows: the
 // CTA scans its share of the frame's probed rows and stores its top 8; the
 // last CTA of the frame to finish (device-scope fence and counter, no
 // waiting) merges the slices' lists and finishes the frame.  The keys carry
@@ -394,15 +396,22 @@ __device__ void exact_split(const ExactArgs &a, long long frame, int i, int s, i
         hint = a.hints + i;
     const int probes = coarse_stage(a, frame, q, sm, hint ? __ldcg(&hint->scan_mask) : ~0u);
     const uint64_t total = sm.scan_base[probes];
-    const uint32_t p0 = static_cast<uint32_t>(total * s / nsplit);
-    const uint32_t p1 = static_cast<uint32_t>(total * (s + 1) / nsplit);
+    // slices of at least one pass of rows each: a small scan (a partial IVF
+    // re-run) takes a few CTAs, and the rest of the frame's CTAs leave
+    // without touching the frame's counter (every CTA computes the same
+    // count from the same scan length)
+    const int used = static_cast<int>(min(static_cast<uint64_t>(nsplit),
+                                          max(uint64_t{1}, (total + kSplitRows - 1) / kSplitRows)));
+    if (s >= used) return;
+    const uint32_t p0 = static_cast<uint32_t>(total * s / used);
+    const uint32_t p1 = static_cast<uint32_t>(total * (s + 1) / used);
     if (tid == 0 && a.counters && p1 > p0) atomicAdd(&a.counters->rerun_rows, static_cast<unsigned long long>(p1 - p0));
     scan_range(a, q, sm, probes, p0, p1);
     unsigned long long *slot = a.split_keys + (static_cast<size_t>(i) * kExactSplitGrid + s) * 8;
     if (tid < 8) slot[tid] = sm.best[tid];
     __threadfence();
     __syncthreads();
-    if (tid == 0) sm.last = atomicAdd(a.split_done + i, 1) == nsplit - 1;
+    if (tid == 0) sm.last = atomicAdd(a.split_done + i, 1) == used - 1;
     __syncthreads();
     if (!sm.last) return;
     __threadfence();
@@ -416,7 +425,7 @@ __device__ void exact_split(const ExactArgs &a, long long frame, int i, int s, i
     Top8 mine;
     mine.init();
     const unsigned long long *all = a.split_keys + static_cast<size_t>(i) * kExactSplitGrid * 8;
-    for (int e = tid; e < nsplit * 8; e += kThreads) mine.insert(__ldcg(all + e));
+    for (int e = tid; e < used * 8; e += kThreads) mine.insert(__ldcg(all + e));
     if (hint != nullptr && tid < 8) mine.insert(__ldcg(&hint->keys[tid]));  // the other probes' top 8
     int head = 0;
     for (int r = 0; r < 8; ++r) {

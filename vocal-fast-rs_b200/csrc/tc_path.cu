@@ -2063,6 +2063,34 @@ __global__ void __launch_bounds__(32 * kMergeWarps, 3) merge_warp_kernel(MergeAr
         wsum = __dadd_rn(wsum, wv[k]);
     }
     const WeightDivisor sum = weight_divisor(wsum);
+    if ((d & 3) == 0 && ((reinterpret_cast<uintptr_t>(a.vectors) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+        // four elements per lane and step: one 16-byte load per neighbour
+        // row, a quarter of the dependent row round trips; each element's
+        // arithmetic (and so its result) is the scalar loop's
+        for (int i4 = lane; i4 < (d >> 2); i4 += 32) {
+            float4 r4[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                r4[k] = k < count ? __ldg(reinterpret_cast<const float4 *>(vr[k]) + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 q4 = reinterpret_cast<const float4 *>(q)[i4];
+            float x[8];
+            float4 o;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) x[k] = r4[k].x;
+            o.x = reference_blend_element<false>(q4.x, x, wv, sum, count, ratio);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) x[k] = r4[k].y;
+            o.y = reference_blend_element<false>(q4.y, x, wv, sum, count, ratio);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) x[k] = r4[k].z;
+            o.z = reference_blend_element<false>(q4.z, x, wv, sum, count, ratio);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) x[k] = r4[k].w;
+            o.w = reference_blend_element<false>(q4.w, x, wv, sum, count, ratio);
+            reinterpret_cast<float4 *>(dst)[i4] = o;
+        }
+        return;
+    }
     for (int i = lane; i < d; i += 32) {
         float x[8];
 #pragma unroll
@@ -2881,6 +2909,34 @@ __global__ void __launch_bounds__(32 * kIvfWarps, 3) ivf_merge_warp_kernel(IvfMe
         wsum = __dadd_rn(wsum, wv[k]);
     }
     const WeightDivisor sum = weight_divisor(wsum);
+    if ((d & 3) == 0 && ((reinterpret_cast<uintptr_t>(a.vectors) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+        // four elements per lane and step: one 16-byte load per neighbour
+        // row, a quarter of the dependent row round trips; each element's
+        // arithmetic (and so its result) is the scalar loop's
+        for (int i4 = lane; i4 < (d >> 2); i4 += 32) {
+            float4 r4[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                r4[k] = k < count ? __ldg(reinterpret_cast<const float4 *>(vr[k]) + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 q4 = reinterpret_cast<const float4 *>(q)[i4];
+            float v[8];
+            float4 o;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = r4[k].x;
+            o.x = reference_blend_element<false>(q4.x, v, wv, sum, count, ratio);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = r4[k].y;
+            o.y = reference_blend_element<false>(q4.y, v, wv, sum, count, ratio);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = r4[k].z;
+            o.z = reference_blend_element<false>(q4.z, v, wv, sum, count, ratio);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = r4[k].w;
+            o.w = reference_blend_element<false>(q4.w, v, wv, sum, count, ratio);
+            reinterpret_cast<float4 *>(dst)[i4] = o;
+        }
+        return;
+    }
     for (int i = lane; i < d; i += 32) {
         float v[8];
 #pragma unroll
