@@ -64,16 +64,16 @@ def _assert_parity(oracle, ix, q, ratio, gd, gl, out, nprobe=None):
 
 
 def test_flat_sixteen_candidate_kernel(cuda, oracle):
-    """2,048 frames x 20,000 rows: the 16-candidate flat kernel (the c5
-    instantiation) against the oracle."""
+    """2,048 frames x 30,000 rows (9 segments of 14 tiles): the
+    16-candidate flat kernel (the c5 instantiation) against the oracle."""
     from vfr import synth
 
-    ix, q = synth.make_np("c1", n=20_000, q=2048)
+    ix, q = synth.make_np("c1", n=30_000, q=2048)
     g = _index(ix)
     gd, gl, out = _search_and_blend(cuda, g, q, 0.75)
     plan = g.diagnostics()["last_plan"]
     assert plan["keep"] == 16 and plan["layout"] == "full", plan
-    assert plan["tiles_per_segment"] > 8
+    assert plan["tiles_per_segment"] > 12
     _assert_parity(oracle, ix, q, 0.75, gd, gl, out)
     diag = g.diagnostics()
     # both calls (search and blend) certified nearly every frame on the tensor path
@@ -95,9 +95,9 @@ def _descending_rows(n, q_frames, seed):
     return synth.flat_arrays(x), q.astype(np.float32)
 
 
-@pytest.mark.parametrize("frames,keep", [(2048, 16), (250, 8)])
-def test_flat_bitonic_merge_on_descending_rows(cuda, oracle, frames, keep):
-    ix, q = _descending_rows(20_000, frames, 7100 + frames)
+@pytest.mark.parametrize("frames,keep,rows", [(2048, 16, 30_000), (250, 8, 20_000)])
+def test_flat_bitonic_merge_on_descending_rows(cuda, oracle, frames, keep, rows):
+    ix, q = _descending_rows(rows, frames, 7100 + frames)
     g = _index(ix)
     gd, gl, out = _search_and_blend(cuda, g, q, 0.75)
     assert g.diagnostics()["last_plan"]["keep"] == keep

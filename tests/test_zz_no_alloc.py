@@ -73,9 +73,9 @@ def _two_calls_match(torch, L, g, q, rate, stream, splits):
 
 
 @pytest.mark.parametrize("rows,frames,keep,layout", [
-    (200_000, 256, 16, "full"),   # 16 candidates per list, 72 segments x 2 frame tiles
-    (340_000, 128, 16, "full"),   # exactly the 148-work-item cap: the key region is full
-    (340_000, 16, 16, "spread"),  # a small block (spread A layout) with long work items
+    (260_000, 256, 16, "full"),   # 16 candidates per list, 73 segments x 2 frame tiles
+    (492_000, 128, 16, "full"),   # exactly the 148-work-item cap: the key region is full
+    (492_000, 16, 16, "spread"),  # a small block (spread A layout) with long work items
     (100_000, 32, 8, "spread"),   # a realtime block against c4's database size
 ])
 def test_noalloc_blend_plans_at_the_scratch_limits(cuda, rows, frames, keep, layout):
@@ -91,7 +91,7 @@ def test_noalloc_blend_plans_at_the_scratch_limits(cuda, rows, frames, keep, lay
     stream = torch.cuda.Stream()
     plan = _two_calls_match(torch, L, g, q, rate, stream, [(0, frames), (frames, 2 * frames)])
     assert plan["keep"] == keep and plan["layout"] == layout, plan
-    if rows == 340_000 and frames == 128:
+    if rows == 492_000 and frames == 128:
         assert plan["segments"] == 148, plan
     g.close()
 

@@ -48,7 +48,7 @@ constexpr int kTileK = 64;   // fp16 elements per 128-byte swizzled row
 constexpr int kShortKeep = 8;
 constexpr int kIvfKeep = 16;
 constexpr int kItemKeep = kIvfKeep;  // largest list size (workspace sizing)
-constexpr int kShortItemTiles = 8;
+constexpr int kShortItemTiles = 12;  // c2's 11-tile items: 8-entry lists certify every frame
 constexpr int kRerank = 64;     // candidates re-ranked exactly per frame (more on distance ties)
 constexpr int kRerankMax = 128;
 constexpr int kMaxSegments = 256;
